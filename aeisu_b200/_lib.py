@@ -1,0 +1,101 @@
+"""ctypes binding of the C ABI declared in include/aeisu.h.
+
+The shared library is built in-tree (``python -m aeisu_b200.build``).  There is no CPU
+fallback: if the library is missing or cannot load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libaeisu_b200.so"
+
+OK, INVALID_ARG, BAD_ARTIFACT, CUDA, NONFINITE, TIMEOUT, UNSUPPORTED, OOM = range(8)
+PRECISIONS = {"fp32": 0, "fp16": 1, "mixed": 2}
+IO_HOST, IO_DEVICE = 0, 1
+FOLDED_VALUES = 115996
+
+
+class AeisuError(RuntimeError):
+    """A failure reported by the library (status code + message)."""
+
+    def __init__(self, status, message):
+        super().__init__(f"[aeisu status {status}] {message}")
+        self.status = status
+
+
+class ArtifactError(AeisuError, ValueError):
+    pass
+
+
+class Timings(C.Structure):
+    _fields_ = [("analysis_project_ms", C.c_float), ("compress_core_ms", C.c_float),
+                ("expand_ms", C.c_float), ("refine_tail_ms", C.c_float),
+                ("reconstruction_ms", C.c_float), ("total_ms", C.c_float), ("detailed", C.c_int)]
+
+
+_SIGNATURES = {
+    "aeisu_open_spyr8": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "aeisu_validate_spyr8": (C.c_int, [C.c_void_p, C.c_size_t, C.c_char_p]),
+    "aeisu_open_spyr8_memory": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "aeisu_open_folded": (C.c_int, [C.c_void_p, C.c_size_t, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "aeisu_close": (None, [C.c_void_p]),
+    "aeisu_upscale_u8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                   C.c_uint, C.c_void_p]),
+    "aeisu_upscale_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                    C.c_uint, C.c_void_p]),
+    "aeisu_forward_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_uint,
+                                    C.c_void_p]),
+    "aeisu_predict_coefficients": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                             C.c_uint, C.c_void_p]),
+    "aeisu_synchronize": (C.c_int, [C.c_void_p, C.c_void_p, C.c_double]),
+    "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
+    "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),
+    "aeisu_set_timeout": (C.c_int, [C.c_void_p, C.c_double]),
+    "aeisu_report": (C.c_char_p, [C.c_void_p]),
+    "aeisu_device_bytes": (C.c_uint64, [C.c_void_p]),
+    "aeisu_kernel_launches": (C.c_uint64, [C.c_void_p]),
+    "aeisu_last_error": (C.c_char_p, []),
+    "aeisu_version": (C.c_char_p, []),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the library once; raise loudly if it is missing."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"aeisu_b200 CUDA library not found at {LIB_PATH}; build it with "
+                "`python -m aeisu_b200.build` (there is no CPU fallback)")
+        handle = C.CDLL(os.fspath(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().aeisu_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status == OK:
+        return
+    msg = last_error()
+    if status == INVALID_ARG:
+        raise ValueError(msg)
+    if status == NONFINITE:
+        raise FloatingPointError(msg)
+    if status == TIMEOUT:
+        raise TimeoutError(msg)
+    if status == BAD_ARTIFACT:
+        raise ArtifactError(status, msg)
+    if status == OOM:
+        raise MemoryError(msg)
+    raise AeisuError(status, msg)

@@ -1,0 +1,373 @@
+// Engine: owns one model on one GPU and runs inference calls.  Padding and tiling follow
+// aeisu/runtime.py:70-103; the launch sequence per region batch follows the reference's
+// mixed frame body (optimized/native/src/neural/srcpyr/SrcPyrCudaRuntime.cu:4131-4873):
+// analysis+project -> compress+core -> expand+shuffle+skip -> refine+tail -> head.
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <sstream>
+#include <thread>
+
+#include "common.h"
+
+namespace aeisu {
+
+DevBuf::~DevBuf() { reset(); }
+
+void DevBuf::reset() {
+    if (p_) cudaFree(p_);
+    p_ = nullptr;
+    cap_ = 0;
+}
+
+void* DevBuf::ensure(size_t bytes, cudaStream_t s) {
+    if (bytes <= cap_) return p_;
+    if (p_) {
+        AEISU_CUDA(cudaStreamSynchronize(s));
+        AEISU_CUDA(cudaFree(p_));
+        p_ = nullptr;
+        cap_ = 0;
+    }
+    bytes = (bytes + 255) / 256 * 256;
+    AEISU_CUDA(cudaMalloc(&p_, bytes));
+    cap_ = bytes;
+    return p_;
+}
+
+void HostBuf::reset() {
+    if (p_) cudaFreeHost(p_);
+    p_ = nullptr;
+    cap_ = 0;
+}
+
+void* HostBuf::ensure(size_t bytes, cudaStream_t s) {
+    if (bytes <= cap_) return p_;
+    if (p_) {
+        AEISU_CUDA(cudaStreamSynchronize(s));
+        reset();
+    }
+    AEISU_CUDA(cudaHostAlloc(&p_, bytes, cudaHostAllocDefault));
+    cap_ = bytes;
+    return p_;
+}
+
+namespace {
+// True when `p` is page-locked (or otherwise directly DMA-able) host memory.
+bool is_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+}  // namespace
+
+// ---- geometry -----------------------------------------------------------------------
+
+Geometry plan_upscale(int n, int h, int w, int tile) {
+    require(n >= 1 && h >= 1 && w >= 1, "frame count and size must be positive");
+    require(tile >= 0 && tile % 32 == 0, "tile must be zero or a positive multiple of 32");
+    require(int64_t(h) * w <= (int64_t(1) << 28) && h <= 32768 && w <= 32768, "frame too large");
+    Geometry g{};
+    g.n = n; g.h = h; g.w = w;
+    const int ey = (32 - h % 32) % 32, ex = (32 - w % 32) % 32;   // -h % 32 in Python
+    g.pad_y = 16 + ey / 2;
+    g.pad_x = 16 + ex / 2;
+    g.ph = h + 32 + ey;
+    g.pw = w + 32 + ex;
+    g.out_h = h; g.out_w = w;
+    std::map<std::pair<int, int>, size_t> index;
+    auto add = [&](const Region& r, int rh, int rw) {
+        auto key = std::make_pair(rh, rw);
+        auto it = index.find(key);
+        if (it == index.end()) {
+            index[key] = g.groups.size();
+            g.groups.push_back({rh, rw, {}});
+            it = index.find(key);
+        }
+        g.groups[it->second].regions.push_back(r);
+    };
+    for (int f = 0; f < n; ++f) {
+        if (tile == 0) {
+            add({f, 0, 0, g.pad_y, g.pad_x, g.pad_y + h, g.pad_x + w}, g.ph, g.pw);
+            continue;
+        }
+        for (int y = 0; y < g.ph; y += tile)
+            for (int x = 0; x < g.pw; x += tile) {
+                const int y1 = std::min(y + tile, g.ph), x1 = std::min(x + tile, g.pw);
+                const int sy = std::max(0, y - 32), sx = std::max(0, x - 32);
+                const int ey2 = std::min(g.ph, y1 + 32), ex2 = std::min(g.pw, x1 + 32);
+                // LR rows/cols of this core that survive the final crop (runtime.py:100)
+                const int cy0 = std::max(y, g.pad_y), cy1 = std::min(y1, g.pad_y + h);
+                const int cx0 = std::max(x, g.pad_x), cx1 = std::min(x1, g.pad_x + w);
+                if (cy0 >= cy1 || cx0 >= cx1) continue;
+                add({f, sy, sx, cy0 - sy, cx0 - sx, cy1 - sy, cx1 - sx}, ey2 - sy, ex2 - sx);
+            }
+    }
+    return g;
+}
+
+Geometry plan_whole(int n, int h, int w) {
+    require(n >= 1 && h >= 4 && w >= 4, "frame count and size must be positive");
+    require(h % 4 == 0 && w % 4 == 0, "Source H/W must be divisible by 4");
+    require(int64_t(h) * w <= (int64_t(1) << 28), "frame too large");
+    Geometry g{};
+    g.n = n; g.h = h; g.w = w;
+    g.pad_y = g.pad_x = 0;
+    g.ph = h; g.pw = w;
+    g.out_h = h; g.out_w = w;
+    g.groups.push_back({h, w, {}});
+    for (int f = 0; f < n; ++f) g.groups[0].regions.push_back({f, 0, 0, 0, 0, h, w});
+    return g;
+}
+
+// ---- engine -------------------------------------------------------------------------
+
+struct Engine::DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        AEISU_CUDA(cudaGetDevice(&prev));
+        if (prev != dev) AEISU_CUDA(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+Engine::Engine(HostModel model, int precision, int device)
+    : model_(std::move(model)), precision_(precision), device_(device) {
+    require(precision >= AEISU_PRECISION_FP32 && precision <= AEISU_PRECISION_MIXED, "unknown precision");
+    int count = 0;
+    AEISU_CUDA(cudaGetDeviceCount(&count));
+    require(device >= 0 && device < count, "device index out of range");
+    if (precision != AEISU_PRECISION_FP32)
+        fail(AEISU_ERR_UNSUPPORTED, "this build provides the FP32 route only");
+    DeviceGuard guard(device_);
+    int lo = 0, hi = 0;
+    AEISU_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    AEISU_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
+    for (auto& e : ev_) AEISU_CUDA(cudaEventCreate(&e));
+    upload_weights();
+    cudaDeviceProp prop{};
+    AEISU_CUDA(cudaGetDeviceProperties(&prop, device_));
+    std::ostringstream os;
+    os << "aeisu-b200: device " << device_ << " " << prop.name << " (sm_" << prop.major << prop.minor << ", "
+       << prop.multiProcessorCount << " SMs); model " << model_.format << " " << model_.architecture;
+    if (!model_.checksum_hex.empty()) os << " sha256 " << model_.checksum_hex;
+    os << "; precision " << (precision_ == 0 ? "fp32" : precision_ == 1 ? "fp16" : "mixed");
+    os << "; route simt-fp32 controller + fp32 head";
+    report_ = os.str();
+}
+
+Engine::~Engine() {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_, &meta_};
+    for (DevBuf* b : all) b->reset();
+    staging_.reset();
+    for (auto& e : ev_)
+        if (e) cudaEventDestroy(e);
+    if (stream_) cudaStreamDestroy(stream_);
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+uint64_t Engine::device_bytes() const {
+    const DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_,
+                           &low_b_, &dec540_, &refined_, &meta_};
+    uint64_t total = 0;
+    for (auto* b : all) total += b->capacity();
+    return total;
+}
+
+void Engine::upload_weights() {
+    // FP32 tensors packed in one allocation: stencil, base, basis, then per layer w | b.
+    std::vector<float> host;
+    auto push = [&](const float* p, size_t n) {
+        size_t at = host.size();
+        host.insert(host.end(), p, p + n);
+        while (host.size() % 64) host.push_back(0.f);
+        return at;
+    };
+    const size_t o_st = push(model_.stencil, 24);
+    const size_t o_base = push(model_.base, 100);
+    const size_t o_basis = push(model_.basis, 1600);
+    size_t o_w[kLayerCount], o_b[kLayerCount];
+    for (int l = 0; l < kLayerCount; ++l) {
+        const LayerWeights& L = model_.layers[l];
+        o_w[l] = push(L.w.data(), L.w.size());
+        o_b[l] = push(L.bias.data(), L.bias.size());
+        for (float s : L.slope)
+            if (s != L.slope[0]) fail(AEISU_ERR_UNSUPPORTED, "per-channel activation slopes are not supported");
+    }
+    w_f32_.ensure(host.size() * 4, stream_);
+    AEISU_CUDA(cudaMemcpy(w_f32_.get(), host.data(), host.size() * 4, cudaMemcpyHostToDevice));
+    const float* d = w_f32_.as<float>();
+    stencil_ = d + o_st;
+    base_ = d + o_base;
+    basis_ = d + o_basis;
+    for (int l = 0; l < kLayerCount; ++l)
+        f32_layers_[l] = {d + o_w[l], d + o_b[l], model_.layers[l].slope[0]};
+    flag_.ensure(256, stream_);
+}
+
+void Engine::record(int stage, cudaStream_t s) {
+    if (!detailed_) return;
+    // ping-pong between ev_[1] and ev_[2]: each mark closes the stage opened by the last one
+    const int cur = (mark_last_ == 1) ? 2 : 1;
+    AEISU_CUDA(cudaEventRecord(ev_[cur], s));
+    AEISU_CUDA(cudaEventSynchronize(ev_[cur]));
+    float ms = 0.f;
+    AEISU_CUDA(cudaEventElapsedTime(&ms, ev_[mark_last_], ev_[cur]));
+    stage_ms_[stage - 1] += ms;
+    mark_last_ = cur;
+}
+
+void Engine::wait(cudaStream_t s, double timeout_ms) {
+    AEISU_CUDA(cudaEventRecord(ev_[7], s));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(ev_[7]);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) AEISU_CUDA(e);
+        const double el = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (el > timeout_ms)
+            fail(AEISU_ERR_TIMEOUT, "GPU work did not complete within " + std::to_string(timeout_ms) + " ms");
+        std::this_thread::sleep_for(std::chrono::microseconds(el < 5.0 ? 10 : 200));
+    }
+}
+
+void Engine::synchronize(cudaStream_t s, double timeout_ms) {
+    DeviceGuard guard(device_);
+    if (!s) s = stream_;
+    wait(s, timeout_ms);
+    int flag = 0;
+    AEISU_CUDA(cudaMemcpy(&flag, flag_.get(), sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        AEISU_CUDA(cudaMemset(flag_.get(), 0, sizeof(int)));
+        fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
+    }
+}
+
+void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
+                       const DstDesc& dst, cudaStream_t s) {
+    const int rh = grp.rh, rw = grp.rw;
+    const size_t packed = size_t(rh / 2) * (rw / 2), low = size_t(rh / 4) * (rw / 4);
+    const size_t per_region = 4 * (packed * (32 + 32 + 64 + 64) + low * 64 * 2);
+    const size_t chunk = std::max<size_t>(1, std::min<size_t>(grp.regions.size(), workspace_cap_ / per_region));
+    for (size_t first = 0; first < grp.regions.size(); first += chunk) {
+        const int R = int(std::min(chunk, grp.regions.size() - first));
+        std::vector<int4> table(2 * size_t(R));
+        int core_h = 0, core_w = 0;
+        for (int i = 0; i < R; ++i) {
+            const Region& r = grp.regions[first + i];
+            table[i] = make_int4(r.frame, r.oy, r.ox, 0);
+            table[R + i] = make_int4(r.cy0, r.cx0, r.cy1, r.cx1);
+            core_h = std::max(core_h, r.cy1 - r.cy0);
+            core_w = std::max(core_w, r.cx1 - r.cx0);
+        }
+        tables_.ensure(table.size() * sizeof(int4), s);
+        AEISU_CUDA(cudaMemcpyAsync(tables_.get(), table.data(), table.size() * sizeof(int4),
+                                   cudaMemcpyHostToDevice, s));
+        RegionSet rs{};
+        rs.regions = tables_.as<int4>();
+        rs.cores = tables_.as<int4>() + R;
+        rs.R = R; rs.rh = rh; rs.rw = rw; rs.core_h = core_h; rs.core_w = core_w;
+        enc540_.ensure(4 * packed * 32 * R, s);
+        dec540_.ensure(4 * packed * 32 * R, s);
+        refined_.ensure(4 * packed * 64 * R, s);
+        meta_.ensure(4 * packed * 64 * R, s);
+        low_a_.ensure(4 * low * 64 * R, s);
+        low_b_.ensure(4 * low * 64 * R, s);
+        int launches = 0;
+        struct Ctx { Engine* e; cudaStream_t s; } ctx{this, s};
+        StageMark mark;
+        mark.ctx = &ctx;
+        mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
+        launch_f32_controller(src, rs, stencil_, f32_layers_, enc540_.as<float>(), low_a_.as<float>(),
+                              low_b_.as<float>(), dec540_.as<float>(), refined_.as<float>(), meta_.as<float>(), s,
+                              &launches, mark);
+        if (c.mode == Mode::Predict) {
+            // one region per frame, covering it: metadata NHWC [h/2, w/2, 64] per frame
+            const size_t bytes = 4 * packed * 64;
+            for (int i = 0; i < R; ++i) {
+                const int f = grp.regions[first + i].frame;
+                char* out = static_cast<char*>(c.host ? dst_.get() : c.dst) + size_t(f) * bytes;
+                AEISU_CUDA(cudaMemcpyAsync(out, meta_.as<char>() + size_t(i) * bytes, bytes,
+                                           cudaMemcpyDeviceToDevice, s));
+            }
+        } else {
+            launch_f32_head(src, rs, dst, meta_.as<float>(), base_, basis_, flag_.as<int>(), s, &launches);
+        }
+        record(5, s);
+        launches_ += uint64_t(launches);
+    }
+    (void)g;
+}
+
+void Engine::run(const Call& c) {
+    DeviceGuard guard(device_);
+    require(c.src != nullptr && c.dst != nullptr, "source and destination must not be null");
+    const Geometry g = (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile) : plan_whole(c.n, c.h, c.w);
+    cudaStream_t s = c.stream ? c.stream : stream_;
+    const size_t src_elem = c.src_kind == 0 ? 1 : 4;
+    const size_t src_bytes = size_t(c.n) * 3 * c.h * c.w * src_elem;
+    size_t dst_bytes;
+    if (c.mode == Mode::Predict) dst_bytes = size_t(c.n) * (c.h / 2) * (c.w / 2) * 64 * 4;
+    else dst_bytes = size_t(c.n) * 3 * (2 * size_t(g.out_h)) * (2 * size_t(g.out_w)) * (c.dst_kind == 0 ? 1 : 4);
+
+    stage_ms_.assign(5, 0.f);
+    AEISU_CUDA(cudaEventRecord(ev_[0], s));
+    const void* src_ptr = c.src;
+    void* dst_ptr = c.dst;
+    if (c.host) {
+        src_.ensure(src_bytes, s);
+        dst_.ensure(dst_bytes, s);
+        AEISU_CUDA(cudaMemcpyAsync(src_.get(), c.src, src_bytes, cudaMemcpyHostToDevice, s));
+        src_ptr = src_.get();
+        dst_ptr = dst_.get();
+    }
+    AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, sizeof(int), s));
+    if (detailed_) {
+        AEISU_CUDA(cudaEventRecord(ev_[1], s));
+        AEISU_CUDA(cudaEventSynchronize(ev_[1]));
+        mark_last_ = 1;
+    }
+    SrcDesc src{src_ptr, c.src_kind, c.h, c.w, g.pad_y, g.pad_x};
+    DstDesc dst{dst_ptr, c.dst_kind, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
+    for (const auto& grp : g.groups) run_group(c, g, grp, src, dst, s);
+    // Pageable destinations go through page-locked staging: a direct copy into pageable
+    // memory would block the host without the completion bound.
+    const bool staged = c.host && !is_pinned(c.dst);
+    if (c.host) {
+        void* out = staged ? staging_.ensure(dst_bytes, s) : c.dst;
+        AEISU_CUDA(cudaMemcpyAsync(out, dst_.get(), dst_bytes, cudaMemcpyDeviceToHost, s));
+    }
+    AEISU_CUDA(cudaEventRecord(ev_[6], s));
+    if (c.host) {
+        wait(s, timeout_ms_);
+        if (staged) std::memcpy(c.dst, staging_.get(), dst_bytes);
+        float total = 0.f;
+        AEISU_CUDA(cudaEventElapsedTime(&total, ev_[0], ev_[6]));
+        timings_ = {};
+        timings_.analysis_project_ms = stage_ms_[0];
+        timings_.compress_core_ms = stage_ms_[1];
+        timings_.expand_ms = stage_ms_[2];
+        timings_.refine_tail_ms = stage_ms_[3];
+        timings_.reconstruction_ms = stage_ms_[4];
+        timings_.total_ms = total;
+        timings_.detailed = detailed_ ? 1 : 0;
+        int flag = 0;
+        AEISU_CUDA(cudaMemcpy(&flag, flag_.get(), sizeof(int), cudaMemcpyDeviceToHost));
+        if (flag && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
+    }
+}
+
+}  // namespace aeisu

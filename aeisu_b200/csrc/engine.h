@@ -1,0 +1,138 @@
+// Per-device execution engine: weights resident on one GPU, workspace, stream, and the
+// orchestration of one inference call (padding geometry, tiling into regions, kernel
+// launches, host<->device copies, bounded completion wait).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "kernels.h"
+#include "model.h"
+
+namespace aeisu {
+
+class DevBuf {
+public:
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf();
+    // Grow to at least `bytes`; waits for `s` before releasing an old allocation.
+    void* ensure(size_t bytes, cudaStream_t s);
+    void reset();
+    void* get() const { return p_; }
+    size_t capacity() const { return cap_; }
+    template <typename T> T* as() const { return static_cast<T*>(p_); }
+
+private:
+    void* p_ = nullptr;
+    size_t cap_ = 0;
+};
+
+// Page-locked host staging buffer (device->host results land here when the caller's
+// buffer is pageable, so the completion wait stays bounded).
+class HostBuf {
+public:
+    HostBuf() = default;
+    HostBuf(const HostBuf&) = delete;
+    HostBuf& operator=(const HostBuf&) = delete;
+    ~HostBuf() { reset(); }
+    void* ensure(size_t bytes, cudaStream_t s);
+    void reset();
+    void* get() const { return p_; }
+
+private:
+    void* p_ = nullptr;
+    size_t cap_ = 0;
+};
+
+// One region of the padded grid (a whole frame for tile=0, a crop for tile>0).
+struct Region { int frame, oy, ox, cy0, cx0, cy1, cx1; };
+
+struct Geometry {
+    int n, h, w;            // input frames and size
+    int pad_y, pad_x;       // replicate padding before the top/left edge
+    int ph, pw;             // padded grid size
+    int out_h, out_w;       // LR extent written to the output (h, w)
+    // regions grouped by shape: every group launches as one batch
+    struct Group { int rh, rw; std::vector<Region> regions; };
+    std::vector<Group> groups;
+};
+
+// Padding and tiling of aeisu/runtime.py:70-99.  tile == 0: one region per frame.
+Geometry plan_upscale(int n, int h, int w, int tile);
+// One region per frame covering an already padded image (FoldedAEISU.forward semantics).
+Geometry plan_whole(int n, int h, int w);
+
+enum class Mode { Upscale, Forward, Predict };
+
+struct Call {
+    Mode mode;
+    const void* src; int src_kind;  // 0 u8 HWC, 1 f32 CHW
+    void* dst; int dst_kind;        // 0 u8 HWC, 1 f32 CHW (Predict: f32 NHWC metadata)
+    int n, h, w, tile;
+    bool host;
+    cudaStream_t stream;
+};
+
+class Engine {
+public:
+    Engine(HostModel model, int precision, int device);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    void run(const Call& call);
+    void synchronize(cudaStream_t s, double timeout_ms);
+
+    const std::string& report() const { return report_; }
+    uint64_t device_bytes() const;
+    uint64_t launches() const { return launches_; }
+    const aeisu_timings& timings() const { return timings_; }
+    void set_detailed(bool on) { detailed_ = on; }
+    void set_timeout(double ms) { timeout_ms_ = ms; }
+    int precision() const { return precision_; }
+    int device() const { return device_; }
+
+private:
+    struct DeviceGuard;
+    void upload_weights();
+    void run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
+                   const DstDesc& dst, cudaStream_t s);
+    void wait(cudaStream_t s, double timeout_ms);
+    void record(int stage, cudaStream_t s);
+
+    HostModel model_;
+    int precision_, device_;
+    cudaStream_t stream_ = nullptr;
+    std::string report_;
+    double timeout_ms_ = 60000.0;
+    bool detailed_ = false;
+    uint64_t launches_ = 0;
+    aeisu_timings timings_{};
+
+    // resident weights
+    DevBuf w_f32_;               // all FP32 tensors, packed
+    const float* stencil_ = nullptr;
+    const float* base_ = nullptr;
+    const float* basis_ = nullptr;
+    F32Layer f32_layers_[kLayerCount]{};
+
+    // workspace
+    DevBuf src_, dst_, tables_, flag_;
+    HostBuf staging_;
+    DevBuf enc540_, low_a_, low_b_, dec540_, refined_, meta_;
+    size_t workspace_cap_ = size_t(6) << 30;
+
+    // timing events: [0] call start, [1]/[2] detailed stage marks, [6] call end, [7] waits
+    cudaEvent_t ev_[8] = {};
+    int mark_last_ = 1;
+    std::vector<float> stage_ms_;
+};
+
+}  // namespace aeisu

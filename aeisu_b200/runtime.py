@@ -1,0 +1,321 @@
+"""Python operator API over the C ABI, mirroring the reference's aeisu.runtime.
+
+Reference surface mirrored (paths relative to the AELabs42/AEISU checkout):
+
+* ``load_model(path, device)``  -> aeisu/runtime.py:45-56 (folded ``.pt``); also SPYR8 ``.bin``
+* ``upscale(model, source, tile=128)`` -> aeisu/runtime.py:70-103 (same padding, tiling,
+  ValueError / FloatingPointError behaviour, clamped CHW float32 result)
+* ``model(src)`` / ``model.predict_coefficients(src)`` -> FoldedAEISU.forward /
+  predict_coefficients (aeisu/model.py:494-551)
+* ``read_rgb`` / ``save_rgb`` -> aeisu/runtime.py:17-27
+
+plus the deployment entry point ``upscale_u8`` (uint8 HWC frames in and out, batched).
+Arrays may be numpy arrays, CPU tensors (host I/O through the library's copies) or CUDA
+tensors on the model's device (device I/O on the current torch stream).  All compute runs
+in ``libaeisu_b200.so``; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib
+
+# FoldedAEISU.state_dict() order and shapes (aeisu/model.py:554-583).
+_CONVS = (
+    ("project_540", 32, 32, 1),
+    ("compress_270", 128, 64, 1),
+    *((f"bottleneck_270_{b}{i}", 32, 32, 3) for b in ("a", "b") for i in range(1, 5)),
+    ("expand_270", 64, 128, 1),
+    ("refine_540", 32, 64, 3),
+    ("metadata_head", 64, 64, 1),
+)
+FOLDED_KEYS = (
+    ("analysis_rgb_basis", (3, 3)), ("analysis_rgb_mix", (3,)), ("analysis_dx_rows", (3,)),
+    ("analysis_dy_cols", (3,)), ("analysis_diag45", (3,)), ("analysis_diag135", (3,)),
+    ("base_kernel", (25, 4)), ("basis_raw", (16, 4, 25)),
+    *(item for name, cin, cout, k in _CONVS
+      for item in ((f"{name}.weight", (cout, cin, k, k)), (f"{name}.bias", (cout,)))),
+)
+SPYR8_MAGIC = b"SPYR8F8\0"
+
+
+def _device_index(device) -> int:
+    if isinstance(device, int):
+        return device
+    text = str(device)
+    if text in ("cuda", "auto"):
+        return 0
+    if text.startswith("cuda:"):
+        return int(text.split(":", 1)[1])
+    raise ValueError(f"aeisu_b200 runs on CUDA devices only, got device={device!r}")
+
+
+def flatten_folded(state) -> np.ndarray:
+    """Concatenate a folded state dict (tensors or arrays) in FoldedAEISU.state_dict() order."""
+    parts = []
+    for key, shape in FOLDED_KEYS:
+        if key not in state:
+            raise ValueError(f"Checkpoint is missing {key}")
+        value = state[key]
+        value = value.detach().cpu().numpy() if hasattr(value, "detach") else np.asarray(value)
+        if tuple(value.shape) != shape:
+            raise ValueError(f"{key}: expected shape {shape}, got {tuple(value.shape)}")
+        parts.append(np.ascontiguousarray(value, np.float32).reshape(-1))
+    extra = set(state) - {k for k, _ in FOLDED_KEYS}
+    if extra:
+        raise ValueError(f"Unexpected checkpoint keys: {sorted(extra)[:4]}")
+    flat = np.concatenate(parts)
+    assert flat.size == _lib.FOLDED_VALUES
+    return flat
+
+
+def _checkpoint_state(payload):
+    """runtime.checkpoint_state (aeisu/runtime.py:35-42)."""
+    if isinstance(payload, dict):
+        for key in ("model", "model_state_dict", "state_dict"):
+            if isinstance(payload.get(key), dict):
+                return payload[key]
+        if payload and all(hasattr(v, "shape") for v in payload.values()):
+            return payload
+    raise ValueError("Checkpoint does not contain a tensor state dictionary")
+
+
+class _Array:
+    """A view of a caller array as (pointer, is_device, keepalive, torch-ness)."""
+
+    def __init__(self, value, dtype, device_index):
+        self.torch = None
+        self.value = value
+        try:
+            import torch
+        except ImportError:  # numpy-only callers
+            torch = None
+        if torch is not None and isinstance(value, torch.Tensor):
+            self.torch = torch
+            want = {np.float32: torch.float32, np.uint8: torch.uint8}[dtype]
+            if value.is_cuda:
+                if value.device.index != device_index:
+                    raise ValueError(f"tensor is on {value.device}, model on cuda:{device_index}")
+                self.keep = value.to(want).contiguous()
+                self.ptr = self.keep.data_ptr()
+                self.device = True
+                self.stream = torch.cuda.current_stream(value.device).cuda_stream
+                return
+            self.keep = value.detach().to(want).contiguous().numpy()
+        else:
+            self.keep = np.ascontiguousarray(value, dtype)
+        self.ptr = self.keep.ctypes.data
+        self.device = False
+        self.stream = None
+
+
+class Model:
+    """A model resident on one GPU (one C-ABI handle)."""
+
+    def __init__(self, handle, device_index, precision, basis_l1_scale=0.5):
+        self._h = handle
+        self.device_index = device_index
+        self.precision = precision
+        self.basis_l1_scale = basis_l1_scale
+
+    # -- construction ----------------------------------------------------------------
+    @classmethod
+    def from_folded_state(cls, state, device="cuda", precision="fp32", basis_l1_scale=0.5):
+        flat = flatten_folded(state)
+        dev = _device_index(device)
+        h = C.c_void_p()
+        _lib.check(_lib.lib().aeisu_open_folded(flat.ctypes.data, flat.size, float(basis_l1_scale),
+                                                _lib.PRECISIONS[precision], dev, C.byref(h)))
+        return cls(h, dev, precision, basis_l1_scale)
+
+    @classmethod
+    def from_spyr8_bytes(cls, data: bytes, device="cuda", precision="mixed"):
+        dev = _device_index(device)
+        buf = C.create_string_buffer(data, len(data))
+        h = C.c_void_p()
+        _lib.check(_lib.lib().aeisu_open_spyr8_memory(buf, len(data), _lib.PRECISIONS[precision], dev,
+                                                      C.byref(h)))
+        return cls(h, dev, precision)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib().aeisu_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _handle(self):
+        if not self._h:
+            raise ValueError("model is closed")
+        return self._h
+
+    # -- introspection ---------------------------------------------------------------
+    @property
+    def report(self) -> str:
+        return _lib.lib().aeisu_report(self._handle()).decode()
+
+    @property
+    def device_bytes(self) -> int:
+        return int(_lib.lib().aeisu_device_bytes(self._handle()))
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(_lib.lib().aeisu_kernel_launches(self._handle()))
+
+    def timings(self) -> dict:
+        t = _lib.Timings()
+        _lib.check(_lib.lib().aeisu_timings_get(self._handle(), C.byref(t)))
+        return {name: getattr(t, name) for name, _ in t._fields_}
+
+    def set_detailed_timing(self, on: bool):
+        _lib.check(_lib.lib().aeisu_set_detailed_timing(self._handle(), int(bool(on))))
+
+    def set_timeout(self, ms: float):
+        _lib.check(_lib.lib().aeisu_set_timeout(self._handle(), float(ms)))
+
+    def synchronize(self, stream=None, timeout_ms=60000.0):
+        _lib.check(_lib.lib().aeisu_synchronize(self._handle(), stream, float(timeout_ms)))
+
+    # -- reference operator surface ----------------------------------------------------
+    def _out(self, arr: _Array, shape, dtype):
+        if arr.device:
+            t = arr.torch
+            return t.empty(shape, dtype={np.float32: t.float32, np.uint8: t.uint8}[dtype],
+                           device=f"cuda:{self.device_index}")
+        return np.empty(shape, dtype)
+
+    @staticmethod
+    def _ptr(out):
+        return out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
+
+    def _wrap(self, arr: _Array, out):
+        if arr.torch is not None and not arr.device:
+            return arr.torch.from_numpy(out)
+        return out
+
+    def predict_coefficients(self, source):
+        """Metadata [B,64,H/2,W/2] (NCHW, as FoldedAEISU.predict_coefficients returns)."""
+        a = _Array(source, np.float32, self.device_index)
+        if a.keep.ndim != 4 or a.keep.shape[1] != 3:
+            raise ValueError(f"Expected source RGB [B,3,H,W], got {tuple(a.keep.shape)}")
+        b, _, h, w = a.keep.shape
+        out = self._out(a, (b, h // 2, w // 2, 64), np.float32)
+        _lib.check(_lib.lib().aeisu_predict_coefficients(
+            self._handle(), a.ptr, b, h, w, self._ptr(out), _lib.IO_DEVICE if a.device else _lib.IO_HOST,
+            a.stream))
+        out = out.permute(0, 3, 1, 2) if a.device else out.transpose(0, 3, 1, 2)
+        return self._wrap(a, out)
+
+    def __call__(self, source):
+        """FoldedAEISU.forward: unclipped 2x RGB [B,3,2H,2W] of a padded batch."""
+        a = _Array(source, np.float32, self.device_index)
+        if a.keep.ndim != 4 or a.keep.shape[1] != 3:
+            raise ValueError(f"Expected source RGB [B,3,H,W], got {tuple(a.keep.shape)}")
+        b, _, h, w = a.keep.shape
+        out = self._out(a, (b, 3, 2 * h, 2 * w), np.float32)
+        _lib.check(_lib.lib().aeisu_forward_f32(
+            self._handle(), a.ptr, b, h, w, self._ptr(out), _lib.IO_DEVICE if a.device else _lib.IO_HOST,
+            a.stream))
+        return self._wrap(a, out)
+
+    forward = __call__
+
+    def upscale_f32(self, source, tile=128):
+        """Unclipped upscale of one CHW or a batch of NCHW float frames."""
+        a = _Array(source, np.float32, self.device_index)
+        x = a.keep
+        single = x.ndim == 3
+        if x.ndim not in (3, 4) or x.shape[-3] != 3:
+            raise ValueError("Expected CHW RGB image")
+        n = 1 if single else x.shape[0]
+        h, w = x.shape[-2:]
+        out = self._out(a, (n, 3, 2 * h, 2 * w), np.float32)
+        _lib.check(_lib.lib().aeisu_upscale_f32(
+            self._handle(), a.ptr, n, h, w, int(tile), self._ptr(out),
+            _lib.IO_DEVICE if a.device else _lib.IO_HOST, a.stream))
+        out = out[0] if single else out
+        return self._wrap(a, out)
+
+    def upscale_u8(self, frames, tile=0, out=None):
+        """uint8 HWC (or NHWC) frames -> uint8 2x frames; clamp + floor(x*255+0.5)."""
+        a = _Array(frames, np.uint8, self.device_index)
+        x = a.keep
+        single = x.ndim == 3
+        if x.ndim not in (3, 4) or x.shape[-1] != 3:
+            raise ValueError("Expected HWC RGB uint8 frames")
+        n = 1 if single else x.shape[0]
+        h, w = x.shape[-3:-1]
+        shape = (2 * h, 2 * w, 3) if single else (n, 2 * h, 2 * w, 3)
+        if out is None:
+            out = self._out(a, shape, np.uint8)
+        elif tuple(out.shape) != shape:
+            raise ValueError(f"out must have shape {shape}")
+        _lib.check(_lib.lib().aeisu_upscale_u8(
+            self._handle(), a.ptr, n, h, w, int(tile), self._ptr(out),
+            _lib.IO_DEVICE if a.device else _lib.IO_HOST, a.stream))
+        return self._wrap(a, out)
+
+
+def load_model(path, device="cuda", precision=None) -> Model:
+    """runtime.load_model (aeisu/runtime.py:45-56) for folded ``.pt`` checkpoints, plus
+    SPYR8 ``.bin`` artifacts.  precision defaults to fp32 for ``.pt`` and mixed for SPYR8."""
+    path = Path(path)
+    with path.open("rb") as f:
+        head = f.read(8)
+    if head == SPYR8_MAGIC:
+        return Model.from_spyr8_bytes(path.read_bytes(), device, precision or "mixed")
+    import torch  # checkpoint container only
+    payload = torch.load(path, map_location="cpu", weights_only=True)
+    state = _checkpoint_state(payload)
+    scale = payload.get("basis_l1_scale", payload.get("config", {}).get("basis_l1_scale", 0.5)) \
+        if isinstance(payload, dict) else 0.5
+    if any(".rep_low_u" in key for key in state):
+        raise ValueError("training checkpoints must be folded first (export.py) before loading")
+    return Model.from_folded_state(state, device, precision or "fp32", scale)
+
+
+def upscale(model: Model, source, tile: int = 128):
+    """runtime.upscale (aeisu/runtime.py:70-103): CHW float [0,1] -> clamped CHW 2x float."""
+    shape = tuple(source.shape)
+    if len(shape) != 3 or shape[0] != 3:
+        raise ValueError("Expected CHW RGB image")
+    if tile < 0 or tile % 32:
+        raise ValueError("tile must be zero or a positive multiple of 32")
+    out = model.upscale_f32(source, tile)
+    if hasattr(out, "isfinite"):
+        if not bool(out.isfinite().all()):
+            raise FloatingPointError("Non-finite model reconstruction")
+        return out.clamp(0, 1)
+    if not np.isfinite(out).all():
+        raise FloatingPointError("Non-finite model reconstruction")
+    return np.clip(out, 0, 1)
+
+
+def upscale_u8(model: Model, frames, tile: int = 0, out=None):
+    return model.upscale_u8(frames, tile, out)
+
+
+def read_rgb(path):
+    """runtime.read_rgb (aeisu/runtime.py:17-20): image file -> float32 CHW in [0,1] (torch)."""
+    import torch
+    from PIL import Image
+    with Image.open(path) as image:
+        array = np.array(image.convert("RGB"), dtype=np.uint8, copy=True)
+    return torch.from_numpy(array).permute(2, 0, 1).float().div(255)
+
+
+def save_rgb(path, image):
+    """runtime.save_rgb (aeisu/runtime.py:23-27): clamp, floor(x*255+0.5), PNG."""
+    from PIL import Image
+    a = image.detach().cpu().clamp(0, 1).permute(1, 2, 0).numpy() if hasattr(image, "detach") \
+        else np.clip(np.asarray(image, np.float32), 0, 1).transpose(1, 2, 0)
+    a = np.floor(a * 255 + 0.5).astype(np.uint8)
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    Image.fromarray(a).save(path)

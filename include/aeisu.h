@@ -1,0 +1,161 @@
+/*
+ * aeisu.h — C ABI of the B200 (sm_100a) AEISU 2x inference runtime.
+ *
+ * One handle = one model resident on one GPU (weights, packed operand layouts,
+ * workspace, CUDA stream).  Calls on one handle are not thread-safe; use one handle
+ * per host thread (handles opened from the same artifact on the same device are
+ * independent, like the reference's sibling slots).  The caller owns every I/O
+ * buffer; the library owns weights and workspace.  Every entry point returns an
+ * aeisu_status (never throws); aeisu_last_error() gives the calling thread's last
+ * message.
+ *
+ * Reference interfaces replaced (paths relative to the AELabs42/AEISU checkout):
+ *   aess::srcpyr::ModelArtifact::Load      optimized/native/src/neural/srcpyr/SrcPyrModel.cpp:243-470
+ *   aess::srcpyr::CudaRuntime (ctor, Configure, Process, StartupReport, PersistentDeviceBytes)
+ *                                          optimized/native/src/neural/srcpyr/SrcPyrCudaRuntime.h:29-96
+ *   aeisu.runtime.load_model               aeisu/runtime.py:45-56
+ *   aeisu.runtime.upscale                  aeisu/runtime.py:70-103
+ *   FoldedAEISU.forward / predict_coefficients   aeisu/model.py:494-551
+ * The Python binding that mirrors aeisu.runtime over this ABI is aeisu_b200/runtime.py.
+ */
+#ifndef AEISU_B200_H
+#define AEISU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct aeisu_engine aeisu_t;
+
+/* Status codes.  The reference raises std::runtime_error (native) or ValueError /
+ * FloatingPointError (aeisu/runtime.py:77-80, 101-102); these are their C forms. */
+typedef enum aeisu_status {
+    AEISU_OK = 0,
+    AEISU_ERR_INVALID_ARG = 1,   /* ValueError: shape, tile, pointer, flag misuse      */
+    AEISU_ERR_BAD_ARTIFACT = 2,  /* artifact parse / checksum / contract failure       */
+    AEISU_ERR_CUDA = 3,          /* a CUDA runtime or driver call failed               */
+    AEISU_ERR_NONFINITE = 4,     /* FloatingPointError: non-finite reconstruction      */
+    AEISU_ERR_TIMEOUT = 5,       /* a bounded wait for GPU completion expired          */
+    AEISU_ERR_UNSUPPORTED = 6,   /* precision/format combination not available         */
+    AEISU_ERR_OOM = 7            /* device or host allocation failed                   */
+} aeisu_status;
+
+/* Arithmetic of the controller convolutions (the head always accumulates in FP32).
+ * FP32  : every layer FP32 (the parity path; aeisu/model.py semantics).
+ * FP16  : FP16 operands, FP32 accumulate (reference "Fp16" route).
+ * MIXED : FP8-E4M3 compress/core/expand, FP16 project/refine/tail, as laid out by
+ *         the SPYR8 artifact (reference "Mixed" route, SrcPyrCudaRuntime.cu:4131-4873). */
+typedef enum aeisu_precision {
+    AEISU_PRECISION_FP32 = 0,
+    AEISU_PRECISION_FP16 = 1,
+    AEISU_PRECISION_MIXED = 2
+} aeisu_precision;
+
+/* Flags for the I/O calls. */
+#define AEISU_IO_HOST   0u   /* src/dst are host pointers (pinned for full PCIe speed); the
+                                call copies, runs and waits (bounded by the handle timeout) */
+#define AEISU_IO_DEVICE 1u   /* src/dst are device pointers on the handle's GPU; the call only
+                                enqueues on `stream` (or the handle's stream when NULL)      */
+
+/* Number of float values in a folded checkpoint (aeisu/model.py:554-583, 34 tensors,
+ * tests/test_reference.py:69). */
+#define AEISU_FOLDED_VALUES 115996
+
+/* Open a model from a SPYR8 v1 artifact file (adaptive_fp8.bin layout).
+ * Replaces ModelArtifact::Load + CudaRuntime(modelPath): same header, descriptor,
+ * SHA-256 (checksum field zeroed) and zero-DC/L1 basis contract checks. */
+int aeisu_open_spyr8(const char* path, int precision, int device, aeisu_t** out);
+
+/* Parse and validate a SPYR8 artifact image on the host only (no GPU needed): header,
+ * descriptors, SHA-256, tensor contract.  On success writes the 64-hex-digit checksum and
+ * a NUL to checksum_hex (at least 65 bytes) when it is not NULL. */
+int aeisu_validate_spyr8(const void* data, size_t bytes, char* checksum_hex);
+
+/* Same as aeisu_open_spyr8, from an artifact image already in host memory. */
+int aeisu_open_spyr8_memory(const void* data, size_t bytes, int precision, int device,
+                            aeisu_t** out);
+
+/* Open a model from folded FP32 weights: the 34 tensors of FoldedAEISU.state_dict()
+ * concatenated in that order (AEISU_FOLDED_VALUES floats), plus basis_l1_scale.
+ * Replaces load_model(path) for folded .pt checkpoints (aeisu/runtime.py:45-56);
+ * the Python binding reads the .pt and passes its tensors here.  Precision FP32 or
+ * FP16 (MIXED needs the FP8 scales of a SPYR8 artifact). */
+int aeisu_open_folded(const float* values, size_t count, float basis_l1_scale,
+                      int precision, int device, aeisu_t** out);
+
+void aeisu_close(aeisu_t* handle);
+
+/* uint8 RGB in, uint8 RGB out: n frames of h x w x 3 (HWC, row-major, contiguous)
+ * -> n frames of 2h x 2w x 3.  Semantics of upscale(model, read_rgb(x), tile) followed
+ * by save_rgb's clamp and floor(x*255+0.5) (aeisu/runtime.py:17-27, 70-103):
+ * replicate align-32 + 16 halo padding, tile == 0 full frame, tile > 0 (multiple of
+ * 32) cores on the padded grid with 32-LR-pixel halos.  Returns AEISU_ERR_NONFINITE
+ * if any reconstruction value is not finite (host I/O; with device I/O the flag is
+ * reported by aeisu_synchronize). */
+int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, int tile,
+                     uint8_t* dst, unsigned flags, void* stream);
+
+/* Float parity path: n frames of float32 CHW (3 x h x w, values as read_rgb gives) ->
+ * UNCLIPPED float32 CHW 3 x 2h x 2w (clip and the finite check are the caller's, as in
+ * aeisu/runtime.py:100-103). */
+int aeisu_upscale_f32(aeisu_t* handle, const float* src, int n, int h, int w, int tile,
+                      float* dst, unsigned flags, void* stream);
+
+/* FoldedAEISU.forward on an already padded NCHW float32 batch (h, w multiples of 4):
+ * unclipped [n,3,2h,2w] (aeisu/model.py:546-551). */
+int aeisu_forward_f32(aeisu_t* handle, const float* src, int n, int h, int w, float* dst,
+                      unsigned flags, void* stream);
+
+/* FoldedAEISU.predict_coefficients on an NCHW float32 batch (h, w multiples of 4):
+ * metadata as float32 NHWC [n, h/2, w/2, 64], channel = parity*16 + component
+ * (aeisu/model.py:494-496; reconstruction.py:20-26).  Values are the raw head output
+ * (before coefficient_clamp), in the handle's precision. */
+int aeisu_predict_coefficients(aeisu_t* handle, const float* src, int n, int h, int w,
+                               float* meta, unsigned flags, void* stream);
+
+/* Wait for all work enqueued on the handle's stream (or `stream`) for at most
+ * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
+ * reconstruction since the last call produced a non-finite value. */
+int aeisu_synchronize(aeisu_t* handle, void* stream, double timeout_ms);
+
+/* Per-stage device times of the last upscale call, in milliseconds (CUDA events;
+ * replaces FrameTimings, NeuralRuntimeTypes.h:36-52). */
+typedef struct aeisu_timings {
+    float analysis_project_ms;   /* feature analysis + unshuffle + project_540          */
+    float compress_core_ms;      /* compress_270 + 4 grouped bottleneck layers           */
+    float expand_ms;             /* expand_270 + pixel shuffle + skip add                */
+    float refine_tail_ms;        /* refine_540 + metadata_head                           */
+    float reconstruction_ms;     /* fused reconstruction head                            */
+    float total_ms;              /* first to last event, including host<->device copies */
+    int   detailed;              /* 1 when the stage split was recorded                  */
+} aeisu_timings;
+
+int aeisu_timings_get(aeisu_t* handle, aeisu_timings* out);
+int aeisu_set_detailed_timing(aeisu_t* handle, int enabled);
+
+/* Bound, in milliseconds, on every host wait for GPU completion (default 60000). */
+int aeisu_set_timeout(aeisu_t* handle, double timeout_ms);
+
+/* Startup report (device, artifact hash, precision, kernel route), like
+ * CudaRuntime::StartupReport (SrcPyrCudaRuntime.cu:3739-3783).  Valid until close. */
+const char* aeisu_report(aeisu_t* handle);
+
+/* Bytes of device memory the handle holds (weights + workspace). */
+uint64_t aeisu_device_bytes(aeisu_t* handle);
+
+/* Number of kernels the library launched on this handle since it was opened. */
+uint64_t aeisu_kernel_launches(aeisu_t* handle);
+
+/* Message of the last failure on the calling thread ("" if none). */
+const char* aeisu_last_error(void);
+
+/* Library version string. */
+const char* aeisu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AEISU_B200_H */

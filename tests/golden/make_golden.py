@@ -1,0 +1,137 @@
+"""Generate the golden parity fixtures from the reference PyTorch implementation.
+
+Run in a container that has a reference checkout (default ``/root/reference``):
+
+    python tests/golden/make_golden.py [--reference PATH]
+
+It imports the reference's own ``aeisu`` package and records, for seeded synthetic
+frames, the outputs of its public operator API (``aeisu.runtime.upscale``,
+``FoldedAEISU.predict_coefficients``, ``FoldedAEISU.forward``) and of the
+reconstruction helpers whose known-answer tests live in tests/test_reference.py.
+The fixtures are committed; tests never need the reference at run time.
+
+Weights: ``random_folded_state(seed)`` from ``aeisu_b200.synthetic`` (regenerated
+bit-identically by the tests from the same seed), plus the reference's trained
+``weights/aeisu_area.pt`` and ``weights/aeisu_bicubic.pt`` whose SHA-256 is stored
+beside each output so a test can confirm it runs the same checkpoint.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from aeisu_b200.synthetic import make_frame, random_folded_state  # noqa: E402
+
+
+def sha256(path):
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    import torch
+    from torch.nn import functional as F
+    from aeisu.model import FoldedAEISU
+    from aeisu.reconstruction import coefficient_clamp, project_basis, unpack_coefficients
+    from aeisu.runtime import load_model, upscale
+
+    torch.set_num_threads(4)
+
+    def folded_from_state(state):
+        model = FoldedAEISU()
+        model.load_state_dict({k: torch.from_numpy(v) for k, v in state.items()}, strict=True)
+        return model.eval().requires_grad_(False)
+
+    def frame_chw(frame):
+        return torch.from_numpy(frame).permute(2, 0, 1).float().div(255)
+
+    def padded(src):
+        h, w = src.shape[-2:]
+        ey, ex = -h % 32, -w % 32
+        py, px = 16 + ey // 2, 16 + ex // 2
+        return F.pad(src[None], (px, 32 + ex - px, py, 32 + ey - py), mode="replicate")
+
+    # 1. reconstruction known-answer tests (tests/test_reference.py:31-54)
+    clamp_in = np.array([-20., -12., -4., -2., 0., 2., 4., 12., 20.], np.float32)
+    rng = np.random.default_rng(5)
+    meta_small = rng.normal(0, 1.5, (2, 64, 3, 5)).astype(np.float32)
+    raw = rng.normal(0, 0.3, (16, 4, 25)).astype(np.float32)
+    np.savez_compressed(
+        HERE / "reconstruction_kat.npz",
+        clamp_in=clamp_in,
+        clamp_out=coefficient_clamp(torch.from_numpy(clamp_in)).numpy(),
+        meta=meta_small,
+        unpacked=unpack_coefficients(torch.from_numpy(meta_small)).numpy(),
+        basis_raw=raw,
+        basis=project_basis(torch.from_numpy(raw)).numpy(),
+    )
+
+    # 2. random-weight models on seeded frames: full frame, tiled, coefficients
+    cases = [(11, 100, 36, 44), (12, 101, 69, 83), (13, 102, 64, 48)]
+    for wseed, fseed, h, w in cases:
+        state = random_folded_state(wseed)
+        model = folded_from_state(state)
+        frame = make_frame(fseed, h, w)
+        src = frame_chw(frame)
+        with torch.inference_mode():
+            image = padded(src)
+            meta = model.predict_coefficients(image)
+            forward = model(image)
+            whole = upscale(model, src, 0)
+            tiled = upscale(model, src, 32)
+        np.savez_compressed(
+            HERE / f"random_w{wseed}_f{fseed}_{h}x{w}.npz",
+            weight_seed=wseed, frame=frame, meta=meta.numpy(),
+            upscale_tile0=whole.numpy(), upscale_tile32=tiled.numpy(),
+        )
+
+    # 3. initial (head-zero) model equals 2x bilinear (tests/test_reference.py:56-61)
+    state = random_folded_state(21)
+    state["metadata_head.weight"][:] = 0
+    state["metadata_head.bias"][:] = 0
+    from aeisu_b200.synthetic import bilinear_base
+    state["base_kernel"] = bilinear_base()
+    src = torch.from_numpy(np.random.default_rng(22).random((1, 3, 12, 16), dtype=np.float32))
+    with torch.inference_mode():
+        out = folded_from_state(state)(src)
+        bil = F.interpolate(src, scale_factor=2, mode="bilinear", align_corners=False)
+    np.savez_compressed(HERE / "bilinear_identity.npz", source=src.numpy(), forward=out.numpy(),
+                        bilinear=bil.numpy())
+
+    # 4. trained checkpoints (outputs only; the weights themselves are not stored)
+    ref = Path(args.reference)
+    for ckpt, fseed, h, w, tile, deg in (("aeisu_area.pt", 200, 48, 64, 0, "area"),
+                                          ("aeisu_area.pt", 0, 256, 256, 0, "area"),
+                                          ("aeisu_bicubic.pt", 300, 150, 200, 64, "bicubic")):
+        path = ref / "weights" / ckpt
+        model = load_model(path, "cpu")
+        frame = make_frame(fseed, h, w, deg)
+        with torch.inference_mode():
+            out = upscale(model, frame_chw(frame), tile)
+        u8 = np.floor(out.permute(1, 2, 0).numpy() * 255 + 0.5).astype(np.uint8)
+        extra = {}
+        if h * w <= 64 * 64:
+            extra["upscale_f32"] = out.numpy()
+        else:
+            cy, cx = h, w  # centre 128x128 HR window of the float output
+            extra["window_f32"] = out[:, cy - 64:cy + 64, cx - 64:cx + 64].numpy()
+            extra["window_origin"] = np.array([cy - 64, cx - 64])
+        np.savez_compressed(
+            HERE / f"{Path(ckpt).stem}_f{fseed}_{h}x{w}_t{tile}.npz",
+            checkpoint=ckpt, checkpoint_sha256=sha256(path), frame=frame, tile=tile,
+            degradation=deg, upscale_u8=u8, **extra)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
