@@ -175,6 +175,7 @@ Engine::~Engine() {
     staging_.reset();
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
+    for (auto& e : pool_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
     if (prev >= 0) cudaSetDevice(prev);
 }
@@ -220,14 +221,40 @@ void Engine::upload_weights() {
 
 void Engine::record(int stage, cudaStream_t s) {
     if (!detailed_) return;
-    // ping-pong between ev_[1] and ev_[2]: each mark closes the stage opened by the last one
-    const int cur = (mark_last_ == 1) ? 2 : 1;
-    AEISU_CUDA(cudaEventRecord(ev_[cur], s));
-    AEISU_CUDA(cudaEventSynchronize(ev_[cur]));
-    float ms = 0.f;
-    AEISU_CUDA(cudaEventElapsedTime(&ms, ev_[mark_last_], ev_[cur]));
-    stage_ms_[stage - 1] += ms;
-    mark_last_ = cur;
+    // Stage marks are events recorded in stream order without waiting; timings() resolves
+    // them once the work has completed.  Mark i closes stage marks_[i].first.
+    if (marks_.size() == pool_.size()) {
+        cudaEvent_t e;
+        AEISU_CUDA(cudaEventCreate(&e));
+        pool_.push_back(e);
+    }
+    const size_t i = marks_.size();
+    AEISU_CUDA(cudaEventRecord(pool_[i], s));
+    marks_.push_back({stage, int(i)});
+}
+
+const aeisu_timings& Engine::timings() {
+    if (!timings_pending_) return timings_;
+    DeviceGuard guard(device_);
+    AEISU_CUDA(cudaEventSynchronize(ev_[6]));
+    timings_ = {};
+    float per[6] = {};
+    for (size_t i = 1; i < marks_.size(); ++i) {
+        float ms = 0.f;
+        AEISU_CUDA(cudaEventElapsedTime(&ms, pool_[marks_[i - 1].second], pool_[marks_[i].second]));
+        if (marks_[i].first >= 1 && marks_[i].first <= 5) per[marks_[i].first] += ms;
+    }
+    timings_.analysis_project_ms = per[1];
+    timings_.compress_core_ms = per[2];
+    timings_.expand_ms = per[3];
+    timings_.refine_tail_ms = per[4];
+    timings_.reconstruction_ms = per[5];
+    float total = 0.f;
+    AEISU_CUDA(cudaEventElapsedTime(&total, ev_[0], ev_[6]));
+    timings_.total_ms = total;
+    timings_.detailed = marks_.size() > 1 ? 1 : 0;
+    timings_pending_ = false;
+    return timings_;
 }
 
 void Engine::wait(cudaStream_t s, double timeout_ms) {
@@ -323,7 +350,8 @@ void Engine::run(const Call& c) {
     if (c.mode == Mode::Predict) dst_bytes = size_t(c.n) * (c.h / 2) * (c.w / 2) * 64 * 4;
     else dst_bytes = size_t(c.n) * 3 * (2 * size_t(g.out_h)) * (2 * size_t(g.out_w)) * (c.dst_kind == 0 ? 1 : 4);
 
-    stage_ms_.assign(5, 0.f);
+    marks_.clear();
+    timings_pending_ = true;
     AEISU_CUDA(cudaEventRecord(ev_[0], s));
     const void* src_ptr = c.src;
     void* dst_ptr = c.dst;
@@ -335,11 +363,7 @@ void Engine::run(const Call& c) {
         dst_ptr = dst_.get();
     }
     AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, sizeof(int), s));
-    if (detailed_) {
-        AEISU_CUDA(cudaEventRecord(ev_[1], s));
-        AEISU_CUDA(cudaEventSynchronize(ev_[1]));
-        mark_last_ = 1;
-    }
+    record(0, s);
     SrcDesc src{src_ptr, c.src_kind, c.h, c.w, g.pad_y, g.pad_x};
     DstDesc dst{dst_ptr, c.dst_kind, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
     for (const auto& grp : g.groups) run_group(c, g, grp, src, dst, s);
@@ -354,16 +378,6 @@ void Engine::run(const Call& c) {
     if (c.host) {
         wait(s, timeout_ms_);
         if (staged) std::memcpy(c.dst, staging_.get(), dst_bytes);
-        float total = 0.f;
-        AEISU_CUDA(cudaEventElapsedTime(&total, ev_[0], ev_[6]));
-        timings_ = {};
-        timings_.analysis_project_ms = stage_ms_[0];
-        timings_.compress_core_ms = stage_ms_[1];
-        timings_.expand_ms = stage_ms_[2];
-        timings_.refine_tail_ms = stage_ms_[3];
-        timings_.reconstruction_ms = stage_ms_[4];
-        timings_.total_ms = total;
-        timings_.detailed = detailed_ ? 1 : 0;
         int flag = 0;
         AEISU_CUDA(cudaMemcpy(&flag, flag_.get(), sizeof(int), cudaMemcpyDeviceToHost));
         if (flag && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");

@@ -93,7 +93,8 @@ public:
     const std::string& report() const { return report_; }
     uint64_t device_bytes() const;
     uint64_t launches() const { return launches_; }
-    const aeisu_timings& timings() const { return timings_; }
+    // Stage times of the last call (waits for it to finish when stage marks are pending).
+    const aeisu_timings& timings();
     void set_detailed(bool on) { detailed_ = on; }
     void set_timeout(double ms) { timeout_ms_ = ms; }
     int precision() const { return precision_; }
@@ -131,8 +132,9 @@ private:
 
     // timing events: [0] call start, [1]/[2] detailed stage marks, [6] call end, [7] waits
     cudaEvent_t ev_[8] = {};
-    int mark_last_ = 1;
-    std::vector<float> stage_ms_;
+    std::vector<cudaEvent_t> pool_;                // stage-mark events, reused across calls
+    std::vector<std::pair<int, int>> marks_;       // (stage closed by this mark, pool index)
+    bool timings_pending_ = false;
 };
 
 }  // namespace aeisu

@@ -40,8 +40,9 @@ STATE_SHAPES = (
 
 
 def leaky(x):
-    """F.leaky_relu(x, 0.1) (aeisu/model.py:202-203)."""
-    return np.where(x > 0, x, x * SLOPE).astype(F32)
+    """F.leaky_relu(x, 0.1) (aeisu/model.py:202-203); max(x, 0.1x) is the same map for slope < 1."""
+    t = np.multiply(x, SLOPE, dtype=F32)
+    return np.maximum(x, t, out=t)
 
 
 def pixel_unshuffle(x, r=2):
@@ -59,26 +60,42 @@ def pixel_shuffle(x, r=2):
             .reshape(b, co, h * r, w * r))
 
 
-def conv2d(x, weight, bias, groups=1):
-    """nn.Conv2d(padding=k//2, zero padding) as im2col + float32 GEMM."""
-    b, c, h, w = x.shape
+def conv2d_nhwc(x, weight, bias, groups=1):
+    """nn.Conv2d(padding=k//2, zero padding) on NHWC float32 data as float32 GEMMs.
+
+    3x3: the zero-padded input is flattened row-major with row pitch W+2, so tap (ky, kx)
+    of every output pixel is the contiguous slice shifted by ky*(W+2)+kx; each tap is one
+    GEMM, accumulated, and the two pitch-padding columns are dropped at the end."""
+    b, h, w, c = x.shape
     cout, cin_g, k, _ = weight.shape
-    p = k // 2
-    xp = np.pad(x, ((0, 0), (0, 0), (p, p), (p, p))) if p else x
-    out = np.empty((b, cout, h, w), F32)
     cout_g = cout // groups
+    if k == 1:
+        out = np.empty((b, h * w, cout), F32)
+        xf = x.reshape(b, h * w, c)
+        for g in range(groups):
+            wg = weight[g * cout_g:(g + 1) * cout_g, :, 0, 0]
+            out[:, :, g * cout_g:(g + 1) * cout_g] = xf[:, :, g * cin_g:(g + 1) * cin_g] @ wg.T
+        out += bias
+        return out.reshape(b, h, w, cout)
+    pitch = w + 2
+    flat = np.pad(x, ((0, 0), (1, 1), (1, 1), (0, 0))).reshape(b, (h + 2) * pitch, c)
+    n = (h - 1) * pitch + w
+    out = np.zeros((b, h * pitch, cout), F32)
     for g in range(groups):
-        xs = xp[:, g * cin_g:(g + 1) * cin_g]
-        if k == 1:
-            cols = xs.transpose(0, 2, 3, 1).reshape(b, h * w, cin_g)
-        else:
-            win = np.lib.stride_tricks.sliding_window_view(xs, (k, k), axis=(2, 3))
-            cols = win.transpose(0, 2, 3, 1, 4, 5).reshape(b, h * w, cin_g * k * k)
-        wg = weight[g * cout_g:(g + 1) * cout_g].reshape(cout_g, -1)
-        res = np.matmul(cols, wg.T)
-        res += bias[g * cout_g:(g + 1) * cout_g]
-        out[:, g * cout_g:(g + 1) * cout_g] = res.transpose(0, 2, 1).reshape(b, cout_g, h, w)
-    return out
+        cs = slice(g * cin_g, (g + 1) * cin_g)
+        os_ = slice(g * cout_g, (g + 1) * cout_g)
+        for ky in range(3):
+            for kx in range(3):
+                off = ky * pitch + kx
+                out[:, :n, os_] += flat[:, off:off + n, cs] @ weight[os_, :, ky, kx].T
+    out = out.reshape(b, h, pitch, cout)[:, :, :w]
+    return out + bias
+
+
+def conv2d(x, weight, bias, groups=1):
+    """NCHW wrapper of conv2d_nhwc."""
+    return np.ascontiguousarray(
+        conv2d_nhwc(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), weight, bias, groups).transpose(0, 3, 1, 2))
 
 
 def feature8(src, st):
@@ -116,19 +133,31 @@ def controller(src, st):
     if src.shape[2] % 4 or src.shape[3] % 4:
         raise ValueError("Source H/W must be divisible by 4")
 
+    # Same graph, computed channels-last; the unshuffle/shuffle index maps are those of
+    # F.pixel_unshuffle / F.pixel_shuffle (channel c*4 + i*2 + j <-> pixel offset (i, j)).
     def conv(name, x, groups=1):
-        return conv2d(x, st[f"{name}.weight"], st[f"{name}.bias"], groups)
+        return conv2d_nhwc(x, st[f"{name}.weight"], st[f"{name}.bias"], groups)
 
-    feat = feature8(src, st)
-    enc540 = leaky(conv("project_540", pixel_unshuffle(feat)))
-    enc270 = leaky(conv("compress_270", pixel_unshuffle(enc540)))
-    a, b = enc270[:, :32], enc270[:, 32:]
+    def unshuffle(x):
+        b, h, w, c = x.shape
+        return (x.reshape(b, h // 2, 2, w // 2, 2, c).transpose(0, 1, 3, 5, 2, 4)
+                .reshape(b, h // 2, w // 2, c * 4))
+
+    def shuffle(x):
+        b, h, w, c4 = x.shape
+        c = c4 // 4
+        return (x.reshape(b, h, w, c, 2, 2).transpose(0, 1, 4, 2, 5, 3).reshape(b, h * 2, w * 2, c))
+
+    feat = np.ascontiguousarray(feature8(src, st).transpose(0, 2, 3, 1))
+    enc540 = leaky(conv("project_540", unshuffle(feat)))
+    enc270 = leaky(conv("compress_270", unshuffle(enc540)))
+    a, b = np.ascontiguousarray(enc270[..., :32]), np.ascontiguousarray(enc270[..., 32:])
     for i in range(1, 5):
         a = leaky(conv(f"bottleneck_270_a{i}", a))
         b = leaky(conv(f"bottleneck_270_b{i}", b))
-    up540 = pixel_shuffle(leaky(conv("expand_270", np.concatenate((a, b), axis=1))))
+    up540 = shuffle(leaky(conv("expand_270", np.concatenate((a, b), axis=-1))))
     dec540 = leaky(conv("refine_540", enc540 + up540))
-    return conv("metadata_head", dec540)
+    return np.ascontiguousarray(conv("metadata_head", dec540).transpose(0, 3, 1, 2))
 
 
 def project_basis(raw, scale=0.5):
@@ -154,7 +183,8 @@ def unpack_coefficients(meta):
     if c != 64:
         raise ValueError("Expected 64 packed coefficient channels")
     packed = meta.reshape(b, 4, 16, h, w).transpose(0, 2, 1, 3, 4).reshape(b, 64, h, w)
-    return coefficient_clamp(pixel_shuffle(packed))
+    # the clamp is elementwise, so it is applied before the (copying) shuffle
+    return pixel_shuffle(coefficient_clamp(packed))
 
 
 def reconstruct(src, meta, base, basis):
@@ -163,16 +193,19 @@ def reconstruct(src, meta, base, basis):
     if meta.shape != (b, 64, h // 2, w // 2):
         raise ValueError("Source, metadata or trim geometry is invalid")
     coeff = unpack_coefficients(meta)                        # [B,16,h,w]
+    cf = np.ascontiguousarray(coeff.transpose(0, 2, 3, 1)).reshape(b, h * w, 16)
     local = np.pad(src, ((0, 0), (0, 0), (2, 2), (2, 2)), mode="edge")
-    patches = np.stack([local[:, :, ky:ky + h, kx:kx + w]
-                        for ky in range(5) for kx in range(5)], axis=2)  # [B,3,25,h,w]
-    phases = []
-    for p in range(4):
-        weights = base[:, p][None, :, None, None] + np.einsum(
-            "bkyx,tk->btyx", coeff, basis[:, :, p], optimize=True).astype(F32)
-        phases.append((patches * weights[:, None]).sum(axis=2, dtype=F32))
-    stacked = np.stack(phases, axis=2).reshape(b, 12, h, w)
-    return pixel_shuffle(stacked).astype(F32)
+    # rgb[b, c, y, x, phase] = sum_t patch_t[c] * (base[t, phase] + sum_k coeff_k * basis[t, k, phase]),
+    # taps t = 5*ky + kx of the replicate-padded 5x5 neighbourhood (unfold order)
+    rgb = np.zeros((b, 3, h, w, 4), F32)
+    for ky in range(5):
+        for kx in range(5):
+            t = ky * 5 + kx
+            wt = (cf @ basis[t] + base[t]).reshape(b, h, w, 4)
+            for c in range(3):
+                rgb[:, c] += local[:, c, ky:ky + h, kx:kx + w, None] * wt
+    out = rgb.reshape(b, 3, h, w, 2, 2).transpose(0, 1, 2, 4, 3, 5).reshape(b, 3, 2 * h, 2 * w)
+    return np.ascontiguousarray(out, F32)
 
 
 class FoldedModel:
