@@ -13,6 +13,7 @@
 #include <thread>
 
 #include "common.h"
+#include "tc_pack.h"
 
 namespace aeisu {
 
@@ -146,9 +147,13 @@ Engine::Engine(HostModel model, int precision, int device)
     int count = 0;
     AEISU_CUDA(cudaGetDeviceCount(&count));
     require(device >= 0 && device < count, "device index out of range");
-    if (precision != AEISU_PRECISION_FP32)
-        fail(AEISU_ERR_UNSUPPORTED, "this build provides the FP32 route only");
+    if (precision == AEISU_PRECISION_MIXED && !model_.has_fp8)
+        fail(AEISU_ERR_UNSUPPORTED, "MIXED precision needs the FP8 weights and scales of a SPYR8 artifact");
     DeviceGuard guard(device_);
+    cudaDeviceProp dp{};
+    AEISU_CUDA(cudaGetDeviceProperties(&dp, device_));
+    if (precision != AEISU_PRECISION_FP32 && !(dp.major == 10 && dp.minor == 0))
+        fail(AEISU_ERR_UNSUPPORTED, "the tensor-core routes need an sm_100 (B200) device");
     int lo = 0, hi = 0;
     AEISU_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
     AEISU_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
@@ -161,7 +166,9 @@ Engine::Engine(HostModel model, int precision, int device)
        << prop.multiProcessorCount << " SMs); model " << model_.format << " " << model_.architecture;
     if (!model_.checksum_hex.empty()) os << " sha256 " << model_.checksum_hex;
     os << "; precision " << (precision_ == 0 ? "fp32" : precision_ == 1 ? "fp16" : "mixed");
-    os << "; route simt-fp32 controller + fp32 head";
+    if (precision_ == AEISU_PRECISION_FP32) os << "; route simt-fp32 controller + fp32 head";
+    else if (precision_ == AEISU_PRECISION_FP16) os << "; route tcgen05 f16 controller + tcgen05 head";
+    else os << "; route tcgen05 e4m3/f16 mixed controller + tcgen05 head";
     report_ = os.str();
 }
 
@@ -170,7 +177,8 @@ Engine::~Engine() {
     cudaGetDevice(&prev);
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
-    DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_, &meta_};
+    DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_,
+                     &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
     for (DevBuf* b : all) b->reset();
     staging_.reset();
     for (auto& e : ev_)
@@ -181,8 +189,8 @@ Engine::~Engine() {
 }
 
 uint64_t Engine::device_bytes() const {
-    const DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_,
-                           &low_b_, &dec540_, &refined_, &meta_};
+    const DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_,
+                           &refined_, &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
     uint64_t total = 0;
     for (auto* b : all) total += b->capacity();
     return total;
@@ -217,6 +225,37 @@ void Engine::upload_weights() {
     for (int l = 0; l < kLayerCount; ++l)
         f32_layers_[l] = {d + o_w[l], d + o_b[l], model_.layers[l].slope[0]};
     flag_.ensure(256, stream_);
+    AEISU_CUDA(cudaMemset(flag_.get(), 0, 256));
+    if (precision_ == AEISU_PRECISION_FP32) return;
+    const TcHostPack P = pack_tc(model_, precision_ == AEISU_PRECISION_MIXED);
+    tc_bytes_.ensure(P.bytes.size(), stream_);
+    tc_floats_.ensure(P.floats.size() * 4, stream_);
+    AEISU_CUDA(cudaMemcpy(tc_bytes_.get(), P.bytes.data(), P.bytes.size(), cudaMemcpyHostToDevice));
+    AEISU_CUDA(cudaMemcpy(tc_floats_.get(), P.floats.data(), P.floats.size() * 4, cudaMemcpyHostToDevice));
+    const uint8_t* B = tc_bytes_.as<uint8_t>();
+    const float* F = tc_floats_.as<float>();
+    auto ep = [&](const TcHostLayer& L) {
+        return EpiParams{F + L.scale, F + L.bias, P.slope, L.out_inv, L.out_deq};
+    };
+    tcw_.stencil = F + P.stencil;
+    tcw_.project = B + P.project;
+    tcw_.project_bias = F + P.project_bias;
+    tcw_.slope = P.slope;
+    tcw_.inv_s1 = P.inv_s1;
+    tcw_.compress = B + P.compress.image;
+    tcw_.compress_ep = ep(P.compress);
+    for (int i = 0; i < 4; ++i) {
+        tcw_.core[i] = B + P.core[i].image;
+        tcw_.core_ep[i] = ep(P.core[i]);
+    }
+    tcw_.expand = B + P.expand.image;
+    tcw_.expand_ep = ep(P.expand);
+    tcw_.refine = B + P.refine;
+    tcw_.tail = B + P.tail;
+    tcw_.refine_bias = F + P.refine_bias;
+    tcw_.tail_bias = F + P.tail_bias;
+    tcw_.head = B + P.head;
+    tc_head_off_ = P.head;
 }
 
 void Engine::record(int stage, cudaStream_t s) {
@@ -275,19 +314,27 @@ void Engine::synchronize(cudaStream_t s, double timeout_ms) {
     DeviceGuard guard(device_);
     if (!s) s = stream_;
     wait(s, timeout_ms);
-    int flag = 0;
-    AEISU_CUDA(cudaMemcpy(&flag, flag_.get(), sizeof(int), cudaMemcpyDeviceToHost));
-    if (flag) {
-        AEISU_CUDA(cudaMemset(flag_.get(), 0, sizeof(int)));
-        fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
-    }
+    int flag[2] = {0, 0};
+    AEISU_CUDA(cudaMemcpy(flag, flag_.get(), sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag[0] || flag[1]) AEISU_CUDA(cudaMemset(flag_.get(), 0, sizeof(flag)));
+    if (flag[1]) fail(AEISU_ERR_CUDA, "tensor-core pipeline wait expired inside a kernel");
+    if (flag[0]) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
 }
 
 void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
                        const DstDesc& dst, cudaStream_t s) {
     const int rh = grp.rh, rw = grp.rw;
     const size_t packed = size_t(rh / 2) * (rw / 2), low = size_t(rh / 4) * (rw / 4);
-    const size_t per_region = 4 * (packed * (32 + 32 + 64 + 64) + low * 64 * 2);
+    const bool tcr = precision_ != AEISU_PRECISION_FP32, fp8 = precision_ == AEISU_PRECISION_MIXED;
+    // workspace bytes per region: f32 NHWC for the FP32 route; chunk-planar f16/e4m3 otherwise
+    const size_t enc_b = tcr ? packed * 64 : packed * 32 * 4;
+    const size_t encu_b = tcr ? low * (fp8 ? 128 : 256) : 0;
+    const size_t low_b = tcr ? low * (fp8 ? 64 : 128) : low * 64 * 4;
+    const size_t dec_b = tcr ? packed * 64 : packed * 32 * 4;
+    const size_t ref_b = tcr ? 0 : packed * 64 * 4;
+    const size_t meta_b = tcr ? size_t(rh) * rw * 32 : packed * 64 * 4;
+    const size_t raw_b = (tcr && c.mode == Mode::Predict) ? packed * 64 * 4 : 0;
+    const size_t per_region = enc_b + encu_b + 2 * low_b + dec_b + ref_b + meta_b + raw_b;
     const size_t chunk = std::max<size_t>(1, std::min<size_t>(grp.regions.size(), workspace_cap_ / per_region));
     for (size_t first = 0; first < grp.regions.size(); first += chunk) {
         const int R = int(std::min(chunk, grp.regions.size() - first));
@@ -307,29 +354,41 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
         rs.regions = tables_.as<int4>();
         rs.cores = tables_.as<int4>() + R;
         rs.R = R; rs.rh = rh; rs.rw = rw; rs.core_h = core_h; rs.core_w = core_w;
-        enc540_.ensure(4 * packed * 32 * R, s);
-        dec540_.ensure(4 * packed * 32 * R, s);
-        refined_.ensure(4 * packed * 64 * R, s);
-        meta_.ensure(4 * packed * 64 * R, s);
-        low_a_.ensure(4 * low * 64 * R, s);
-        low_b_.ensure(4 * low * 64 * R, s);
+        enc540_.ensure(enc_b * R, s);
+        dec540_.ensure(dec_b * R, s);
+        if (ref_b) refined_.ensure(ref_b * R, s);
+        if (encu_b) encu_.ensure(encu_b * R, s);
+        if (raw_b) raw_.ensure(raw_b * R, s);
+        meta_.ensure(meta_b * R, s);
+        low_a_.ensure(low_b * R, s);
+        low_b_.ensure(low_b * R, s);
         int launches = 0;
         struct Ctx { Engine* e; cudaStream_t s; } ctx{this, s};
         StageMark mark;
         mark.ctx = &ctx;
         mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
-        launch_f32_controller(src, rs, stencil_, f32_layers_, enc540_.as<float>(), low_a_.as<float>(),
-                              low_b_.as<float>(), dec540_.as<float>(), refined_.as<float>(), meta_.as<float>(), s,
-                              &launches, mark);
-        if (c.mode == Mode::Predict) {
+        const bool predict = c.mode == Mode::Predict;
+        if (tcr) {
+            launch_tc_controller(fp8, src, rs, tcw_, enc540_.get(), encu_.get(), low_a_.get(), low_b_.get(),
+                                 dec540_.get(), meta_.get(), predict ? raw_.as<float>() : nullptr,
+                                 flag_.as<int>() + 1, s, &launches, mark);
+        } else {
+            launch_f32_controller(src, rs, stencil_, f32_layers_, enc540_.as<float>(), low_a_.as<float>(),
+                                  low_b_.as<float>(), dec540_.as<float>(), refined_.as<float>(), meta_.as<float>(), s,
+                                  &launches, mark);
+        }
+        if (predict) {
             // one region per frame, covering it: metadata NHWC [h/2, w/2, 64] per frame
             const size_t bytes = 4 * packed * 64;
+            const char* meta = tcr ? raw_.as<char>() : meta_.as<char>();
             for (int i = 0; i < R; ++i) {
                 const int f = grp.regions[first + i].frame;
                 char* out = static_cast<char*>(c.host ? dst_.get() : c.dst) + size_t(f) * bytes;
-                AEISU_CUDA(cudaMemcpyAsync(out, meta_.as<char>() + size_t(i) * bytes, bytes,
-                                           cudaMemcpyDeviceToDevice, s));
+                AEISU_CUDA(cudaMemcpyAsync(out, meta + size_t(i) * bytes, bytes, cudaMemcpyDeviceToDevice, s));
             }
+        } else if (tcr) {
+            launch_tc_head(src, rs, dst, meta_.get(), tc_bytes_.as<uint8_t>() + tc_head_off_, flag_.as<int>(),
+                           flag_.as<int>() + 1, s, &launches);
         } else {
             launch_f32_head(src, rs, dst, meta_.as<float>(), base_, basis_, flag_.as<int>(), s, &launches);
         }
@@ -362,7 +421,7 @@ void Engine::run(const Call& c) {
         src_ptr = src_.get();
         dst_ptr = dst_.get();
     }
-    AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, sizeof(int), s));
+    AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, 2 * sizeof(int), s));  // [0] non-finite, [1] pipeline error
     record(0, s);
     SrcDesc src{src_ptr, c.src_kind, c.h, c.w, g.pad_y, g.pad_x};
     DstDesc dst{dst_ptr, c.dst_kind, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
@@ -378,9 +437,11 @@ void Engine::run(const Call& c) {
     if (c.host) {
         wait(s, timeout_ms_);
         if (staged) std::memcpy(c.dst, staging_.get(), dst_bytes);
-        int flag = 0;
-        AEISU_CUDA(cudaMemcpy(&flag, flag_.get(), sizeof(int), cudaMemcpyDeviceToHost));
-        if (flag && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
+        int flag[2] = {0, 0};
+        AEISU_CUDA(cudaMemcpy(flag, flag_.get(), sizeof(flag), cudaMemcpyDeviceToHost));
+        if (flag[1]) fail(AEISU_ERR_CUDA, "tensor-core pipeline wait expired inside a kernel (code " +
+                                              std::to_string(flag[1]) + ")");
+        if (flag[0] && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
     }
 }
 

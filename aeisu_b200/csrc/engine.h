@@ -123,11 +123,14 @@ private:
     const float* base_ = nullptr;
     const float* basis_ = nullptr;
     F32Layer f32_layers_[kLayerCount]{};
+    DevBuf tc_bytes_, tc_floats_;  // tensor-core routes: operand images, epilogue vectors
+    TcWeights tcw_{};
+    size_t tc_head_off_ = 0;
 
     // workspace
     DevBuf src_, dst_, tables_, flag_;
     HostBuf staging_;
-    DevBuf enc540_, low_a_, low_b_, dec540_, refined_, meta_;
+    DevBuf enc540_, low_a_, low_b_, dec540_, refined_, meta_, encu_, raw_;
     size_t workspace_cap_ = size_t(6) << 30;
 
     // timing events: [0] call start, [1]/[2] detailed stage marks, [6] call end, [7] waits

@@ -49,6 +49,45 @@ void launch_f32_controller(const SrcDesc& src, const RegionSet& rs, const float*
                            const F32Layer* layers, float* enc540, float* low_a, float* low_b,
                            float* dec540, float* refined, float* meta, cudaStream_t s, int* launches,
                            const StageMark& mark);
+// Epilogue parameters of a tensor-core convolution layer.
+struct EpiParams {
+    const float* scale;   // per output channel: accumulator multiplier (FP8: s_in * w_scale)
+    const float* bias;    // per output channel
+    float slope;          // LeakyReLU negative slope
+    float out_inv;        // FP8 output quantisation: 1/s_out
+    float out_deq;        // expand: dequantisation s_out
+};
+
+// Device images of the tensor-core routes' weights, already in the K-major operand layout
+// of tc.cuh (chunk-major, 16 bytes per row per chunk), plus per-channel epilogue vectors.
+struct TcWeights {
+    const float* stencil;
+    const uint8_t* project;        // [4 chunks][32][16 B] f16
+    const float* project_bias;
+    float slope;
+    float inv_s1;                  // 1/activation_scales[1] (mixed route)
+    const uint8_t* compress;       // [K/epc][64][16 B], K order phase*32 + c
+    EpiParams compress_ep;
+    const uint8_t* core[4];        // 2 groups x [9*32/epc][32][16 B], K order tap*32 + c
+    EpiParams core_ep[4];
+    const uint8_t* expand;         // [64/epc][128][16 B], N order phase*32 + c
+    EpiParams expand_ep;
+    const uint8_t* refine;         // [36][64][16 B] f16, K order tap*32 + c
+    const uint8_t* tail;           // [8][64][16 B] f16
+    const float* refine_bias;
+    const float* tail_bias;
+    const uint8_t* head;           // 3 x [2][128][16 B] f16: basis hi, basis lo, base hi|lo
+};
+
+// Tensor-core route (k_tc.cu).  fp8 selects the mixed FP8/FP16 route, else FP16.
+// Buffers are chunk-planar: enc540 [R][ph][4][pw][16], encu [R][lh][K/epc][lw][16],
+// low [R][lh][64/epc][lw][16], dec540 [R][ph][4][pw][16], meta [R][rh][2][rw][16].
+void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
+                          void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
+                          int* err, cudaStream_t s, int* launches, const StageMark& mark);
+void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const void* meta,
+                    const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, int* launches);
+
 void launch_f32_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst,
                      const float* meta, const float* base, const float* basis, int* nonfinite,
                      cudaStream_t s, int* launches);

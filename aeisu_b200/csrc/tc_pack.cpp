@@ -1,0 +1,126 @@
+#include "tc_pack.h"
+
+#include "common.h"
+
+namespace aeisu {
+namespace {
+
+size_t append_bytes(std::vector<uint8_t>& dst, const std::vector<uint8_t>& img) {
+    while (dst.size() % 128) dst.push_back(0);
+    const size_t at = dst.size();
+    dst.insert(dst.end(), img.begin(), img.end());
+    return at;
+}
+
+size_t append_floats(std::vector<float>& dst, const std::vector<float>& v) {
+    while (dst.size() % 32) dst.push_back(0.f);
+    const size_t at = dst.size();
+    dst.insert(dst.end(), v.begin(), v.end());
+    return at;
+}
+
+float round_f16(float v) { return f16_bits_to_f32(f32_to_f16_bits(v)); }
+
+}  // namespace
+
+TcHostPack pack_tc(const HostModel& m, bool fp8) {
+    require(!fp8 || m.has_fp8, "the mixed route needs the FP8 weights and scales of a SPYR8 artifact",
+            AEISU_ERR_UNSUPPORTED);
+    TcHostPack P;
+    const float* s = m.act_scales;
+    P.slope = m.layers[kProject].slope[0];
+    P.inv_s1 = fp8 ? 1.0f / s[1] : 1.f;
+    P.stencil = append_floats(P.floats, std::vector<float>(m.stencil, m.stencil + 24));
+
+    // project_540: [32 out][32 in], K = torch input channel order (feature c*4 + phase)
+    {
+        const LayerWeights& L = m.layers[kProject];
+        P.project = append_bytes(P.bytes, pack_operand(32, 32, 2, [&](int n, int k) { return L.w_fp16[n * 32 + k]; }));
+        P.project_bias = append_floats(P.floats, L.bias);
+    }
+    // per-channel epilogue vectors; `perm` maps the packed output order to the torch channel
+    auto epilogue = [&](TcHostLayer& out, const LayerWeights& L, int n, float s_in, float s_out, auto perm) {
+        std::vector<float> scale(n), bias(n);
+        for (int i = 0; i < n; ++i) {
+            const int o = perm(i);
+            scale[i] = fp8 ? s_in * L.w_scale[o] : 1.f;
+            bias[i] = fp8 ? L.bias_fp8[o] : L.bias[o];
+        }
+        out.scale = append_floats(P.floats, scale);
+        out.bias = append_floats(P.floats, bias);
+        out.out_inv = fp8 ? 1.0f / s_out : 1.f;
+    };
+    const int es = fp8 ? 1 : 2;
+    auto elem = [&](const LayerWeights& L, size_t idx) -> uint32_t { return fp8 ? L.w_fp8[idx] : L.w_fp16[idx]; };
+
+    // compress_270: [64][128]; packed K order phase*32 + c <- torch input c*4 + phase
+    {
+        const LayerWeights& L = m.layers[kCompress];
+        P.compress.image = append_bytes(P.bytes, pack_operand(64, 128, es, [&](int n, int kk) {
+            return elem(L, size_t(n) * 128 + (kk % 32) * 4 + kk / 32);
+        }));
+        epilogue(P.compress, L, 64, s[1], s[2], [](int i) { return i; });
+    }
+    // bottleneck i: two groups of [32 out][9 taps x 32 in], K order tap*32 + c
+    for (int i = 0; i < 4; ++i) {
+        const LayerWeights& L = m.layers[kCore0 + i];
+        std::vector<uint8_t> img;
+        for (int g = 0; g < 2; ++g) {
+            auto part = pack_operand(32, 288, es, [&](int n, int kk) {
+                const int tap = kk / 32, c = kk % 32;
+                return elem(L, (size_t(g * 32 + n) * 32 + c) * 9 + tap);
+            });
+            img.insert(img.end(), part.begin(), part.end());
+        }
+        P.core[i].image = append_bytes(P.bytes, img);
+        epilogue(P.core[i], L, 64, s[i + 2], s[i + 3], [](int n) { return n; });
+    }
+    // expand_270: [128][64], output order phase*32 + c <- torch output c*4 + phase
+    {
+        const LayerWeights& L = m.layers[kExpand];
+        auto torch_out = [](int n) { return (n % 32) * 4 + n / 32; };
+        P.expand.image = append_bytes(P.bytes, pack_operand(128, 64, es, [&](int n, int k) {
+            return elem(L, size_t(torch_out(n)) * 64 + k);
+        }));
+        epilogue(P.expand, L, 128, s[6], s[7], torch_out);
+        P.expand.out_deq = fp8 ? s[7] : 1.f;
+    }
+    // refine_540: [64][9 taps x 32], f16 in both routes; metadata_head [64][64] f16
+    {
+        const LayerWeights& R = m.layers[kRefine];
+        P.refine = append_bytes(P.bytes, pack_operand(64, 288, 2, [&](int n, int kk) {
+            return R.w_fp16[(size_t(n) * 32 + kk % 32) * 9 + kk / 32];
+        }));
+        P.refine_bias = append_floats(P.floats, R.bias);
+        const LayerWeights& T = m.layers[kTail];
+        P.tail = append_bytes(P.bytes, pack_operand(64, 64, 2, [&](int n, int k) { return T.w_fp16[n * 64 + k]; }));
+        std::vector<float> tb(64);
+        for (int i = 0; i < 64; ++i) tb[i] = round_f16(T.bias[i]);  // f16 tail bias (Refine.cuh:494-495)
+        P.tail_bias = append_floats(P.floats, tb);
+    }
+    // head: column n = tap*4 + phase (100 used of 128); FP32 bank split into hi + lo f16
+    {
+        auto bank = [&](int n, int k, bool lo) -> uint32_t {
+            if (n >= 100) return 0;
+            const float v = m.basis[((n / 4) * 16 + k) * 4 + n % 4];
+            const uint16_t hi = f32_to_f16_bits(v);
+            return lo ? f32_to_f16_bits(v - f16_bits_to_f32(hi)) : hi;
+        };
+        auto hi = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, false); });
+        auto lo = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, true); });
+        auto base = pack_operand(128, 16, 2, [&](int n, int k) -> uint32_t {
+            if (n >= 100 || k > 1) return 0;
+            const float v = m.base[(n / 4) * 4 + n % 4];
+            const uint16_t h = f32_to_f16_bits(v);
+            return k == 0 ? h : f32_to_f16_bits(v - f16_bits_to_f32(h));
+        });
+        std::vector<uint8_t> img(hi);
+        img.insert(img.end(), lo.begin(), lo.end());
+        img.insert(img.end(), base.begin(), base.end());
+        P.head = append_bytes(P.bytes, img);
+    }
+    while (P.bytes.size() % 128) P.bytes.push_back(0);
+    return P;
+}
+
+}  // namespace aeisu

@@ -196,7 +196,7 @@ class Model:
         return out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data
 
     def _wrap(self, arr: _Array, out):
-        if arr.torch is not None and not arr.device:
+        if arr.torch is not None and not arr.device and isinstance(out, np.ndarray):
             return arr.torch.from_numpy(out)
         return out
 

@@ -1,0 +1,128 @@
+"""Tensor-core routes (FP16 and mixed FP8-E4M3/FP16) on the GPU against the FP32 semantics.
+
+Bar (north star): PSNR >= 50 dB against the reference FP32 output on the same weights.
+The SPYR8 artifact of the reference (adaptive_fp8.bin) was exported from aeisu_area.pt, so
+its FP32 reference is the folded area checkpoint; synthetic artifacts are built from random
+folded weights with activation scales calibrated by the oracle."""
+import numpy as np
+import pytest
+
+from conftest import staged
+from oracle import aeisu_np as O
+from aeisu_b200 import Model, load_model, upscale
+from aeisu_b200.synthetic import make_frame, make_frames, random_folded_state
+from spyr8_helpers import build_artifact
+
+pytestmark = pytest.mark.gpu
+MIN_PSNR = 50.0
+
+
+def psnr_vs(ref_chw, got_chw):
+    return O.psnr(np.clip(got_chw, 0, 1), np.clip(ref_chw, 0, 1))
+
+
+def psnr_u8(a, b):
+    return O.psnr(a.astype(np.float64) / 255, b.astype(np.float64) / 255)
+
+
+@pytest.fixture(scope="module")
+def synthetic():
+    state = random_folded_state(41, coeff_gain=0.5)
+    frames = [make_frame(600 + i, 96, 128) for i in range(3)]
+    return state, build_artifact(state, frames)
+
+
+@pytest.mark.parametrize("precision", ["fp16", "mixed"])
+@pytest.mark.parametrize("h,w,tile", [(72, 100, 0), (33, 65, 0), (150, 200, 64), (1, 1, 0)])
+def test_synthetic_weights_psnr(synthetic, precision, h, w, tile):
+    state, artifact = synthetic
+    frame = make_frame(700 + h, h, w)
+    ref = O.upscale(O.FoldedModel(state), O.u8_to_chw(frame), tile)
+    model = (Model.from_spyr8_bytes(artifact, "cuda:0", precision) if precision == "mixed"
+             else Model.from_folded_state(state, "cuda:0", "fp16"))
+    try:
+        got = model.upscale_f32(O.u8_to_chw(frame), tile)
+        assert got.shape == ref.shape
+        p = psnr_vs(ref, got)
+        assert p >= MIN_PSNR, f"{precision} PSNR {p:.2f} dB"
+        u8 = model.upscale_u8(frame, tile)
+        assert psnr_u8(u8, O.chw_to_u8(ref)) >= MIN_PSNR - 3
+    finally:
+        model.close()
+
+
+@pytest.mark.parametrize("precision", ["fp16", "mixed"])
+def test_reference_artifact_psnr(precision):
+    ref_model = O.load_folded(staged("aeisu_area.pt"))
+    model = load_model(staged("adaptive_fp8.bin"), "cuda:0", precision)
+    try:
+        for seed, (h, w) in ((800, (72, 128)), (801, (256, 256))):
+            frame = make_frame(seed, h, w)
+            ref = O.upscale(ref_model, O.u8_to_chw(frame), 0)
+            got = model.upscale_f32(O.u8_to_chw(frame), 0)
+            p = psnr_vs(ref, got)
+            assert p >= MIN_PSNR, f"{precision} PSNR {p:.2f} dB on {w}x{h}"
+    finally:
+        model.close()
+
+
+def test_fp16_route_from_folded_checkpoint_1080p():
+    path = staged("aeisu_area.pt")
+    frame = make_frame(1000, 1080, 1920)
+    ref = O.upscale(O.load_folded(path), O.u8_to_chw(frame), 0)
+    model = load_model(path, "cuda:0", "fp16")
+    try:
+        p = psnr_u8(model.upscale_u8(frame, 0), O.chw_to_u8(ref))
+        assert p >= MIN_PSNR, f"fp16 1080p PSNR {p:.2f} dB"
+    finally:
+        model.close()
+
+
+@pytest.mark.parametrize("precision", ["fp16", "mixed"])
+def test_batch_tile_and_device_io_consistency(precision):
+    import torch
+    model = load_model(staged("adaptive_fp8.bin"), "cuda:0", precision)
+    try:
+        frames = make_frames(900, 3, 64, 96)
+        batch = model.upscale_u8(frames, 0)
+        for i in range(3):
+            np.testing.assert_array_equal(batch[i], model.upscale_u8(frames[i], 0))
+        dev = model.upscale_u8(torch.from_numpy(frames).cuda(), 0)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(dev.cpu().numpy(), batch)
+        tiled = model.upscale_u8(frames, 32)
+        assert psnr_u8(tiled, batch) >= 45
+    finally:
+        model.close()
+
+
+@pytest.mark.parametrize("precision", ["fp16", "mixed"])
+def test_coefficients_close_to_fp32(synthetic, precision):
+    state, artifact = synthetic
+    model = (Model.from_spyr8_bytes(artifact, "cuda:0", precision) if precision == "mixed"
+             else Model.from_folded_state(state, "cuda:0", "fp16"))
+    try:
+        x = np.random.default_rng(3).random((1, 3, 64, 96), dtype=np.float32)
+        ref = O.FoldedModel(state).predict_coefficients(x)
+        got = model.predict_coefficients(x)
+        err = np.abs(got - ref)
+        scale = np.abs(ref).max()
+        assert err.mean() <= 0.02 * scale and err.max() <= 0.25 * scale
+    finally:
+        model.close()
+
+
+def test_mixed_needs_fp8_scales():
+    with pytest.raises(Exception):
+        Model.from_folded_state(random_folded_state(1), "cuda:0", "mixed")
+
+
+def test_tensor_core_routes_report_and_launch_counts():
+    model = load_model(staged("adaptive_fp8.bin"), "cuda:0", "mixed")
+    try:
+        before = model.kernel_launches
+        model.upscale_u8(make_frame(5, 40, 40), 0)
+        assert model.kernel_launches - before == 9
+        assert "tcgen05" in model.report
+    finally:
+        model.close()
