@@ -27,7 +27,13 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
     require(!fp8 || m.has_fp8, "the mixed route needs the FP8 weights and scales of a SPYR8 artifact",
             AEISU_ERR_UNSUPPORTED);
     TcHostPack P;
-    const float* s = m.act_scales;
+    // Activation scales of the artifact times a power-of-two headroom.  E4M3 is a floating
+    // point format, so the factor leaves the rounding of every value below the old limit
+    // bit-identical and only stops values in [448 s, 448 hs) from saturating (the artifact was
+    // calibrated on natural images; high-contrast content exceeds its range in the later
+    // bottleneck layers).
+    float s[10];
+    for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * kFp8ActivationHeadroom;
     P.slope = m.layers[kProject].slope[0];
     P.inv_s1 = fp8 ? 1.0f / s[1] : 1.f;
     P.stencil = append_floats(P.floats, std::vector<float>(m.stencil, m.stencil + 24));

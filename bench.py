@@ -37,6 +37,7 @@ WORKLOADS = {
     # name: (frames per step, h, w, tile, precision, checkpoint, degradation, metric-config)
     "mixed720": (64, 720, 1280, 0, "mixed", "adaptive_fp8.bin", "area"),
     "fp16_1080": (1, 1080, 1920, 0, "fp16", "aeisu_area.pt", "area"),
+    "mixed1080": (1, 1080, 1920, 0, "mixed", "adaptive_fp8.bin", "area"),
     "tiled1080": (32, 1080, 1920, 256, "fp16", "aeisu_bicubic.pt", "bicubic"),
     "stream4k": (8, 2160, 3840, 0, "mixed", "adaptive_fp8.bin", "area"),
 }
