@@ -7,8 +7,13 @@
 //
 // Activations in HBM use a chunk-planar layout: tensor[r][y][chunk][x][16 bytes], one
 // 16-byte chunk = 8 f16 or 16 e4m3 channels.  A row segment of one chunk is contiguous,
-// so a warp loads/stores 512 B per instruction and the shared-memory copy of a row segment
-// is exactly the K-major no-swizzle operand layout of tc.cuh.
+// so a warp loads/stores 512 B per instruction, and a TMA box of one row window lands in
+// shared memory as exactly the K-major no-swizzle operand layout of tc.cuh.
+//
+// The 3x3 layers and the head are pipelined per CTA over a column strip of 128 pixels and a
+// band of rows: input rows stream through a ring of shared-memory slots (TMA, zero-filled
+// outside the grid = the convolution's zero padding), each row is loaded once per strip,
+// the MMAs of row y+1 run while the epilogue of row y drains the other TMEM buffer.
 //
 // Numerics follow the reference's mixed route (SrcPyrCudaRuntime.cu:4131-4873):
 //   project  f16 x f16, +bias, LeakyReLU -> f16 skip                 (K1, 2360-2584)
@@ -18,97 +23,22 @@
 //   refine   f16, +bias, act -> f16; tail f16 + f16(bias) -> coefficients (K11, Refine.cuh:334-557)
 //   head     clamp transfer, base + basis mix, 5x5 RGB apply          (K15, AdaptiveReconstruction.cuh:288-417)
 // The FP16 route uses the same kernels with f16 operands everywhere and plain biases.
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.h"
 #include "kernels.h"
-#include "tc.cuh"
+#include "tc_dev.cuh"
+#include "tmap.h"
 
 namespace aeisu {
 namespace {
 
 using namespace tc;
-
-constexpr int kM = 128;              // pixels per MMA tile (TMEM lanes)
-constexpr int kThreads = 128;        // one thread per tile pixel / TMEM lane
-constexpr int kErrTimeout = 1;
-
-__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
-__device__ __forceinline__ float leaky(float v, float s) { return v > 0.f ? v : v * s; }
-
-__device__ __forceinline__ float3 load_src(const SrcDesc& s, int f, int py, int px) {
-    const int y = clampi(py - s.pad_y, 0, s.H - 1), x = clampi(px - s.pad_x, 0, s.W - 1);
-    if (s.kind == 0) {
-        const uint8_t* p = static_cast<const uint8_t*>(s.ptr) + ((size_t(f) * s.H + y) * s.W + x) * 3;
-        return make_float3(__fdiv_rn(float(p[0]), 255.f), __fdiv_rn(float(p[1]), 255.f),
-                           __fdiv_rn(float(p[2]), 255.f));
-    }
-    const size_t plane = size_t(s.H) * s.W;
-    const float* p = static_cast<const float*>(s.ptr) + size_t(f) * 3 * plane + size_t(y) * s.W + x;
-    return make_float3(p[0], p[plane], p[2 * plane]);
-}
-
-__device__ __forceinline__ float mix3(float a, float b, float c, float w0, float w1, float w2) {
-    return __fadd_rn(__fadd_rn(__fmul_rn(a, w0), __fmul_rn(b, w1)), __fmul_rn(c, w2));
-}
-
-// Common per-CTA set-up: TMEM columns, one mbarrier for MMA completion.
-__device__ __forceinline__ void cta_setup(uint32_t* tmem_slot, uint64_t* bar, uint32_t ncols) {
-    if (threadIdx.x < 32) tmem_alloc(tmem_slot, ncols);
-    if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
-    }
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-}
-
-__device__ __forceinline__ void cta_teardown(uint32_t tmem, uint32_t ncols) {
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    if (threadIdx.x < 32) tmem_free(tmem, ncols);
-}
-
-// Issue-side helpers: thread 0 issues, commits; everyone waits (bounded) for completion.
-// Returns false on timeout (identical for the whole CTA).
-__device__ __forceinline__ bool mma_wait_all(uint64_t* bar, uint32_t& phase, int* err) {
-    bool ok = mbar_wait_bounded(bar, phase, err, kErrTimeout);
-    phase ^= 1u;
-    ok = !__syncthreads_or(!ok);
-    fence_after_sync();
-    return ok;
-}
-
-// Copy a byte image (weights in operand layout) from global to shared memory.
-__device__ __forceinline__ void copy_image(uint8_t* dst, const uint8_t* src, int bytes) {
-    const uint4* s = reinterpret_cast<const uint4*>(src);
-    uint4* d = reinterpret_cast<uint4*>(dst);
-    for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
-}
-
-// 32 f32 values -> 4 x 16 B chunks of f16.
-__device__ __forceinline__ void pack_f16x32(const float (&v)[32], uint4 (&o)[4]) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-        o[c] = make_uint4(pack_half2(v[8 * c], v[8 * c + 1]), pack_half2(v[8 * c + 2], v[8 * c + 3]),
-                          pack_half2(v[8 * c + 4], v[8 * c + 5]), pack_half2(v[8 * c + 6], v[8 * c + 7]));
-}
-// 32 f32 values -> 2 x 16 B chunks of e4m3.
-__device__ __forceinline__ void pack_e4m3x32(const float (&v)[32], uint4 (&o)[2]) {
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-        o[c] = make_uint4(e4m3x4(v[16 * c], v[16 * c + 1], v[16 * c + 2], v[16 * c + 3]),
-                          e4m3x4(v[16 * c + 4], v[16 * c + 5], v[16 * c + 6], v[16 * c + 7]),
-                          e4m3x4(v[16 * c + 8], v[16 * c + 9], v[16 * c + 10], v[16 * c + 11]),
-                          e4m3x4(v[16 * c + 12], v[16 * c + 13], v[16 * c + 14], v[16 * c + 15]));
-}
-
-__device__ __forceinline__ uint4* cp_at(void* base, int r, int H, int y, int nch, int c, int W, int x) {
-    return reinterpret_cast<uint4*>(static_cast<uint8_t*>(base) + ((((size_t)r * H + y) * nch + c) * W + x) * 16);
-}
+using namespace tcd;
 
 // ---- stage 1: feature analysis + unshuffle + project_540 ------------------------------------
 // A = 32 features (f16) of 128 packed pixels of one packed row; B = project weights [32][32].
@@ -123,13 +53,15 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
     __shared__ alignas(128) uint8_t sB[4 * 32 * 16];
     __shared__ float s_st[24];
     __shared__ float s_bias[32];
+    __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
     copy_image(sB, wimg, sizeof(sB));
     if (threadIdx.x < 24) s_st[threadIdx.x] = stencil[threadIdx.x];
     if (threadIdx.x < 32) s_bias[threadIdx.x] = bias[threadIdx.x];
+    fill_lut(s_lut);
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 32);
+    cta_setup(&s_tmem, &s_bar, 1, 32);
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
@@ -150,7 +82,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
                 const int ly = clampi(2 * qy - 1 + a, 0, rs.rh - 1), lx = clampi(2 * qxc - 1 + b, 0, rs.rw - 1);
-                const float3 c = load_src(src, reg.x, reg.y + ly, reg.z + lx);
+                const float3 c = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
                 g[a][b] = mix3(c.x, c.y, c.z, s_st[9], s_st[10], s_st[11]);
                 if (a >= 1 && a <= 2 && b >= 1 && b <= 2) rgb[a - 1][b - 1] = c;
             }
@@ -246,7 +178,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
     copy_image(sB, wimg, KCH * 64 * 16);
     if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 64);
+    cta_setup(&s_tmem, &s_bar, 1, 64);
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
@@ -259,7 +191,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
         const int x = seg * kM + t, xc = min(x, lw - 1);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(const_cast<void*>(encu), r, lh, y, KCH, c, lw, xc);
+            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(encu, r, lh, y, KCH, c, lw, xc);
         fence_async_smem();
         __syncthreads();
         if (t == 0) {
@@ -279,7 +211,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + h * 32, v);
 #pragma unroll
             for (int n = 0; n < 32; ++n) {
-                const float a = FP8 ? fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]) : v[n] + s_bias[h * 32 + n];
+                const float a = fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]);
                 v[n] = leaky(a, ep.slope) * (FP8 ? ep.out_inv : 1.f);
             }
             if (x < lw) {
@@ -318,7 +250,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
     copy_image(sB, wimg, KCH * 128 * 16);
     if (threadIdx.x < 128) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 128);
+    cta_setup(&s_tmem, &s_bar, 1, 128);
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
     const int lh = rs.rh / 4, lw = rs.rw / 4, ph = rs.rh / 2, pw = rs.rw / 2;
@@ -331,7 +263,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
         const int x = seg * kM + t, xc = min(x, lw - 1);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(const_cast<void*>(low), r, lh, y, KCH, c, lw, xc);
+            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(low, r, lh, y, KCH, c, lw, xc);
         fence_async_smem();
         __syncthreads();
         if (t == 0) {
@@ -353,13 +285,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
                 const int oy = 2 * y + (p >> 1), ox = 2 * x + (p & 1);
                 uint4 sk[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) sk[c] = *cp_at(const_cast<void*>(enc540), r, ph, oy, 4, c, pw, ox);
+                for (int c = 0; c < 4; ++c) sk[c] = *cp_at(enc540, r, ph, oy, 4, c, pw, ox);
                 const __half* skh = reinterpret_cast<const __half*>(sk);
 #pragma unroll
                 for (int n = 0; n < 32; ++n) {
                     const int col = p * 32 + n;
-                    float a = FP8 ? fmaf(v[n], s_scale[col], s_bias[col]) : v[n] + s_bias[col];
-                    a = leaky(a, ep.slope);
+                    float a = leaky(fmaf(v[n], s_scale[col], s_bias[col]), ep.slope);
                     if (FP8) {
                         // K8: requantise to e4m3 at 1/s7, dequantise, add the f16 skip
                         float q[4];
@@ -380,218 +311,281 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
     cta_teardown(tmem, 128);
 }
 
-// ---- grouped 3x3 bottleneck (2 groups of 32 -> 32) ----------------------------------------
-// Tile: ROWS output rows x 128 pixels.  Shared memory holds the ROWS+2 input rows of the
-// 130-pixel window (zero outside the grid), chunk-planar; tap (ky, kx) of output row o is the
-// operand starting at input row o+ky, pixel kx: no im2col copy.
-template <bool FP8, int ROWS>
-__global__ void __launch_bounds__(kThreads) k_tc_core(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
-                                                      const void* __restrict__ in, void* __restrict__ out, int* err) {
+// ---- pipelined 3x3 layers ------------------------------------------------------------------
+// Ring of NR input-row slots fed by TMA (thread 0), double-buffered TMEM accumulators.
+// Per output row y of a (strip, band) work item:
+//   wait MMA(y)  ->  TMA(row y+3) into the slot row y-1 used  ->  MMAs of row y+1 into the
+//   other TMEM buffer  ->  epilogue of row y  ->  barrier.
+// Every TMA issued is waited exactly once and every commit is waited exactly once, so the
+// mbarrier parities stay in step across work items.
+constexpr int kRing = 4;
+
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* p) {
+    const uint32_t a = smem_addr(p);
+    return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
+struct Ring {
+    uint8_t* base;
+    uint32_t base_addr;
+    int slot_bytes;
+    uint64_t* full;       // kRing barriers
+    uint32_t phase = 0;   // bit s: parity of the next completion of slot s (issuing thread)
+    uint32_t pending = 0; // bit s: a load into slot s has not been waited for
+    __device__ static int slot(int row) { return (row + 4 * kRing) % kRing; }
+    __device__ void load(const CUtensorMap* map, int x0, int row, int r) {
+        const int s = slot(row);
+        mbar_arrive_expect_tx(&full[s], uint32_t(slot_bytes));
+        tma_load_5d(base + s * slot_bytes, map, 0, x0 - 1, 0, row, r, &full[s]);
+        pending |= 1u << s;
+    }
+    __device__ bool wait(int row, int* err) {
+        const int s = slot(row);
+        const bool ok = mbar_wait_bounded(&full[s], (phase >> s) & 1u, err, kErrTimeout);
+        if (ok) {
+            phase ^= 1u << s;
+            pending &= ~(1u << s);
+        }
+        return ok;
+    }
+    // Abort path: wait (bounded) for loads still in flight before the CTA exits.
+    __device__ void drain(int* err) {
+        for (int s = 0; s < kRing; ++s)
+            if (pending & (1u << s)) {
+                mbar_wait_bounded(&full[s], (phase >> s) & 1u, err, kErrTimeout, 200000000LL);
+                phase ^= 1u << s;
+            }
+        pending = 0;
+    }
+    __device__ uint32_t addr(int row) const { return base_addr + slot(row) * slot_bytes; }
+};
+
+// Grouped (2 x 32->32) 3x3 bottleneck layer.
+template <bool FP8>
+__global__ void __launch_bounds__(kThreads) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+                                                      const uint8_t* __restrict__ wimg, EpiParams ep,
+                                                      void* __restrict__ out, int band, int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
     constexpr int CPG = ICH / 2;              // chunks per group
-    constexpr int WIN = kM + 2;               // window pixels
-    constexpr int LBO = WIN * 16;
+    constexpr int WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
     constexpr int BG = 9 * CPG * 32 * 16;     // bytes of one group's weights
-    constexpr uint32_t NCOL = ROWS * 64 <= 32 ? 32 : (ROWS * 64 <= 64 ? 64 : (ROWS * 64 <= 128 ? 128 : 256));
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* sA = smem;                                   // (ROWS+2) x ICH x WIN x 16
-    uint8_t* sB = smem + (ROWS + 2) * ICH * LBO;          // 2 groups
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
+    uint8_t* sB = smem + kRing * SLOT;
     float* s_scale = reinterpret_cast<float*>(sB + 2 * BG);
     float* s_bias = s_scale + 64;
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar;
+    __shared__ alignas(8) uint64_t s_bar[kRing + 2];   // ring slots, then MMA-done per TMEM buffer
     copy_image(sB, wimg, 2 * BG);
     if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, NCOL);
+    cta_setup(&s_tmem, s_bar, kRing + 2, 128);
     const uint32_t tmem = s_tmem;
-    uint32_t phase = 0;
+    Ring ring{smem, smem_addr(smem), SLOT, s_bar};
+    uint32_t mma_phase = 0, mma_pend = 0;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
-    const int nseg = (lw + kM - 1) / kM, nrow = (lh + ROWS - 1) / ROWS;
-    const long long ntiles = (long long)rs.R * nrow * nseg;
+    const int nstrip = (lw + kM - 1) / kM, nband = (lh + band - 1) / band;
+    const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5;
-    const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int seg = int(tile % nseg), yb = int((tile / nseg) % nrow), r = int(tile / ((long long)nseg * nrow));
-        const int y0 = yb * ROWS, x0 = seg * kM;
-        for (int i = t; i < (ROWS + 2) * ICH * WIN; i += kThreads) {
-            const int p = i % WIN, c = (i / WIN) % ICH, row = i / (WIN * ICH);
-            const int y = y0 - 1 + row, x = x0 - 1 + p;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (y >= 0 && y < lh && x >= 0 && x < lw) v = *cp_at(const_cast<void*>(in), r, lh, y, ICH, c, lw, x);
-            *reinterpret_cast<uint4*>(sA + i * 16) = v;
-        }
-        fence_async_smem();
-        __syncthreads();
-        if (t == 0) {
-            fence_after_sync();
-            constexpr uint32_t idesc = idesc_m128(32);
-            for (int o = 0; o < ROWS; ++o)
+    const uint32_t b0 = smem_addr(sB);
+    constexpr uint32_t idesc = idesc_m128(32);
+    auto issue = [&](int y, int buf) {   // MMAs of output row y into TMEM buffer buf
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    int step = 0;
+        for (int g = 0; g < 2; ++g) {
+            int step = 0;
 #pragma unroll
-                    for (int tap = 0; tap < 9; ++tap) {
-                        const int ky = tap / 3, kx = tap % 3;
+            for (int ky = 0; ky < 3; ++ky) {
+                const uint32_t row = ring.addr(y - 1 + ky);
 #pragma unroll
-                        for (int k = 0; k < CPG / 2; ++k, ++step) {
-                            const uint32_t aa = a0 + ((o + ky) * ICH + g * CPG + 2 * k) * LBO + kx * 16;
-                            const uint32_t bb = b0 + g * BG + (tap * CPG + 2 * k) * 32 * 16;
-                            const uint64_t a = sdesc(aa, LBO, 128), b = sdesc(bb, 32 * 16, 128);
-                            const uint32_t d = tmem + o * 64 + g * 32;
-                            if (FP8) mma_e4m3(d, a, b, idesc, step > 0); else mma_f16(d, a, b, idesc, step > 0);
-                        }
+                for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                    for (int k = 0; k < CPG / 2; ++k, ++step) {
+                        const uint64_t a = sdesc(row + (g * CPG + 2 * k) * LBO + kx * 16, LBO, 128);
+                        const uint64_t b = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * k) * 32 * 16, 32 * 16, 128);
+                        const uint32_t d = tmem + buf * 64 + g * 32;
+                        if (FP8) mma_e4m3(d, a, b, idesc, step > 0); else mma_f16(d, a, b, idesc, step > 0);
                     }
-                }
-            commit(&s_bar);
+            }
         }
-        if (!mma_wait_all(&s_bar, phase, err)) break;
-        const int x = x0 + t;
-#pragma unroll 1
-        for (int o = 0; o < ROWS; ++o) {
-            const int y = y0 + o;
+        commit(&s_bar[kRing + buf]);
+        mma_pend |= 1u << buf;
+    };
+    bool ok = true;
+    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const StripBand sb = strip_band(item, nstrip, nband, band, lh);
+        if (t == 0) {
+            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) ring.load(&tin, sb.x0, row, sb.r);
+            for (int row = sb.y0 - 1; row <= sb.y0 + 1 && ok; ++row) ok = ring.wait(row, err);
+            fence_after_sync();
+            if (ok) issue(sb.y0, 0);
+        }
+        for (int y = sb.y0; y < sb.y1; ++y) {
+            const int buf = (y - sb.y0) & 1;
+            bool good = mbar_wait_bounded(&s_bar[kRing + buf], (mma_phase >> buf) & 1u, err, kErrTimeout);
+            if (good) {
+                mma_phase ^= 1u << buf;
+                mma_pend &= ~(1u << buf);
+            }
+            fence_after_sync();
+            if (t == 0 && good && ok) {
+                if (y + 3 <= sb.y1) ring.load(&tin, sb.x0, y + 3, sb.r);
+                if (y + 1 < sb.y1) {
+                    good = ring.wait(y + 2, err);
+                    if (good) issue(y + 1, buf ^ 1);
+                }
+            }
+            const int x = sb.x0 + t;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + o * 64 + h * 32, v);
+                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + buf * 64 + h * 32, v);
 #pragma unroll
-                for (int n = 0; n < 32; ++n) {
-                    const float a = FP8 ? fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]) : v[n] + s_bias[h * 32 + n];
-                    v[n] = leaky(a, ep.slope) * (FP8 ? ep.out_inv : 1.f);
-                }
-                if (y < lh && x < lw) {
+                for (int n = 0; n < 32; ++n)
+                    v[n] = leaky(fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
+                if (x < lw) {
                     if (FP8) {
                         uint4 q[2];
                         pack_e4m3x32(v, q);
-                        for (int c = 0; c < 2; ++c) *cp_at(out, r, lh, y, ICH, h * 2 + c, lw, x) = q[c];
+                        for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 2 + c, lw, x) = q[c];
                     } else {
                         uint4 q[4];
                         pack_f16x32(v, q);
-                        for (int c = 0; c < 4; ++c) *cp_at(out, r, lh, y, ICH, h * 4 + c, lw, x) = q[c];
+                        for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 4 + c, lw, x) = q[c];
                     }
                 }
             }
+            fence_before_sync();
+            if (__syncthreads_or(!(good && ok))) { ok = false; break; }
         }
-        fence_before_sync();
-        __syncthreads();
     }
-    cta_teardown(tmem, NCOL);
+    if (!ok && t == 0) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
+        ring.drain(err);
+        for (int b = 0; b < 2; ++b)
+            if (mma_pend & (1u << b))
+                mbar_wait_bounded(&s_bar[kRing + b], (mma_phase >> b) & 1u, err, kErrTimeout, 200000000LL);
+    }
+    cta_teardown(tmem, 128);
 }
 
-// ---- refine_540 (3x3 32->64) + metadata_head (1x1 64->64) ---------------------------------
-// Refine accumulates into TMEM, its LeakyReLU'd f16 output is written back to shared
-// memory as the A operand of the tail GEMM (never reaching HBM), and the tail epilogue
-// writes clamped f16 coefficients in the head's layout: meta[r][Y][2][X][8 f16] with
-// LR pixel (Y, X) = (2*qy + i, 2*qx + j) taking channels (2i + j)*16 .. +16.
-// Optionally also the raw float32 head output (NHWC, 64 channels) for coefficient queries.
-template <int ROWS>
-__global__ void __launch_bounds__(kThreads) k_tc_refine_tail(RegionSet rs, const uint8_t* __restrict__ wref,
-                                                             const uint8_t* __restrict__ wtail, const float* __restrict__ rbias,
+// refine_540 (3x3 32->64) + metadata_head (1x1 64->64), pipelined like k_tc_core.  The
+// refine output (LeakyReLU, f16) goes back to shared memory as the tail GEMM's A operand and
+// never reaches HBM.  The tail epilogue writes clamped f16 coefficients in the head's
+// layout meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
+// (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
+__global__ void __launch_bounds__(kThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+                                                             const uint8_t* __restrict__ wref,
+                                                             const uint8_t* __restrict__ wtail,
+                                                             const float* __restrict__ rbias,
                                                              const float* __restrict__ tbias, float slope,
-                                                             const void* __restrict__ dec, void* __restrict__ meta,
-                                                             float* __restrict__ raw, int* err) {
-    constexpr int ICH = 4, WIN = kM + 2, LBO = WIN * 16;
+                                                             void* __restrict__ meta, float* __restrict__ raw,
+                                                             int band, int* err) {
+    constexpr int ICH = 4, WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
     constexpr int BREF = 36 * 64 * 16, BTAIL = 8 * 64 * 16, A2 = 8 * kM * 16;
-    constexpr uint32_t NCOL = ROWS * 128 <= 128 ? 128 : (ROWS * 128 <= 256 ? 256 : 512);
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* sA = smem;                                  // (ROWS+2) x 4 x WIN x 16
-    uint8_t* sB = sA + (ROWS + 2) * ICH * LBO;           // refine weights
-    uint8_t* sT = sB + BREF;                             // tail weights
-    uint8_t* sA2 = sT + BTAIL;                           // ROWS x (8 x 128 x 16)
-    float* s_rb = reinterpret_cast<float*>(sA2 + ROWS * A2);
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
+    uint8_t* sB = smem + kRing * SLOT;   // refine weights
+    uint8_t* sT = sB + BREF;             // tail weights
+    uint8_t* sA2 = sT + BTAIL;           // tail operand (one row)
+    float* s_rb = reinterpret_cast<float*>(sA2 + A2);
     float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar;
+    __shared__ alignas(8) uint64_t s_bar[kRing + 3];   // ring, refine-done x2, tail-done
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
     if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, NCOL);
+    cta_setup(&s_tmem, s_bar, kRing + 3, 256);
     const uint32_t tmem = s_tmem;
-    uint32_t phase = 0;
+    Ring ring{smem, smem_addr(smem), SLOT, s_bar};
+    uint32_t mma_phase = 0, tail_phase = 0, mma_pend = 0;   // pend bits: refine buf 0/1, tail (bit 2)
     const int ph = rs.rh / 2, pw = rs.rw / 2;
-    const int nseg = (pw + kM - 1) / kM, nrow = (ph + ROWS - 1) / ROWS;
-    const long long ntiles = (long long)rs.R * nrow * nseg;
+    const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
+    const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5;
-    const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
+    const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
     constexpr uint32_t idesc = idesc_m128(64);
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int seg = int(tile % nseg), yb = int((tile / nseg) % nrow), r = int(tile / ((long long)nseg * nrow));
-        const int y0 = yb * ROWS, x0 = seg * kM;
-        for (int i = t; i < (ROWS + 2) * ICH * WIN; i += kThreads) {
-            const int p = i % WIN, c = (i / WIN) % ICH, row = i / (WIN * ICH);
-            const int y = y0 - 1 + row, x = x0 - 1 + p;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (y >= 0 && y < ph && x >= 0 && x < pw) v = *cp_at(const_cast<void*>(dec), r, ph, y, ICH, c, pw, x);
-            *reinterpret_cast<uint4*>(sA + i * 16) = v;
+    auto issue_refine = [&](int y, int buf) {
+        int step = 0;
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+            const uint32_t row = ring.addr(y - 1 + ky);
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int k = 0; k < 2; ++k, ++step)
+                    mma_f16(tmem + buf * 128, sdesc(row + 2 * k * LBO + kx * 16, LBO, 128),
+                            sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * k) * 64 * 16, 64 * 16, 128), idesc, step > 0);
         }
-        fence_async_smem();
-        __syncthreads();
+        commit(&s_bar[kRing + buf]);
+        mma_pend |= 1u << buf;
+    };
+    bool ok = true;
+    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const StripBand sb = strip_band(item, nstrip, nband, band, ph);
         if (t == 0) {
+            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) ring.load(&tin, sb.x0, row, sb.r);
+            for (int row = sb.y0 - 1; row <= sb.y0 + 1 && ok; ++row) ok = ring.wait(row, err);
             fence_after_sync();
-            for (int o = 0; o < ROWS; ++o) {
-                int step = 0;
-#pragma unroll
-                for (int tap = 0; tap < 9; ++tap) {
-                    const int ky = tap / 3, kx = tap % 3;
-#pragma unroll
-                    for (int k = 0; k < 2; ++k, ++step) {
-                        const uint32_t aa = a0 + ((o + ky) * ICH + 2 * k) * LBO + kx * 16;
-                        const uint32_t bb = b0 + (tap * 4 + 2 * k) * 64 * 16;
-                        mma_f16(tmem + o * 128, sdesc(aa, LBO, 128), sdesc(bb, 64 * 16, 128), idesc, step > 0);
-                    }
-                }
-            }
-            commit(&s_bar);
+            if (ok) issue_refine(sb.y0, 0);
         }
-        if (!mma_wait_all(&s_bar, phase, err)) break;
-        // refine epilogue -> tail operand in shared memory
-#pragma unroll 1
-        for (int o = 0; o < ROWS; ++o) {
+        for (int y = sb.y0; y < sb.y1; ++y) {
+            const int buf = (y - sb.y0) & 1;
+            bool good = mbar_wait_bounded(&s_bar[kRing + buf], (mma_phase >> buf) & 1u, err, kErrTimeout);
+            if (good) {
+                mma_phase ^= 1u << buf;
+                mma_pend &= ~(1u << buf);
+            }
+            fence_after_sync();
+            if (t == 0 && good && ok && y + 3 <= sb.y1) ring.load(&tin, sb.x0, y + 3, sb.r);
+            // refine epilogue -> tail operand
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + o * 128 + h * 32, v);
+                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + buf * 128 + h * 32, v);
 #pragma unroll
                 for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_rb[h * 32 + n], slope);
                 uint4 q[4];
                 pack_f16x32(v, q);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA2 + o * A2 + ((h * 4 + c) * kM + t) * 16) = q[c];
+                for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA2 + ((h * 4 + c) * kM + t) * 16) = q[c];
             }
-        }
-        fence_async_smem();
-        fence_before_sync();
-        __syncthreads();
-        if (t == 0) {
-            fence_after_sync();
-            for (int o = 0; o < ROWS; ++o)
+            fence_async_smem();
+            fence_before_sync();
+            __syncthreads();
+            if (t == 0 && good && ok) {
+                fence_after_sync();
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    mma_f16(tmem + o * 128 + 64, sdesc(a20 + o * A2 + k * 2 * kM * 16, kM * 16, 128),
+                    mma_f16(tmem + buf * 128 + 64, sdesc(a20 + k * 2 * kM * 16, kM * 16, 128),
                             sdesc(t0 + k * 2 * 64 * 16, 64 * 16, 128), idesc, k > 0);
-            commit(&s_bar);
-        }
-        if (!mma_wait_all(&s_bar, phase, err)) break;
-        const int x = x0 + t;
-#pragma unroll 1
-        for (int o = 0; o < ROWS; ++o) {
-            const int y = y0 + o;
+                commit(&s_bar[kRing + 2]);
+                mma_pend |= 4u;
+                if (y + 1 < sb.y1) {
+                    good = ring.wait(y + 2, err);
+                    if (good) issue_refine(y + 1, buf ^ 1);
+                }
+            }
+            const bool tail_ok = mbar_wait_bounded(&s_bar[kRing + 2], tail_phase, err, kErrTimeout);
+            if (tail_ok) {
+                tail_phase ^= 1u;
+                mma_pend &= ~4u;
+            }
+            fence_after_sync();
+            const int x = sb.x0 + t;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + o * 128 + 64 + h * 32, v);
-                if (y < ph && x < pw) {
+                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 64 + h * 32, v);
+                if (x < pw) {
 #pragma unroll
                     for (int n = 0; n < 32; ++n) v[n] += s_tb[h * 32 + n];
                     if (raw) {
-                        float* rp = raw + (((size_t)r * ph + y) * pw + x) * 64 + h * 32;
+                        float* rp = raw + (((size_t)sb.r * ph + y) * pw + x) * 64 + h * 32;
 #pragma unroll
                         for (int n = 0; n < 32; ++n) rp[n] = v[n];
                     }
-                    // two parities per half: channels (2i+j)*16 + k, transfer-clamped
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) {
+                    for (int n = 0; n < 32; ++n) {   // coefficient_clamp
                         const float m = fabsf(v[n]);
                         const float s = fminf(fmaf(0.05f, m - 2.f, 2.f), 2.5f);
                         v[n] = m <= 2.f ? v[n] : copysignf(s, v[n]);
@@ -603,137 +597,207 @@ __global__ void __launch_bounds__(kThreads) k_tc_refine_tail(RegionSet rs, const
                         const int parity = h * 2 + pp;
                         const int Y = 2 * y + (parity >> 1), X = 2 * x + (parity & 1);
 #pragma unroll
-                        for (int c = 0; c < 2; ++c) *cp_at(meta, r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
+                        for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
                     }
                 }
             }
+            fence_before_sync();
+            if (__syncthreads_or(!(good && ok && tail_ok))) { ok = false; break; }
         }
-        fence_before_sync();
-        __syncthreads();
     }
-    cta_teardown(tmem, NCOL);
+    if (!ok && t == 0) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
+        ring.drain(err);
+        for (int b = 0; b < 2; ++b)
+            if (mma_pend & (1u << b))
+                mbar_wait_bounded(&s_bar[kRing + b], (mma_phase >> b) & 1u, err, kErrTimeout, 200000000LL);
+        if (mma_pend & 4u) mbar_wait_bounded(&s_bar[kRing + 2], tail_phase, err, kErrTimeout, 200000000LL);
+    }
+    cta_teardown(tmem, 256);
 }
 
 // ---- reconstruction head -------------------------------------------------------------------
-// Tile: 128 LR pixels of one row of a region's core rectangle.  D[px][tap*4 + phase] =
-// sum_k c_k * basis_hi + sum_k c_k * basis_lo + 1 * base_hi + 1 * base_lo (three K=16 MMAs;
-// the FP32 bank is split into two f16 terms so the filters keep FP32-level accuracy).
-// Then each thread applies its 25x4 filter weights to the 5x5 RGB neighbourhood staged in
-// shared memory and writes its 2x2 output pixels.
+// Work item: a strip of 128 LR pixels of a region's core rectangle and a band of rows.  Per
+// row: D[px][tap*4 + phase] = sum_k c_k * basis_hi + sum_k c_k * basis_lo + base_hi + base_lo
+// (three K=16 MMAs; the FP32 bank is split in two f16 terms so the filters keep FP32-level
+// accuracy), then each thread applies its 25x4 weights to the 5x5 RGB neighbourhood.  The
+// source rows slide through a 6-row ring (each source row converted once per strip), the
+// next row's coefficients are prefetched with cp.async while the current row's epilogue runs,
+// and output rows are staged in shared memory and stored coalesced.
+constexpr int kHeadRing = 6;
+constexpr int kHeadTW = kM + 4;
+
 __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
                                                       const void* __restrict__ meta, const uint8_t* __restrict__ bimg,
-                                                      int* nonfinite, int* err) {
-    constexpr int BCH = 2 * 128 * 16;       // one B operand: 2 chunks x 128 rows
-    constexpr int TW = kM + 4;              // staged source columns
-    __shared__ alignas(128) uint8_t sA[2 * kM * 16];
+                                                      int band, int* nonfinite, int* err) {
+    constexpr int BCH = 2 * 128 * 16;   // one B operand: 2 chunks x 128 rows
+    __shared__ alignas(128) uint8_t sA[2][2 * kM * 16];
     __shared__ alignas(128) uint8_t sOnes[2 * kM * 16];
     __shared__ alignas(128) uint8_t sB[3 * BCH];
-    __shared__ float4 s_src[5][TW];
+    __shared__ float4 s_src[kHeadRing][kHeadTW];
+    __shared__ float s_out[2][3][2 * kM];
+    __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
     copy_image(sB, bimg, 3 * BCH);
     for (int i = threadIdx.x; i < 2 * kM; i += blockDim.x) {
-        const uint32_t one2 = 0x3C003C00u;  // f16 1.0, 1.0
+        const uint32_t one2 = 0x3C003C00u;   // f16 1.0, 1.0
         *reinterpret_cast<uint4*>(sOnes + i * 16) = (i < kM) ? make_uint4(one2, 0, 0, 0) : make_uint4(0, 0, 0, 0);
     }
+    fill_lut(s_lut);
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 128);
+    cta_setup(&s_tmem, &s_bar, 1, 128);
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
-    const int nseg = (rs.core_w + kM - 1) / kM;
-    const long long per_region = (long long)rs.core_h * nseg;
-    const long long ntiles = (long long)rs.R * per_region;
     const int t = threadIdx.x, warp = t >> 5;
-    const uint32_t a0 = smem_addr(sA), o0 = smem_addr(sOnes), b0 = smem_addr(sB);
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int r = int(tile / per_region);
-        const int cy = int((tile % per_region) / nseg), seg = int(tile % nseg);
+    const int nstrip = (rs.core_w + kM - 1) / kM, nband = (rs.core_h + band - 1) / band;
+    const long long items = (long long)rs.R * nstrip * nband;
+    const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB);
+    constexpr uint32_t idesc = idesc_m128(128);
+    bool ok = true;
+    bool pend = false;   // thread 0: an MMA round was committed and not yet waited for
+
+    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const int r = int(item / ((long long)nstrip * nband));
+        const int bi = int((item / nstrip) % nband), si = int(item % nstrip);
         const int4 core = rs.cores[r];
-        const int y = core.x + cy, x0 = core.y + seg * kM;
-        if (y >= core.z || x0 >= core.w) continue;   // uniform across the CTA
+        const int y0 = core.x + bi * band, x0 = core.y + si * kM;
+        if (y0 >= core.z || x0 >= core.w) continue;            // uniform across the CTA
+        const int y1 = min(y0 + band, core.z), xe = min(x0 + kM, core.w);
         const int4 reg = rs.regions[r];
-        const int x = x0 + t, xc = min(x, rs.rw - 1);
-        // coefficients (already clamped, f16) -> A
+        const int xc = min(x0 + t, rs.rw - 1);
+        // source row `row` (region-local) -> ring slot, converted to float RGB
+        auto src_row = [&](int row, int col) {
+            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(x0 - 2 + col, 0, rs.rw - 1);
+            const float3 s = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
+            return make_float4(s.x, s.y, s.z, 0.f);
+        };
+        auto slot = [](int row) { return (row + 4 * kHeadRing) % kHeadRing; };
+        auto coef = [&](int y, int b) {   // cp.async the clamped f16 coefficients of row y
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(const_cast<void*>(meta), r, rs.rh, y, 2, c, rs.rw, xc);
-        // 5 x (128+4) RGB neighbourhood, replicate-clamped to the region then to the frame
-        for (int i = t; i < 5 * TW; i += kThreads) {
-            const int row = i / TW, col = i % TW;
-            const int ly = clampi(y - 2 + row, 0, rs.rh - 1), lx = clampi(x0 - 2 + col, 0, rs.rw - 1);
-            const float3 s = load_src(src, reg.x, reg.y + ly, reg.z + lx);
-            s_src[row][col] = make_float4(s.x, s.y, s.z, 0.f);
-        }
+            for (int c = 0; c < 2; ++c)
+                cp_async16(&sA[b][(c * kM + t) * 16], cp_at(meta, r, rs.rh, y, 2, c, rs.rw, xc));
+            cp_async_commit();
+        };
+        // prologue: source rows y0-2 .. y0+2, coefficients of y0, MMA(y0)
+        for (int row = y0 - 2; row <= y0 + 2; ++row)
+            for (int col = t; col < kHeadTW; col += kThreads) s_src[slot(row)][col] = src_row(row, col);
+        coef(y0, 0);
+        cp_async_wait_all();
         fence_async_smem();
+        fence_before_sync();
         __syncthreads();
         if (t == 0) {
             fence_after_sync();
-            constexpr uint32_t idesc = idesc_m128(128);
-            const uint64_t a = sdesc(a0, kM * 16, 128), ones = sdesc(o0, kM * 16, 128);
+            const uint64_t a = sdesc(smem_addr(sA[0]), kM * 16, 128);
             mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
             mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
-            mma_f16(tmem, ones, sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
+            mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
             commit(&s_bar);
+            pend = true;
         }
-        if (!mma_wait_all(&s_bar, phase, err)) break;
-        float acc[4][3] = {};
+        for (int y = y0; y < y1; ++y) {
+            const int b = (y - y0) & 1;
+            // prefetch: next row's coefficients (async) and source row y+3 (registers)
+            if (y + 1 < y1) coef(y + 1, b ^ 1);
+            float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f), pre1 = pre0;
+            const bool pre = y + 3 <= y1 + 1;
+            if (pre) {
+                pre0 = src_row(y + 3, t);
+                if (t + kThreads < kHeadTW) pre1 = src_row(y + 3, t + kThreads);
+            }
+            ok = mbar_wait_bounded(&s_bar, phase, err, kErrTimeout);
+            if (ok) {
+                phase ^= 1u;
+                pend = false;
+            }
+            fence_after_sync();
+            // epilogue: apply the 25 x 4 filter weights of this pixel
+            float acc[4][3] = {};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float w[32];
-            tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + q * 32, w);
+            for (int q = 0; q < 4; ++q) {
+                float w[32];
+                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + q * 32, w);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int tap = q * 8 + j;
-                if (tap < 25) {
-                    const int ty = tap / 5, tx = tap % 5;
-                    const float4 s = s_src[ty][t + tx];
+                for (int j = 0; j < 8; ++j) {
+                    const int tap = q * 8 + j;
+                    if (tap < 25) {
+                        const float4 s = s_src[slot(y - 2 + tap / 5)][t + tap % 5];
 #pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        acc[p][0] = fmaf(s.x, w[j * 4 + p], acc[p][0]);
-                        acc[p][1] = fmaf(s.y, w[j * 4 + p], acc[p][1]);
-                        acc[p][2] = fmaf(s.z, w[j * 4 + p], acc[p][2]);
+                        for (int p = 0; p < 4; ++p) {
+                            acc[p][0] = fmaf(s.x, w[j * 4 + p], acc[p][0]);
+                            acc[p][1] = fmaf(s.y, w[j * 4 + p], acc[p][1]);
+                            acc[p][2] = fmaf(s.z, w[j * 4 + p], acc[p][2]);
+                        }
                     }
                 }
             }
-        }
-        if (x < core.w) {
             bool bad = false;
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const int oy = 2 * (reg.y + y - dst.pad_y) + (p >> 1), ox = 2 * (reg.z + x - dst.pad_x) + (p & 1);
+            for (int p = 0; p < 4; ++p)
 #pragma unroll
                 for (int ch = 0; ch < 3; ++ch) {
-                    const float v = acc[p][ch];
-                    bad |= !isfinite(v);
-                    if (dst.kind == 1) {
-                        static_cast<float*>(dst.ptr)[((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox] = v;
-                    } else {
-                        const float cl = fminf(fmaxf(v, 0.f), 1.f);
-                        static_cast<uint8_t*>(dst.ptr)[((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3 + ch] =
-                            uint8_t(floorf(__fadd_rn(__fmul_rn(cl, 255.f), 0.5f)));
+                    bad |= !isfinite(acc[p][ch]) && (x0 + t < xe);
+                    s_out[p >> 1][ch][2 * t + (p & 1)] = acc[p][ch];
+                }
+            if (bad) atomicOr(nonfinite, 1);
+            if (pre) {
+                s_src[slot(y + 3)][t] = pre0;
+                if (t + kThreads < kHeadTW) s_src[slot(y + 3)][t + kThreads] = pre1;
+            }
+            cp_async_wait_all();
+            fence_async_smem();
+            fence_before_sync();
+            if (__syncthreads_or(!ok)) {
+                ok = false;
+                break;
+            }
+            if (t == 0 && y + 1 < y1) {
+                fence_after_sync();
+                const uint64_t a = sdesc(smem_addr(sA[b ^ 1]), kM * 16, 128);
+                mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
+                mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
+                mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
+                commit(&s_bar);
+                pend = true;
+            }
+            // coalesced stores of the two staged output rows
+            const int n = 2 * (xe - x0);
+            const int ox0 = 2 * (reg.z + x0 - dst.pad_x);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int oy = 2 * (reg.y + y - dst.pad_y) + i;
+                if (dst.kind == 1) {
+                    for (int ch = 0; ch < 3; ++ch) {
+                        float* row = static_cast<float*>(dst.ptr) + ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox0;
+                        for (int k = t; k < n; k += kThreads) row[k] = s_out[i][ch][k];
+                    }
+                } else {
+                    uint8_t* row = static_cast<uint8_t*>(dst.ptr) + ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox0) * 3;
+                    for (int k = t; k < 3 * n; k += kThreads) {
+                        const float v = fminf(fmaxf(s_out[i][k % 3][k / 3], 0.f), 1.f);
+                        row[k] = uint8_t(floorf(__fadd_rn(__fmul_rn(v, 255.f), 0.5f)));
                     }
                 }
             }
-            if (bad) atomicOr(nonfinite, 1);
+            __syncthreads();   // s_out is rewritten by the next row
         }
-        fence_before_sync();
-        __syncthreads();
+    }
+    if (!ok) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
+        cp_async_wait_all();
+        if (t == 0 && pend) mbar_wait_bounded(&s_bar, phase, err, kErrTimeout, 200000000LL);
     }
     cta_teardown(tmem, 128);
 }
 
-int g_sms = 0;
 int sm_count() {
-    if (!g_sms) {
-        int dev = 0;
-        AEISU_CUDA(cudaGetDevice(&dev));
-        AEISU_CUDA(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev));
-    }
-    return g_sms;
+    int dev = 0, n = 0;
+    AEISU_CUDA(cudaGetDevice(&dev));
+    AEISU_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    return n;
 }
 
-unsigned grid_for(long long tiles, int per_sm) {
-    const long long cap = (long long)sm_count() * per_sm;
+unsigned grid_for(long long tiles, int per_sm, int sms) {
+    const long long cap = (long long)sms * per_sm;
     return unsigned(tiles < cap ? (tiles > 0 ? tiles : 1) : cap);
 }
 
@@ -742,50 +806,63 @@ void smem_attr(K kernel, int bytes) {
     AEISU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
-constexpr int kCoreRows = 2;
-constexpr int kRefineRows = 2;
+// Rows per work item: enough items to fill every CTA slot, at most 32 rows.
+int pick_band(long long strips_x_regions, int rows, int slots) {
+    const long long per_slot = (strips_x_regions * rows + slots - 1) / slots;
+    return int(std::max<long long>(4, std::min<long long>(32, per_slot)));
+}
 
 }  // namespace
 
 void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
                           int* err, cudaStream_t s, int* launches, const StageMark& mark) {
+    const int sms = sm_count();
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
     const long long proj_tiles = (long long)rs.R * ph * ((pw + kM - 1) / kM);
     const long long low_tiles = (long long)rs.R * lh * ((lw + kM - 1) / kM);
-    const long long core_tiles = (long long)rs.R * ((lh + kCoreRows - 1) / kCoreRows) * ((lw + kM - 1) / kM);
-    const long long ref_tiles = (long long)rs.R * ((ph + kRefineRows - 1) / kRefineRows) * ((pw + kM - 1) / kM);
-    if (fp8) k_tc_project<true><<<grid_for(proj_tiles, 8), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, err);
-    else k_tc_project<false><<<grid_for(proj_tiles, 8), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, err);
+    if (fp8) k_tc_project<true><<<grid_for(proj_tiles, 8, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, err);
+    else k_tc_project<false><<<grid_for(proj_tiles, 8, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, err);
     mark(1);
     {
         const int kch = fp8 ? 8 : 16;
         const int bytes = kch * kM * 16 + kch * 64 * 16 + 2 * 64 * 4;
-        if (fp8) { smem_attr(k_tc_compress<true>, bytes); k_tc_compress<true><<<grid_for(low_tiles, 4), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
-        else { smem_attr(k_tc_compress<false>, bytes); k_tc_compress<false><<<grid_for(low_tiles, 4), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
+        if (fp8) { smem_attr(k_tc_compress<true>, bytes); k_tc_compress<true><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
+        else { smem_attr(k_tc_compress<false>, bytes); k_tc_compress<false><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
     }
     {
         const int ich = fp8 ? 4 : 8;
-        const int bytes = (kCoreRows + 2) * ich * (kM + 2) * 16 + 2 * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
+        const int per_sm = fp8 ? 4 : 2;
+        const int bytes = 1024 + kRing * ich * (kM + 2) * 16 + 2 * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
+        const long long strips = (long long)rs.R * ((lw + kM - 1) / kM);
+        const int band = pick_band(strips, lh, sms * per_sm);
+        const long long items = strips * ((lh + band - 1) / band);
+        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM + 2);
+        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM + 2);
         void* bufs[2] = {low_a, low_b};
-        if (fp8) smem_attr(k_tc_core<true, kCoreRows>, bytes); else smem_attr(k_tc_core<false, kCoreRows>, bytes);
+        const CUtensorMap* maps[2] = {&map_a, &map_b};
+        if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) k_tc_core<true, kCoreRows><<<grid_for(core_tiles, 3), kThreads, bytes, s>>>(rs, w.core[i], w.core_ep[i], bufs[i & 1], bufs[(i + 1) & 1], err);
-            else k_tc_core<false, kCoreRows><<<grid_for(core_tiles, 2), kThreads, bytes, s>>>(rs, w.core[i], w.core_ep[i], bufs[i & 1], bufs[(i + 1) & 1], err);
+            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else k_tc_core<false><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);
     {
         const int kch = fp8 ? 4 : 8;
         const int bytes = kch * kM * 16 + kch * 128 * 16 + 2 * 128 * 4;
-        if (fp8) { smem_attr(k_tc_expand<true>, bytes); k_tc_expand<true><<<grid_for(low_tiles, 4), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
-        else { smem_attr(k_tc_expand<false>, bytes); k_tc_expand<false><<<grid_for(low_tiles, 4), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
+        if (fp8) { smem_attr(k_tc_expand<true>, bytes); k_tc_expand<true><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
+        else { smem_attr(k_tc_expand<false>, bytes); k_tc_expand<false><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
     }
     mark(3);
     {
-        const int bytes = (kRefineRows + 2) * 4 * (kM + 2) * 16 + 36 * 64 * 16 + 8 * 64 * 16 + kRefineRows * 8 * kM * 16 + 2 * 64 * 4;
-        smem_attr(k_tc_refine_tail<kRefineRows>, bytes);
-        k_tc_refine_tail<kRefineRows><<<grid_for(ref_tiles, 2), kThreads, bytes, s>>>(rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, dec540, meta, raw_meta, err);
+        const int bytes = 1024 + kRing * 4 * (kM + 2) * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 8 * kM * 16 + 2 * 64 * 4;
+        const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
+        const int band = pick_band(strips, ph, sms * 2);
+        const long long items = strips * ((ph + band - 1) / band);
+        const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
+        smem_attr(k_tc_refine_tail, bytes);
+        k_tc_refine_tail<<<grid_for(items, 2, sms), kThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;
@@ -794,9 +871,12 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
 
 void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const void* meta,
                     const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, int* launches) {
-    const long long tiles = (long long)rs.R * rs.core_h * ((rs.core_w + kM - 1) / kM);
-    if (tiles == 0) return;
-    k_tc_head<<<grid_for(tiles, 4), kThreads, 0, s>>>(src, rs, dst, meta, head_img, nonfinite, err);
+    if ((long long)rs.R * rs.core_h * rs.core_w == 0) return;
+    const int sms = sm_count();
+    const long long strips = (long long)rs.R * ((rs.core_w + kM - 1) / kM);
+    const int band = pick_band(strips, rs.core_h, sms * 4);
+    const long long items = strips * ((rs.core_h + band - 1) / band);
+    k_tc_head<<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
     AEISU_CUDA(cudaGetLastError());
     *launches += 1;
 }

@@ -122,6 +122,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// ---- asynchronous copies ------------------------------------------------------------------
+
+// 16-byte global -> shared copy; `valid == false` writes zeros without reading global memory.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid = true) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(smem_addr(smem)), "l"(gmem), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// TMA: 5-D tiled tensor load into shared memory, completion counted on `bar` (transaction
+// bytes).  Coordinates are innermost first; out-of-range elements are written as zero.
+// (Plain load, no cluster multicast: the source is always this GPU's own memory.)
+__device__ __forceinline__ void tma_load_5d(void* smem, const void* tmap, int c0, int c1, int c2, int c3, int c4,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        :: "r"(smem_addr(smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_addr(bar))
+        : "memory");
+}
+
 // ---- numeric conversions ---------------------------------------------------------------
 
 // float -> OCP E4M3 code, round to nearest even, saturating to +-448 (as __nv_fp8_e4m3).

@@ -1,0 +1,122 @@
+// Device helpers shared by the tensor-core route kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace aeisu {
+namespace tcd {
+
+using namespace tc;
+
+constexpr int kM = 128;         // pixels per MMA tile (TMEM lanes)
+constexpr int kThreads = 128;   // one thread per tile pixel / TMEM lane
+constexpr int kErrTimeout = 1;  // device error code: an mbarrier wait expired
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+__device__ __forceinline__ float leaky(float v, float s) { return v > 0.f ? v : v * s; }
+
+// (a*w0 + b*w1) + c*w2 without contraction, as the reference's separate tensor ops.
+__device__ __forceinline__ float mix3(float a, float b, float c, float w0, float w1, float w2) {
+    return __fadd_rn(__fadd_rn(__fmul_rn(a, w0), __fmul_rn(b, w1)), __fmul_rn(c, w2));
+}
+
+// Source pixel at padded-grid coordinate (py, px) of frame f (replicate padding by clamping).
+// `lut` maps uint8 to value/255 (correctly rounded, as read_rgb's float division).
+__device__ __forceinline__ float3 load_src(const SrcDesc& s, int f, int py, int px, const float* lut) {
+    const int y = clampi(py - s.pad_y, 0, s.H - 1), x = clampi(px - s.pad_x, 0, s.W - 1);
+    if (s.kind == 0) {
+        const uint8_t* p = static_cast<const uint8_t*>(s.ptr) + ((size_t(f) * s.H + y) * s.W + x) * 3;
+        return make_float3(lut[p[0]], lut[p[1]], lut[p[2]]);
+    }
+    const size_t plane = size_t(s.H) * s.W;
+    const float* p = static_cast<const float*>(s.ptr) + size_t(f) * 3 * plane + size_t(y) * s.W + x;
+    return make_float3(p[0], p[plane], p[2 * plane]);
+}
+
+__device__ __forceinline__ void fill_lut(float* lut) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = __fdiv_rn(float(i), 255.f);
+}
+
+// Per-CTA set-up: TMEM columns (warp 0) and `nbar` mbarriers with arrival count 1.
+__device__ __forceinline__ void cta_setup(uint32_t* tmem_slot, uint64_t* bars, int nbar, uint32_t ncols) {
+    if (threadIdx.x < 32) tmem_alloc(tmem_slot, ncols);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nbar; ++i) mbar_init(bars + i, 1);
+        fence_mbar_init();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+}
+
+__device__ __forceinline__ void cta_teardown(uint32_t tmem, uint32_t ncols) {
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (threadIdx.x < 32) tmem_free(tmem, ncols);
+}
+
+// Everyone waits (bounded) for MMA completion; returns false on expiry, uniformly.  On the
+// abort path thread 0 (the issuer) gives the committed MMAs one more bounded wait so they
+// land before the caller releases TMEM.
+__device__ __forceinline__ bool mma_wait_all(uint64_t* bar, uint32_t& phase, int* err) {
+    const bool ok = mbar_wait_bounded(bar, phase, err, kErrTimeout);
+    if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0 && !ok) mbar_wait_bounded(bar, phase, err, kErrTimeout, 200000000LL);
+        return false;
+    }
+    phase ^= 1u;
+    fence_after_sync();
+    return true;
+}
+
+// Copy a byte image (weights in operand layout) from global to shared memory.
+__device__ __forceinline__ void copy_image(uint8_t* dst, const uint8_t* src, int bytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+}
+
+// 32 f32 values -> 4 x 16 B chunks of f16.
+__device__ __forceinline__ void pack_f16x32(const float (&v)[32], uint4 (&o)[4]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        o[c] = make_uint4(pack_half2(v[8 * c], v[8 * c + 1]), pack_half2(v[8 * c + 2], v[8 * c + 3]),
+                          pack_half2(v[8 * c + 4], v[8 * c + 5]), pack_half2(v[8 * c + 6], v[8 * c + 7]));
+}
+// 32 f32 values -> 2 x 16 B chunks of e4m3.
+__device__ __forceinline__ void pack_e4m3x32(const float (&v)[32], uint4 (&o)[2]) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+        o[c] = make_uint4(e4m3x4(v[16 * c], v[16 * c + 1], v[16 * c + 2], v[16 * c + 3]),
+                          e4m3x4(v[16 * c + 4], v[16 * c + 5], v[16 * c + 6], v[16 * c + 7]),
+                          e4m3x4(v[16 * c + 8], v[16 * c + 9], v[16 * c + 10], v[16 * c + 11]),
+                          e4m3x4(v[16 * c + 12], v[16 * c + 13], v[16 * c + 14], v[16 * c + 15]));
+}
+
+// Address of chunk c of pixel (y, x) of region r in a chunk-planar tensor [R][H][nch][W][16].
+__device__ __forceinline__ uint4* cp_at(const void* base, int r, int H, int y, int nch, int c, int W, int x) {
+    return reinterpret_cast<uint4*>(const_cast<uint8_t*>(static_cast<const uint8_t*>(base)) +
+                                    ((((size_t)r * H + y) * nch + c) * W + x) * 16);
+}
+
+// Work decomposition of the pipelined kernels: (region, column strip of 128, band of rows).
+struct StripBand {
+    int r, x0, y0, y1;
+};
+__device__ __forceinline__ StripBand strip_band(long long item, int nstrip, int nband, int band, int H) {
+    StripBand s;
+    s.r = int(item / ((long long)nstrip * nband));
+    const int b = int((item / nstrip) % nband);
+    s.x0 = int(item % nstrip) * kM;
+    s.y0 = b * band;
+    s.y1 = min(s.y0 + band, H);
+    return s;
+}
+
+}  // namespace tcd
+}  // namespace aeisu

@@ -1,0 +1,45 @@
+#include "tmap.h"
+
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.h"
+
+namespace aeisu {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) fail(AEISU_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+}  // namespace
+
+CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, int win) {
+    require(win >= 1 && win <= 256 && nch >= 1 && nch <= 256, "tensor map box out of range");
+    require((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base must be 16-byte aligned");
+    CUtensorMap map{};
+    const cuuint64_t dims[5] = {16, cuuint64_t(W), cuuint64_t(nch), cuuint64_t(H), cuuint64_t(R)};
+    const cuuint64_t strides[4] = {16, cuuint64_t(W) * 16, cuuint64_t(nch) * W * 16, cuuint64_t(H) * nch * W * 16};
+    const cuuint32_t box[5] = {16, cuuint32_t(win), cuuint32_t(nch), 1, 1};
+    const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+    const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void*>(base), dims, strides,
+                                   box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(AEISU_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    return map;
+}
+
+}  // namespace aeisu

@@ -1,0 +1,15 @@
+// Host-side TMA tensor maps for the chunk-planar activations.
+#pragma once
+
+#include <cuda.h>
+
+namespace aeisu {
+
+// A chunk-planar activation t[R][H][nch][W][16 B] seen as a 5-D byte tensor
+// {16, W, nch, H, R}; the box is one row window {16 B, win pixels, nch chunks, 1, 1}, which
+// lands in shared memory as [chunk][pixel][16 B] -- the K-major operand layout of tc.cuh.
+// Elements outside the tensor (x < 0, x >= W, y < 0, y >= H) are filled with zeros, which is
+// the zero padding of the 3x3 convolutions.
+CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, int win);
+
+}  // namespace aeisu
