@@ -41,16 +41,24 @@ using namespace tc;
 using namespace tcd;
 
 // ---- stage 1: feature analysis + unshuffle + project_540 ------------------------------------
-// A = 32 features (f16) of 128 packed pixels of one packed row; B = project weights [32][32].
+// Work item: a strip of 128 packed pixels and a band of packed rows.  The LR source rows the
+// strip needs (2qy-1 .. 2qy+2, 258 columns) slide through a 6-row ring in shared memory as
+// (r, g, b, luma) float4, so each source pixel is read and mixed once per strip; the next two
+// rows are loaded into registers while the current row's features and MMA run.
+// A = 32 features (f16) of the strip's packed pixels; B = project weights [32][32].
 // Writes enc540 (f16, 4 chunks, packed grid: the skip input of expand) and the compress
 // input at low resolution, unshuffled with K order phase*32 + c (f16: 16 chunks, e4m3: 8).
+constexpr int kProjRing = 6;
+constexpr int kProjTW = 2 * kM + 2;   // 258 LR columns per strip
+
 template <bool FP8>
 __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet rs, const float* __restrict__ stencil,
                                                          const uint8_t* __restrict__ wimg, const float* __restrict__ bias,
                                                          float slope, float inv_s1, void* __restrict__ enc540,
-                                                         void* __restrict__ encu, int* err) {
+                                                         void* __restrict__ encu, int band, int* err) {
     __shared__ alignas(128) uint8_t sA[4 * kM * 16];
     __shared__ alignas(128) uint8_t sB[4 * 32 * 16];
+    __shared__ float4 s_src[kProjRing][kProjTW];
     __shared__ float s_st[24];
     __shared__ float s_bias[32];
     __shared__ float s_lut[256];
@@ -65,97 +73,124 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
-    const int nseg = (pw + kM - 1) / kM;
-    const long long ntiles = (long long)rs.R * ph * nseg;
+    const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
+    const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5;
     const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int seg = int(tile % nseg), qy = int((tile / nseg) % ph), r = int(tile / ((long long)nseg * ph));
-        const int qx = seg * kM + t;
-        const int qxc = min(qx, pw - 1);
-        const int4 reg = rs.regions[r];
-        // --- features of packed pixel (qy, qxc), exactly as the FP32 route ---
-        float g[4][4];
-        float3 rgb[2][2];
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int ly = clampi(2 * qy - 1 + a, 0, rs.rh - 1), lx = clampi(2 * qxc - 1 + b, 0, rs.rw - 1);
-                const float3 c = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
-                g[a][b] = mix3(c.x, c.y, c.z, s_st[9], s_st[10], s_st[11]);
-                if (a >= 1 && a <= 2 && b >= 1 && b <= 2) rgb[a - 1][b - 1] = c;
-            }
-        float f[32];
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int p = i * 2 + j;
-                const float3 c = rgb[i][j];
-                f[0 * 4 + p] = mix3(c.x, c.y, c.z, s_st[0], s_st[1], s_st[2]);
-                f[1 * 4 + p] = mix3(c.x, c.y, c.z, s_st[3], s_st[4], s_st[5]);
-                f[2 * 4 + p] = mix3(c.x, c.y, c.z, s_st[6], s_st[7], s_st[8]);
-                f[3 * 4 + p] = g[i + 1][j + 1];
-                const float ul = g[i][j], uc = g[i][j + 1], ur = g[i][j + 2];
-                const float cl = g[i + 1][j], cr = g[i + 1][j + 2];
-                const float dl = g[i + 2][j], dc = g[i + 2][j + 1], dr = g[i + 2][j + 2];
-                const float hmid = __fsub_rn(cr, cl), vmid = __fsub_rn(dc, uc);
-                f[4 * 4 + p] = mix3(__fsub_rn(ur, ul), hmid, __fsub_rn(dr, dl), s_st[12], s_st[13], s_st[14]);
-                f[5 * 4 + p] = mix3(__fsub_rn(dl, ul), vmid, __fsub_rn(dr, ur), s_st[15], s_st[16], s_st[17]);
-                f[6 * 4 + p] = mix3(__fsub_rn(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
-                f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
-                                         __fmul_rn(hmid, s_st[23]));
-            }
-        uint4 fa[4];
-        pack_f16x32(f, fa);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = fa[c];
-        fence_async_smem();
+    constexpr int PER = (kProjTW + kThreads - 1) / kThreads;   // staged columns per thread (3)
+    auto slot = [](int row) { return (row + 4 * kProjRing) % kProjRing; };
+    bool ok = true;
+    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const StripBand sb = strip_band(item, nstrip, nband, band, ph);
+        const int4 reg = rs.regions[sb.r];
+        // source pixel (region-local LR row, strip column c) -> (r, g, b, luma)
+        auto fetch = [&](int row, int c) {
+            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(2 * sb.x0 - 1 + c, 0, rs.rw - 1);
+            const float3 v = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
+            return make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
+        };
+        for (int row = 2 * sb.y0 - 1; row <= 2 * sb.y0 + 2; ++row)
+            for (int c = t; c < kProjTW; c += kThreads) s_src[slot(row)][c] = fetch(row, c);
         __syncthreads();
-        if (t == 0) {
-            fence_after_sync();
-            constexpr uint32_t idesc = idesc_m128(32);
+        for (int qy = sb.y0; qy < sb.y1; ++qy) {
+            // prefetch the two source rows the next packed row adds
+            float4 pre[2][PER];
+            const bool more = qy + 1 < sb.y1;
+            if (more)
 #pragma unroll
-            for (int k = 0; k < 2; ++k)
-                mma_f16(tmem, sdesc(a0 + k * 2 * kM * 16, kM * 16, 128), sdesc(b0 + k * 2 * 32 * 16, 32 * 16, 128),
-                        idesc, k);
-            commit(&s_bar);
-        }
-        if (!mma_wait_all(&s_bar, phase, err)) break;
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(32 * warp) << 16), v);
+                for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_bias[n], slope);
-        uint4 o[4];
-        pack_f16x32(v, o);
-        if (qx < pw) {
+                    for (int j = 0; j < PER; ++j)
+                        if (t + j * kThreads < kProjTW) pre[k][j] = fetch(2 * qy + 3 + k, t + j * kThreads);
+            // features of packed pixel (qy, qx), exactly as the FP32 route
+            const int qx = sb.x0 + t, lc = 2 * (min(qx, pw - 1) - sb.x0);   // strip column of LR 2qx-1
+            float g[4][4];
+            float3 rgb[2][2];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) *cp_at(enc540, r, ph, qy, 4, c, pw, qx) = o[c];
-            const int p = (qy & 1) * 2 + (qx & 1);
-            if (FP8) {
-                // compress input: e4m3(f16 skip value * 1/s1), as K4's staging
-                float q[32];
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&o[c]);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        q[8 * c + 2 * e] = __low2float(h2[e]) * inv_s1;
-                        q[8 * c + 2 * e + 1] = __high2float(h2[e]) * inv_s1;
-                    }
+                for (int b = 0; b < 4; ++b) {
+                    const float4 v = s_src[slot(2 * qy - 1 + a)][lc + b];
+                    g[a][b] = v.w;
+                    if (a >= 1 && a <= 2 && b >= 1 && b <= 2) rgb[a - 1][b - 1] = make_float3(v.x, v.y, v.z);
                 }
-                uint4 o8[2];
-                pack_e4m3x32(q, o8);
+            float f[32];
 #pragma unroll
-                for (int c = 0; c < 2; ++c) *cp_at(encu, r, lh, qy >> 1, 8, p * 2 + c, lw, qx >> 1) = o8[c];
-            } else {
+            for (int i = 0; i < 2; ++i)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) *cp_at(encu, r, lh, qy >> 1, 16, p * 4 + c, lw, qx >> 1) = o[c];
+                for (int j = 0; j < 2; ++j) {
+                    const int p = i * 2 + j;
+                    const float3 c = rgb[i][j];
+                    f[0 * 4 + p] = mix3(c.x, c.y, c.z, s_st[0], s_st[1], s_st[2]);
+                    f[1 * 4 + p] = mix3(c.x, c.y, c.z, s_st[3], s_st[4], s_st[5]);
+                    f[2 * 4 + p] = mix3(c.x, c.y, c.z, s_st[6], s_st[7], s_st[8]);
+                    f[3 * 4 + p] = g[i + 1][j + 1];
+                    const float ul = g[i][j], uc = g[i][j + 1], ur = g[i][j + 2];
+                    const float cl = g[i + 1][j], cr = g[i + 1][j + 2];
+                    const float dl = g[i + 2][j], dc = g[i + 2][j + 1], dr = g[i + 2][j + 2];
+                    const float hmid = __fsub_rn(cr, cl), vmid = __fsub_rn(dc, uc);
+                    f[4 * 4 + p] = mix3(__fsub_rn(ur, ul), hmid, __fsub_rn(dr, dl), s_st[12], s_st[13], s_st[14]);
+                    f[5 * 4 + p] = mix3(__fsub_rn(dl, ul), vmid, __fsub_rn(dr, ur), s_st[15], s_st[16], s_st[17]);
+                    f[6 * 4 + p] = mix3(__fsub_rn(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
+                    f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
+                                             __fmul_rn(hmid, s_st[23]));
+                }
+            uint4 fa[4];
+            pack_f16x32(f, fa);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = fa[c];
+            fence_async_smem();
+            __syncthreads();
+            if (t == 0) {
+                fence_after_sync();
+                constexpr uint32_t idesc = idesc_m128(32);
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+                    mma_f16(tmem, sdesc(a0 + k * 2 * kM * 16, kM * 16, 128), sdesc(b0 + k * 2 * 32 * 16, 32 * 16, 128),
+                            idesc, k);
+                commit(&s_bar);
             }
+            if (more)
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+#pragma unroll
+                    for (int j = 0; j < PER; ++j)
+                        if (t + j * kThreads < kProjTW) s_src[slot(2 * qy + 3 + k)][t + j * kThreads] = pre[k][j];
+            if (!mma_wait_all(&s_bar, phase, err)) { ok = false; break; }
+            float v[32];
+            tmem_ld32(tmem + (uint32_t(32 * warp) << 16), v);
+#pragma unroll
+            for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_bias[n], slope);
+            uint4 o[4];
+            pack_f16x32(v, o);
+            if (qx < pw) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) *cp_at(enc540, sb.r, ph, qy, 4, c, pw, qx) = o[c];
+                const int p = (qy & 1) * 2 + (qx & 1);
+                if (FP8) {
+                    // compress input: e4m3(f16 skip value * 1/s1), as K4's staging
+                    float q[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const __half2* h2 = reinterpret_cast<const __half2*>(&o[c]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            q[8 * c + 2 * e] = __low2float(h2[e]) * inv_s1;
+                            q[8 * c + 2 * e + 1] = __high2float(h2[e]) * inv_s1;
+                        }
+                    }
+                    uint4 o8[2];
+                    pack_e4m3x32(q, o8);
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 8, p * 2 + c, lw, qx >> 1) = o8[c];
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 16, p * 4 + c, lw, qx >> 1) = o[c];
+                }
+            }
+            fence_before_sync();
+            __syncthreads();
         }
-        fence_before_sync();
-        __syncthreads();
     }
     cta_teardown(tmem, 32);
 }
@@ -634,7 +669,6 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
     __shared__ alignas(128) uint8_t sOnes[2 * kM * 16];
     __shared__ alignas(128) uint8_t sB[3 * BCH];
     __shared__ float4 s_src[kHeadRing][kHeadTW];
-    __shared__ float s_out[2][3][2 * kM];
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
@@ -731,15 +765,41 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                     }
                 }
             }
-            bool bad = false;
+            // each thread stores its own 2x2 output pixels: 6 bytes per output row as three
+            // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
+            // floats per channel plane
+            if (x0 + t < xe) {
+                bool bad = false;
 #pragma unroll
-            for (int p = 0; p < 4; ++p)
+                for (int p = 0; p < 4; ++p)
 #pragma unroll
-                for (int ch = 0; ch < 3; ++ch) {
-                    bad |= !isfinite(acc[p][ch]) && (x0 + t < xe);
-                    s_out[p >> 1][ch][2 * t + (p & 1)] = acc[p][ch];
+                    for (int ch = 0; ch < 3; ++ch) bad |= !isfinite(acc[p][ch]);
+                if (bad) atomicOr(nonfinite, 1);
+                const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int oy = 2 * (reg.y + y - dst.pad_y) + i;
+                    if (dst.kind == 1) {
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch)
+                            *reinterpret_cast<float2*>(static_cast<float*>(dst.ptr) +
+                                                       ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
+                                make_float2(acc[2 * i][ch], acc[2 * i + 1][ch]);
+                    } else {
+                        uint32_t q[6];
+#pragma unroll
+                        for (int k = 0; k < 6; ++k) {
+                            const float v = fminf(fmaxf(acc[2 * i + k / 3][k % 3], 0.f), 1.f);
+                            q[k] = uint32_t(floorf(__fadd_rn(__fmul_rn(v, 255.f), 0.5f)));
+                        }
+                        uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
+                                                                  ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
+                        o[0] = uint16_t(q[0] | (q[1] << 8));
+                        o[1] = uint16_t(q[2] | (q[3] << 8));
+                        o[2] = uint16_t(q[4] | (q[5] << 8));
+                    }
                 }
-            if (bad) atomicOr(nonfinite, 1);
+            }
             if (pre) {
                 s_src[slot(y + 3)][t] = pre0;
                 if (t + kThreads < kHeadTW) s_src[slot(y + 3)][t + kThreads] = pre1;
@@ -760,26 +820,6 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                 commit(&s_bar);
                 pend = true;
             }
-            // coalesced stores of the two staged output rows
-            const int n = 2 * (xe - x0);
-            const int ox0 = 2 * (reg.z + x0 - dst.pad_x);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int oy = 2 * (reg.y + y - dst.pad_y) + i;
-                if (dst.kind == 1) {
-                    for (int ch = 0; ch < 3; ++ch) {
-                        float* row = static_cast<float*>(dst.ptr) + ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox0;
-                        for (int k = t; k < n; k += kThreads) row[k] = s_out[i][ch][k];
-                    }
-                } else {
-                    uint8_t* row = static_cast<uint8_t*>(dst.ptr) + ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox0) * 3;
-                    for (int k = t; k < 3 * n; k += kThreads) {
-                        const float v = fminf(fmaxf(s_out[i][k % 3][k / 3], 0.f), 1.f);
-                        row[k] = uint8_t(floorf(__fadd_rn(__fmul_rn(v, 255.f), 0.5f)));
-                    }
-                }
-            }
-            __syncthreads();   // s_out is rewritten by the next row
         }
     }
     if (!ok) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
@@ -819,10 +859,14 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
                           int* err, cudaStream_t s, int* launches, const StageMark& mark) {
     const int sms = sm_count();
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
-    const long long proj_tiles = (long long)rs.R * ph * ((pw + kM - 1) / kM);
     const long long low_tiles = (long long)rs.R * lh * ((lw + kM - 1) / kM);
-    if (fp8) k_tc_project<true><<<grid_for(proj_tiles, 8, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, err);
-    else k_tc_project<false><<<grid_for(proj_tiles, 8, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, err);
+    {
+        const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
+        const int band = pick_band(strips, ph, sms * 4);
+        const long long items = strips * ((ph + band - 1) / band);
+        if (fp8) k_tc_project<true><<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err);
+        else k_tc_project<false><<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err);
+    }
     mark(1);
     {
         const int kch = fp8 ? 8 : 16;
