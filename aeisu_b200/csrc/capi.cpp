@@ -10,6 +10,7 @@
 #include "common.h"
 #include "engine.h"
 #include "model.h"
+#include "noalloc.h"
 
 struct aeisu_engine {
     std::unique_ptr<aeisu::Engine> engine;
@@ -107,6 +108,13 @@ int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, i
         aeisu::Call c{aeisu::Mode::Upscale, src, 0, dst, 0, n, h, w, tile, flags == AEISU_IO_HOST,
                       static_cast<cudaStream_t>(stream)};
         engine_of(handle).run(c);
+    });
+}
+
+int aeisu_upscale_u8_noalloc(aeisu_t* handle, const uint8_t* src, int n, int h, int w, uint8_t* dst,
+                             void* stream) {
+    return guarded([&] {
+        aeisu::upscale_u8_noalloc(engine_of(handle), src, n, h, w, dst, static_cast<cudaStream_t>(stream));
     });
 }
 

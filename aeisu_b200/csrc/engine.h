@@ -100,6 +100,24 @@ public:
     int precision() const { return precision_; }
     int device() const { return device_; }
 
+    // Device-resident weights and status flags, for entry points that run the kernels on
+    // buffers they do not take from this engine's workspace.
+    struct Resident {
+        const TcWeights* tc;
+        const uint8_t* head_img;
+        const float* stencil;
+        const F32Layer* f32;
+        const float* base;
+        const float* basis;
+        int* flags;             // [0] non-finite output, [1] kernel pipeline error
+        cudaStream_t stream;
+    };
+    Resident resident() const {
+        return {&tcw_, tc_bytes_.as<uint8_t>() + tc_head_off_, stencil_, f32_layers_, base_, basis_,
+                flag_.as<int>(), stream_};
+    }
+    void count_launches(int n) { launches_ += uint64_t(n); }
+
 private:
     struct DeviceGuard;
     void upload_weights();

@@ -1,0 +1,15 @@
+// Upscale into caller-provided device buffers using only the library's static scratch array
+// (no device or host allocation); see noalloc.cu for the limits and the sharing rules.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace aeisu {
+
+class Engine;
+
+void upscale_u8_noalloc(Engine& e, const uint8_t* src, int n, int h, int w, uint8_t* dst, cudaStream_t stream);
+
+}  // namespace aeisu

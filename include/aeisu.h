@@ -98,6 +98,21 @@ void aeisu_close(aeisu_t* handle);
 int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, int tile,
                      uint8_t* dst, unsigned flags, void* stream);
 
+/* Allocation-free variant of aeisu_upscale_u8 with device I/O and tile = 0 (no counterpart
+ * in the reference).  For hosts that must not allocate GPU memory when they submit a frame
+ * (a presentation loop that cannot stall on cudaMalloc, a process with a fixed memory budget,
+ * a caller that owns every buffer): all intermediate tensors live in one static device array
+ * of 64 MiB that every GPU loading the library holds until exit.  src/dst are device
+ * pointers (n frames of h x w x 3 uint8 in, 2h x 2w x 3 out); work is enqueued on `stream`
+ * (NULL: the handle's stream) and the call returns without waiting.  Frames needing more
+ * scratch than the array holds (about 0.8 Mpixel of padded input for the mixed route) are
+ * rejected with AEISU_ERR_INVALID_ARG.  The array is shared and keeps the previous call's
+ * contents: calls whose GPU work overlaps in time race and must be serialised.  The first
+ * call on a device looks up the array's address; make it before any stream capture.
+ * Non-finite outputs are reported by aeisu_synchronize. */
+int aeisu_upscale_u8_noalloc(aeisu_t* handle, const uint8_t* src, int n, int h, int w,
+                             uint8_t* dst, void* stream);
+
 /* Float parity path: n frames of float32 CHW (3 x h x w, values as read_rgb gives) ->
  * UNCLIPPED float32 CHW 3 x 2h x 2w (clip and the finite check are the caller's, as in
  * aeisu/runtime.py:100-103). */
