@@ -180,6 +180,7 @@ Engine::~Engine() {
     DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_,
                      &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
     for (DevBuf* b : all) b->reset();
+    table_cache_.clear();
     staging_.reset();
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
@@ -347,12 +348,23 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
             core_h = std::max(core_h, r.cy1 - r.cy0);
             core_w = std::max(core_w, r.cx1 - r.cx0);
         }
-        tables_.ensure(table.size() * sizeof(int4), s);
-        AEISU_CUDA(cudaMemcpyAsync(tables_.get(), table.data(), table.size() * sizeof(int4),
-                                   cudaMemcpyHostToDevice, s));
+        // Region tables are uploaded once per call geometry and kept on the device: an upload
+        // from pageable memory would wait for the stream to drain on every call.
+        const TableKey key{int(c.mode), c.n, c.h, c.w, c.tile, rh * 65536 + rw, int(first)};
+        auto it = table_cache_.find(key);
+        if (it == table_cache_.end()) {
+            if (table_cache_.size() >= 256) {
+                AEISU_CUDA(cudaStreamSynchronize(s));
+                table_cache_.clear();
+            }
+            auto buf = std::make_unique<DevBuf>();
+            buf->ensure(table.size() * sizeof(int4), s);
+            AEISU_CUDA(cudaMemcpy(buf->get(), table.data(), table.size() * sizeof(int4), cudaMemcpyHostToDevice));
+            it = table_cache_.emplace(key, std::move(buf)).first;
+        }
         RegionSet rs{};
-        rs.regions = tables_.as<int4>();
-        rs.cores = tables_.as<int4>() + R;
+        rs.regions = it->second->as<int4>();
+        rs.cores = it->second->as<int4>() + R;
         rs.R = R; rs.rh = rh; rs.rw = rw; rs.core_h = core_h; rs.core_w = core_w;
         enc540_.ensure(enc_b * R, s);
         dec540_.ensure(dec_b * R, s);

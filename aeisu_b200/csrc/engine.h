@@ -5,7 +5,9 @@
 
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cstdint>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -144,6 +146,10 @@ private:
     DevBuf tc_bytes_, tc_floats_;  // tensor-core routes: operand images, epilogue vectors
     TcWeights tcw_{};
     size_t tc_head_off_ = 0;
+
+    // region tables per call geometry (mode, n, h, w, tile, group shape, first region)
+    using TableKey = std::array<int, 7>;
+    std::map<TableKey, std::unique_ptr<DevBuf>> table_cache_;
 
     // workspace
     DevBuf src_, dst_, tables_, flag_;

@@ -89,19 +89,23 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             const float3 v = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
             return make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
         };
+        auto fetch_raw = [&](int row, int c) {
+            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(2 * sb.x0 - 1 + c, 0, rs.rw - 1);
+            return fetch_src_raw(src, reg.x, reg.y + ly, reg.z + lx);
+        };
         for (int row = 2 * sb.y0 - 1; row <= 2 * sb.y0 + 2; ++row)
             for (int c = t; c < kProjTW; c += kThreads) s_src[slot(row)][c] = fetch(row, c);
         __syncthreads();
         for (int qy = sb.y0; qy < sb.y1; ++qy) {
             // prefetch the two source rows the next packed row adds
-            float4 pre[2][PER];
+            uint3 pre[2][PER];
             const bool more = qy + 1 < sb.y1;
             if (more)
 #pragma unroll
                 for (int k = 0; k < 2; ++k)
 #pragma unroll
                     for (int j = 0; j < PER; ++j)
-                        if (t + j * kThreads < kProjTW) pre[k][j] = fetch(2 * qy + 3 + k, t + j * kThreads);
+                        if (t + j * kThreads < kProjTW) pre[k][j] = fetch_raw(2 * qy + 3 + k, t + j * kThreads);
             // features of packed pixel (qy, qx), exactly as the FP32 route
             const int qx = sb.x0 + t, lc = 2 * (min(qx, pw - 1) - sb.x0);   // strip column of LR 2qx-1
             float g[4][4];
@@ -155,7 +159,11 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                 for (int k = 0; k < 2; ++k)
 #pragma unroll
                     for (int j = 0; j < PER; ++j)
-                        if (t + j * kThreads < kProjTW) s_src[slot(2 * qy + 3 + k)][t + j * kThreads] = pre[k][j];
+                        if (t + j * kThreads < kProjTW) {
+                            const float3 v = finish_src(src, pre[k][j], s_lut);
+                            s_src[slot(2 * qy + 3 + k)][t + j * kThreads] =
+                                make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
+                        }
             if (!mma_wait_all(&s_bar, phase, err)) { ok = false; break; }
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16), v);
@@ -705,6 +713,10 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             const float3 s = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
             return make_float4(s.x, s.y, s.z, 0.f);
         };
+        auto src_raw = [&](int row, int col) {
+            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(x0 - 2 + col, 0, rs.rw - 1);
+            return fetch_src_raw(src, reg.x, reg.y + ly, reg.z + lx);
+        };
         auto slot = [](int row) { return (row + 4 * kHeadRing) % kHeadRing; };
         auto coef = [&](int y, int b) {   // cp.async the clamped f16 coefficients of row y
 #pragma unroll
@@ -733,11 +745,11 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             const int b = (y - y0) & 1;
             // prefetch: next row's coefficients (async) and source row y+3 (registers)
             if (y + 1 < y1) coef(y + 1, b ^ 1);
-            float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f), pre1 = pre0;
+            uint3 pre0 = make_uint3(0u, 0u, 0u), pre1 = pre0;
             const bool pre = y + 3 <= y1 + 1;
             if (pre) {
-                pre0 = src_row(y + 3, t);
-                if (t + kThreads < kHeadTW) pre1 = src_row(y + 3, t + kThreads);
+                pre0 = src_raw(y + 3, t);
+                if (t + kThreads < kHeadTW) pre1 = src_raw(y + 3, t + kThreads);
             }
             ok = mbar_wait_bounded(&s_bar, phase, err, kErrTimeout);
             if (ok) {
@@ -769,12 +781,13 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
             // floats per channel plane
             if (x0 + t < xe) {
-                bool bad = false;
+                // one test for all twelve values: a non-finite term makes the sum non-finite
+                float all = 0.f;
 #pragma unroll
                 for (int p = 0; p < 4; ++p)
 #pragma unroll
-                    for (int ch = 0; ch < 3; ++ch) bad |= !isfinite(acc[p][ch]);
-                if (bad) atomicOr(nonfinite, 1);
+                    for (int ch = 0; ch < 3; ++ch) all += acc[p][ch];
+                if (!isfinite(all)) atomicOr(nonfinite, 1);
                 const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -786,12 +799,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                                                        ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
                                 make_float2(acc[2 * i][ch], acc[2 * i + 1][ch]);
                     } else {
+                        // floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add
+                        // (runtime.py:24-25 in float32); round-down conversion is the floor
                         uint32_t q[6];
 #pragma unroll
-                        for (int k = 0; k < 6; ++k) {
-                            const float v = fminf(fmaxf(acc[2 * i + k / 3][k % 3], 0.f), 1.f);
-                            q[k] = uint32_t(floorf(__fadd_rn(__fmul_rn(v, 255.f), 0.5f)));
-                        }
+                        for (int k = 0; k < 6; ++k)
+                            q[k] = __float2uint_rd(__fadd_rn(__fmul_rn(__saturatef(acc[2 * i + k / 3][k % 3]), 255.f), 0.5f));
                         uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
                                                                   ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
                         o[0] = uint16_t(q[0] | (q[1] << 8));
@@ -801,8 +814,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                 }
             }
             if (pre) {
-                s_src[slot(y + 3)][t] = pre0;
-                if (t + kThreads < kHeadTW) s_src[slot(y + 3)][t + kThreads] = pre1;
+                const float3 a = finish_src(src, pre0, s_lut);
+                s_src[slot(y + 3)][t] = make_float4(a.x, a.y, a.z, 0.f);
+                if (t + kThreads < kHeadTW) {
+                    const float3 c = finish_src(src, pre1, s_lut);
+                    s_src[slot(y + 3)][t + kThreads] = make_float4(c.x, c.y, c.z, 0.f);
+                }
             }
             cp_async_wait_all();
             fence_async_smem();

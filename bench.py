@@ -81,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.device_index), "-lms", "200"],
+                 "-i", str(self.device_index), "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -157,6 +157,34 @@ def _cpu_threads():
         return os.cpu_count() or 1
 
 
+def measure_latency(dev, runs, distinct=16):
+    """p50/p99 device latency of one 1920x1080 -> 3840x2160 frame (FP16 route and mixed route),
+    input resident in HBM, cycling `distinct` seeded frames, CUDA events around each call."""
+    import torch
+    from aeisu_b200 import load_model
+    frames = torch.from_numpy(gen_frames(50_000, distinct, 1080, 1920, "area")).to(dev)
+    out = torch.empty((3840 * 2160 * 3,), dtype=torch.uint8, device=dev).view(2160, 3840, 3)
+    res = {}
+    for precision, ckpt in (("fp16", "aeisu_area.pt"), ("mixed", "adaptive_fp8.bin")):
+        model = load_model(WEIGHTS / ckpt, f"cuda:{dev.index}", precision)
+        stream = torch.cuda.Stream(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+        with torch.cuda.stream(stream):
+            for i in range(10):
+                model.upscale_u8(frames[i % distinct], 0, out=out)
+            for i in range(runs):
+                ev[i][0].record(stream)
+                model.upscale_u8(frames[i % distinct], 0, out=out)
+                ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        ms = sorted(a.elapsed_time(b) for a, b in ev)
+        res[precision] = {"p50_ms": ms[len(ms) // 2], "p99_ms": ms[min(len(ms) - 1, int(len(ms) * 0.99))]}
+        model.close()
+    res["config"] = (f"1920x1080 -> 3840x2160, batch 1, tile 0, {runs} runs over {distinct} distinct seeded frames, "
+                     "input in HBM, CUDA events per call on the launching stream")
+    return res
+
+
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
     """Time the reference algorithm's CPU implementation (the oracle port, FP32, all host
     threads) on a bounded sample of the workload's frames."""
@@ -209,13 +237,15 @@ def run_reference(args, wl):
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="mixed720")
     ap.add_argument("--precision", default=None, help="override the workload's precision")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--latency-runs", type=int, default=1000,
+                    help="1080p->4K single-frame latency runs (0 disables)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -294,6 +324,8 @@ def main():
     model.set_detailed_timing(False)
     stage_ms = {k: v / args.steps for k, v in stage_sum.items() if k.endswith("_ms")}
 
+    latency = measure_latency(dev, args.latency_runs) if (rank == 0 and args.latency_runs > 0) else None
+
     # end-to-end through the public API with pinned host buffers
     host_src = torch.from_numpy(frames).pin_memory()
     host_out = torch.empty((n, 2 * h, 2 * w, 3), dtype=torch.uint8).pin_memory()
@@ -348,6 +380,7 @@ def main():
                     "h2d_bytes_per_step": int(n * h * w * 3), "d2h_bytes_per_step": int(n * 4 * h * w * 3),
                     "steps": e2e_steps},
             "gpu_launches": int(launches),
+            "latency_1080p": latency,
             "clocks": clocks.summary(),
             "report": model.report,
         }
