@@ -403,12 +403,9 @@ struct Ring {
     __device__ uint32_t addr(int row) const { return base_addr + slot(row) * slot_bytes; }
 };
 
-// Grouped (2 x 32->32) 3x3 bottleneck layer.  256 threads: warpgroup g drains group g's 32
-// output channels of each row (both warpgroups read TMEM lanes 0..127).
-constexpr int kPipeThreads = 256;
-
+// Grouped (2 x 32->32) 3x3 bottleneck layer.
 template <bool FP8>
-__global__ void __launch_bounds__(kPipeThreads) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+__global__ void __launch_bounds__(kThreads) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                       const uint8_t* __restrict__ wimg, EpiParams ep,
                                                       void* __restrict__ out, int band, int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
@@ -432,7 +429,7 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_core(const __grid_constant_
     const int lh = rs.rh / 4, lw = rs.rw / 4;
     const int nstrip = (lw + kM - 1) / kM, nband = (lh + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
-    const int t = threadIdx.x, wg = t >> 7, px = t & (kM - 1), quad = (t >> 5) & 3;
+    const int t = threadIdx.x, warp = t >> 5;
     const uint32_t b0 = smem_addr(sB);
     constexpr uint32_t idesc = idesc_m128(32);
     auto issue = [&](int y, int buf) {   // MMAs of output row y into TMEM buffer buf
@@ -480,11 +477,13 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_core(const __grid_constant_
                     if (good) issue(y + 1, buf ^ 1);
                 }
             }
-            // warpgroup h drains output channels [32h, 32h+32) (group h) of this row
-            const int x = sb.x0 + px, h = wg;
-            {
-                float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * quad) << 16) + buf * 64 + h * 32, v);
+            const int x = sb.x0 + t;
+            float vv[2][32];
+            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 64, tmem + (uint32_t(32 * warp) << 16) + buf * 64 + 32,
+                        vv[0], vv[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float (&v)[32] = vv[h];
 #pragma unroll
                 for (int n = 0; n < 32; ++n)
                     v[n] = leaky(fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
@@ -518,7 +517,7 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_core(const __grid_constant_
 // never reaches HBM.  The tail epilogue writes clamped f16 coefficients in the head's
 // layout meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
-__global__ void __launch_bounds__(kPipeThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+__global__ void __launch_bounds__(kThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                              const uint8_t* __restrict__ wref,
                                                              const uint8_t* __restrict__ wtail,
                                                              const float* __restrict__ rbias,
@@ -547,7 +546,7 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_refine_tail(const __grid_co
     const int ph = rs.rh / 2, pw = rs.rw / 2;
     const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
-    const int t = threadIdx.x, wg = t >> 7, px = t & (kM - 1), quad = (t >> 5) & 3;
+    const int t = threadIdx.x, warp = t >> 5;
     const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
     constexpr uint32_t idesc = idesc_m128(64);
     auto issue_refine = [&](int y, int buf) {
@@ -583,17 +582,19 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_refine_tail(const __grid_co
             }
             fence_after_sync();
             if (t == 0 && good && ok && y + 3 <= sb.y1) ring.load(&tin, sb.x0, y + 3, sb.r);
-            // refine epilogue -> tail operand; warpgroup h drains refine channels [32h, 32h+32)
-            {
-                const int h = wg;
-                float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * quad) << 16) + buf * 128 + h * 32, v);
+            // refine epilogue -> tail operand
+            float vr[2][32];
+            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 128, tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 32,
+                        vr[0], vr[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float (&v)[32] = vr[h];
 #pragma unroll
                 for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_rb[h * 32 + n], slope);
                 uint4 q[4];
                 pack_f16x32(v, q);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA2 + ((h * 4 + c) * kM + px) * 16) = q[c];
+                for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA2 + ((h * 4 + c) * kM + t) * 16) = q[c];
             }
             fence_async_smem();
             fence_before_sync();
@@ -617,12 +618,13 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_refine_tail(const __grid_co
                 mma_pend &= ~4u;
             }
             fence_after_sync();
-            // warpgroup h drains tail channels [32h, 32h+32): parities 2h and 2h+1
-            const int x = sb.x0 + px;
-            {
-                const int h = wg;
-                float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * quad) << 16) + buf * 128 + 64 + h * 32, v);
+            const int x = sb.x0 + t;
+            float vt[2][32];
+            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 64,
+                        tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 96, vt[0], vt[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float (&v)[32] = vt[h];
                 if (x < pw) {
 #pragma unroll
                     for (int n = 0; n < 32; ++n) v[n] += s_tb[h * 32 + n];
@@ -667,17 +669,23 @@ __global__ void __launch_bounds__(kPipeThreads) k_tc_refine_tail(const __grid_co
 // row: D[px][tap*4 + phase] = sum_k c_k * basis_hi + sum_k c_k * basis_lo + base_hi + base_lo
 // (three K=16 MMAs; the FP32 bank is split in two f16 terms so the filters keep FP32-level
 // accuracy), then each thread applies its 25x4 weights to the 5x5 RGB neighbourhood.  The
-// source rows slide through a 6-row ring (each source row converted once per strip), the
-// next row's coefficients are prefetched with cp.async while the current row's epilogue runs,
-// and output rows are staged in shared memory and stored coalesced.
-constexpr int kHeadRing = 6;
+// source rows slide through an 8-row ring (each source row converted once per strip); the
+// next row's coefficients are prefetched with cp.async and its new source row is loaded into
+// registers while the current row computes.  Four CTAs share an SM, so one CTA's MMA and
+// TMEM waits hide behind the others' FMAs.
+constexpr int kHeadRing = 8;
 constexpr int kHeadTW = kM + 4;
-constexpr int kHeadThreads = 256;   // two warpgroups: warpgroup g computes output row 2y + g
 
-__global__ void __launch_bounds__(kHeadThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
-                                                          const void* __restrict__ meta,
-                                                          const uint8_t* __restrict__ bimg, int band, int* nonfinite,
-                                                          int* err) {
+// floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add (runtime.py:24-25 in
+// float32).  The sum lies in [0.5, 255.5]; adding 2^23 with round-down leaves floor(sum) in
+// the low mantissa bits, so byte 0 of the result is the output code.
+__device__ __forceinline__ uint32_t u8_code_bits(float v) {
+    return __float_as_uint(__fadd_rd(__fadd_rn(__fmul_rn(__saturatef(v), 255.f), 0.5f), 8388608.f));
+}
+
+__global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
+                                                      const void* __restrict__ meta, const uint8_t* __restrict__ bimg,
+                                                      int band, int* nonfinite, int* err) {
     constexpr int BCH = 2 * 128 * 16;   // one B operand: 2 chunks x 128 rows
     __shared__ alignas(128) uint8_t sA[2][2 * kM * 16];
     __shared__ alignas(128) uint8_t sOnes[2 * kM * 16];
@@ -696,15 +704,23 @@ __global__ void __launch_bounds__(kHeadThreads) k_tc_head(SrcDesc src, RegionSet
     cta_setup(&s_tmem, &s_bar, 1, 128);
     const uint32_t tmem = s_tmem;
     uint32_t phase = 0;
-    const int t = threadIdx.x, wg = t >> 7, px = t & (kM - 1), quad = (t >> 5) & 3;
+    const int t = threadIdx.x, warp = t >> 5;
     const int nstrip = (rs.core_w + kM - 1) / kM, nband = (rs.core_h + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB);
     constexpr uint32_t idesc = idesc_m128(128);
-    // TMEM address of this thread's lane, at the columns of its warpgroup's two phases
-    const uint32_t tcol = tmem + (uint32_t(32 * quad) << 16) + uint32_t(wg * 64);
+    const bool two = t + kThreads < kHeadTW;   // this thread stages a second window column
     bool ok = true;
     bool pend = false;   // thread 0: an MMA round was committed and not yet waited for
+    auto issue = [&](int b) {   // MMA round of the row whose coefficients sit in sA[b]
+        fence_after_sync();
+        const uint64_t a = sdesc(smem_addr(sA[b]), kM * 16, 128);
+        mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
+        mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
+        mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
+        commit(&s_bar);
+        pend = true;
+    };
 
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
         const int r = int(item / ((long long)nstrip * nband));
@@ -714,102 +730,120 @@ __global__ void __launch_bounds__(kHeadThreads) k_tc_head(SrcDesc src, RegionSet
         if (y0 >= core.z || x0 >= core.w) continue;            // uniform across the CTA
         const int y1 = min(y0 + band, core.z), xe = min(x0 + kM, core.w);
         const int4 reg = rs.regions[r];
-        const int xc = min(x0 + px, rs.rw - 1);
-        auto src_raw = [&](int row, int col) {
-            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(x0 - 2 + col, 0, rs.rw - 1);
-            return fetch_src_raw(src, reg.x, reg.y + ly, reg.z + lx);
-        };
-        auto slot = [](int row) { return (row + 4 * kHeadRing) % kHeadRing; };
-        auto coef = [&](int y, int b) {   // cp.async the clamped f16 coefficients of row y (warpgroup 0)
-            if (wg == 0) {
+        // source columns this thread stages (window columns t and t + 128), clamped once
+        int sx[2];
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    cp_async16(&sA[b][(c * kM + px) * 16], cp_at(meta, r, rs.rh, y, 2, c, rs.rw, xc));
+        for (int j = 0; j < 2; ++j)
+            sx[j] = clampi(reg.z + clampi(x0 - 2 + t + j * kThreads, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+        auto src_raw = [&](int row, int j) -> uint3 {
+            const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
+            if (src.kind == 0) {
+                const uint8_t* p = static_cast<const uint8_t*>(src.ptr) + ((size_t(reg.x) * src.H + sy) * src.W + sx[j]) * 3;
+                return make_uint3(uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16), 0u, 0u);
             }
+            const size_t plane = size_t(src.H) * src.W;
+            const float* p = static_cast<const float*>(src.ptr) + size_t(reg.x) * 3 * plane + size_t(sy) * src.W + sx[j];
+            return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
+        };
+        auto slot = [&](int row) { return (row - y0 + 2) & (kHeadRing - 1); };
+        auto put = [&](int row, int j, uint3 raw) {
+            const float3 v = finish_src(src, raw, s_lut);
+            s_src[slot(row)][t + j * kThreads] = make_float4(v.x, v.y, v.z, 0.f);
+        };
+        // coefficients of row y: meta[r][y][chunk][X][16 B], X = this thread's column
+        const uint8_t* cbase = static_cast<const uint8_t*>(meta) +
+                               ((size_t)r * rs.rh * 2 * rs.rw + min(x0 + t, rs.rw - 1)) * 16;
+        const size_t crow = size_t(2) * rs.rw * 16;
+        auto coef = [&](int y, int b) {
+            const uint8_t* g = cbase + size_t(y) * crow;
+            cp_async16(&sA[b][t * 16], g);
+            cp_async16(&sA[b][(kM + t) * 16], g + size_t(rs.rw) * 16);
             cp_async_commit();
         };
         // prologue: source rows y0-2 .. y0+2, coefficients of y0, MMA(y0)
-        for (int i = t; i < 5 * kHeadTW; i += kHeadThreads) {
-            const int row = y0 - 2 + i / kHeadTW, col = i % kHeadTW;
-            const float3 s = finish_src(src, src_raw(row, col), s_lut);
-            s_src[slot(row)][col] = make_float4(s.x, s.y, s.z, 0.f);
+        for (int row = y0 - 2; row <= y0 + 2; ++row) {
+            put(row, 0, src_raw(row, 0));
+            if (two) put(row, 1, src_raw(row, 1));
         }
         coef(y0, 0);
         cp_async_wait_all();
         fence_async_smem();
         fence_before_sync();
         __syncthreads();
-        if (t == 0) {
-            fence_after_sync();
-            const uint64_t a = sdesc(smem_addr(sA[0]), kM * 16, 128);
-            mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
-            mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
-            mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
-            commit(&s_bar);
-            pend = true;
-        }
+        if (t == 0) issue(0);
         for (int y = y0; y < y1; ++y) {
             const int b = (y - y0) & 1;
-            // prefetch: next row's coefficients (async) and source row y+3 (raw, into registers:
-            // 132 columns over 256 threads)
-            if (y + 1 < y1) coef(y + 1, b ^ 1);
-            const bool pre = y + 3 <= y1 + 1 && t < kHeadTW;
-            const uint3 raw = pre ? src_raw(y + 3, t) : make_uint3(0u, 0u, 0u);
+            // prefetch: next row's coefficients (async) and source row y+3 (registers)
+            const bool next = y + 1 < y1;
+            uint3 pre0 = make_uint3(0u, 0u, 0u), pre1 = pre0;
+            if (next) {
+                coef(y + 1, b ^ 1);
+                pre0 = src_raw(y + 3, 0);
+                if (two) pre1 = src_raw(y + 3, 1);
+            }
             ok = mbar_wait_bounded(&s_bar, phase, err, kErrTimeout);
             if (ok) {
                 phase ^= 1u;
                 pend = false;
             }
             fence_after_sync();
-            // epilogue: this warpgroup's two phases (output row 2y + wg), 25 taps each
-            float w0[32], w1[32];
-            tmem_ld32(tcol, w0);
-            tmem_ld32(tcol + 32, w1);
-            const float4* rows[5];
+            // epilogue: apply the 25 x 4 filter weights of this pixel
+            float acc[4][3] = {};
 #pragma unroll
-            for (int ty = 0; ty < 5; ++ty) rows[ty] = &s_src[slot(y - 2 + ty)][px];
-            float acc[2][3] = {};
+            for (int q = 0; q < 4; ++q) {
+                float w[32];
+                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + q * 32, w);
 #pragma unroll
-            for (int tap = 0; tap < 25; ++tap) {
-                const float4 s = rows[tap / 5][tap % 5];
-                acc[0][0] = fmaf(s.x, w0[tap], acc[0][0]);
-                acc[0][1] = fmaf(s.y, w0[tap], acc[0][1]);
-                acc[0][2] = fmaf(s.z, w0[tap], acc[0][2]);
-                acc[1][0] = fmaf(s.x, w1[tap], acc[1][0]);
-                acc[1][1] = fmaf(s.y, w1[tap], acc[1][1]);
-                acc[1][2] = fmaf(s.z, w1[tap], acc[1][2]);
-            }
-            // each thread stores its two output pixels of row 2y + wg: 6 bytes as three 16-bit
-            // words (2-byte aligned: the row offset is a multiple of 6), or two floats per plane
-            if (x0 + px < xe) {
-                // one test for all six values: a non-finite term makes the sum non-finite
-                const float all = acc[0][0] + acc[0][1] + acc[0][2] + acc[1][0] + acc[1][1] + acc[1][2];
-                if (!isfinite(all)) atomicOr(nonfinite, 1);
-                const int ox = 2 * (reg.z + x0 + px - dst.pad_x);
-                const int oy = 2 * (reg.y + y - dst.pad_y) + wg;
-                if (dst.kind == 1) {
+                for (int j = 0; j < 8; ++j) {
+                    const int tap = q * 8 + j;
+                    if (tap < 25) {
+                        const float4 s = s_src[slot(y - 2 + tap / 5)][t + tap % 5];
 #pragma unroll
-                    for (int ch = 0; ch < 3; ++ch)
-                        *reinterpret_cast<float2*>(static_cast<float*>(dst.ptr) +
-                                                   ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
-                            make_float2(acc[0][ch], acc[1][ch]);
-                } else {
-                    // floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add
-                    // (runtime.py:24-25 in float32); round-down conversion is the floor
-                    uint32_t q[6];
-#pragma unroll
-                    for (int k = 0; k < 6; ++k)
-                        q[k] = __float2uint_rd(__fadd_rn(__fmul_rn(__saturatef(acc[k / 3][k % 3]), 255.f), 0.5f));
-                    uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
-                                                              ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
-                    o[0] = uint16_t(q[0] | (q[1] << 8));
-                    o[1] = uint16_t(q[2] | (q[3] << 8));
-                    o[2] = uint16_t(q[4] | (q[5] << 8));
+                        for (int p = 0; p < 4; ++p) {
+                            acc[p][0] = fmaf(s.x, w[j * 4 + p], acc[p][0]);
+                            acc[p][1] = fmaf(s.y, w[j * 4 + p], acc[p][1]);
+                            acc[p][2] = fmaf(s.z, w[j * 4 + p], acc[p][2]);
+                        }
+                    }
                 }
             }
-            if (pre) {
-                const float3 a = finish_src(src, raw, s_lut);
-                s_src[slot(y + 3)][t] = make_float4(a.x, a.y, a.z, 0.f);
+            // each thread stores its own 2x2 output pixels: 6 bytes per output row as three
+            // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
+            // floats per channel plane
+            if (x0 + t < xe) {
+                // one test for all twelve values: a non-finite term makes the sum non-finite
+                float all = 0.f;
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                    for (int ch = 0; ch < 3; ++ch) all += acc[p][ch];
+                if (!isfinite(all)) atomicOr(nonfinite, 1);
+                const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int oy = 2 * (reg.y + y - dst.pad_y) + i;
+                    if (dst.kind == 1) {
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch)
+                            *reinterpret_cast<float2*>(static_cast<float*>(dst.ptr) +
+                                                       ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
+                                make_float2(acc[2 * i][ch], acc[2 * i + 1][ch]);
+                    } else {
+                        uint32_t q[6];
+#pragma unroll
+                        for (int k = 0; k < 6; ++k) q[k] = u8_code_bits(acc[2 * i + k / 3][k % 3]);
+                        uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
+                                                                  ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
+                        o[0] = uint16_t(__byte_perm(q[0], q[1], 0x0040));
+                        o[1] = uint16_t(__byte_perm(q[2], q[3], 0x0040));
+                        o[2] = uint16_t(__byte_perm(q[4], q[5], 0x0040));
+                    }
+                }
+            }
+            // source row y+3 into the ring (read after this row's barrier)
+            if (next) {
+                put(y + 3, 0, pre0);
+                if (two) put(y + 3, 1, pre1);
             }
             cp_async_wait_all();
             fence_async_smem();
@@ -818,15 +852,7 @@ __global__ void __launch_bounds__(kHeadThreads) k_tc_head(SrcDesc src, RegionSet
                 ok = false;
                 break;
             }
-            if (t == 0 && y + 1 < y1) {
-                fence_after_sync();
-                const uint64_t a = sdesc(smem_addr(sA[b ^ 1]), kM * 16, 128);
-                mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
-                mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
-                mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
-                commit(&s_bar);
-                pend = true;
-            }
+            if (t == 0 && next) issue(b ^ 1);
         }
     }
     if (!ok) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
@@ -857,6 +883,19 @@ void smem_attr(K kernel, int bytes) {
 int pick_band(long long strips_x_regions, int rows, int slots) {
     const long long per_slot = (strips_x_regions * rows + slots - 1) / slots;
     return int(std::max<long long>(4, std::min<long long>(32, per_slot)));
+}
+
+// Rows per head work item: the band that minimises the rows the busiest CTA slot runs
+// (items are dealt round-robin), counting about four rows of set-up per item.
+int pick_band_balanced(long long strips_x_regions, int rows, int slots) {
+    int best = 4;
+    long long best_cost = -1;
+    for (int band = 4; band <= std::max(4, rows); ++band) {
+        const long long items = strips_x_regions * ((rows + band - 1) / band);
+        const long long cost = (items + slots - 1) / slots * (band + 4);
+        if (best_cost < 0 || cost < best_cost) { best = band; best_cost = cost; }
+    }
+    return best;
 }
 
 }  // namespace
@@ -894,8 +933,8 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const CUtensorMap* maps[2] = {&map_a, &map_b};
         if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kPipeThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else k_tc_core<false><<<grid_for(items, per_sm, sms), kPipeThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else k_tc_core<false><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);
@@ -913,7 +952,7 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const long long items = strips * ((ph + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
         smem_attr(k_tc_refine_tail, bytes);
-        k_tc_refine_tail<<<grid_for(items, 2, sms), kPipeThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
+        k_tc_refine_tail<<<grid_for(items, 2, sms), kThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;
@@ -925,9 +964,9 @@ void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst,
     if ((long long)rs.R * rs.core_h * rs.core_w == 0) return;
     const int sms = sm_count();
     const long long strips = (long long)rs.R * ((rs.core_w + kM - 1) / kM);
-    const int band = pick_band(strips, rs.core_h, sms * 2);
+    const int band = pick_band_balanced(strips, rs.core_h, sms * 4);
     const long long items = strips * ((rs.core_h + band - 1) / band);
-    k_tc_head<<<grid_for(items, 2, sms), kHeadThreads, 0, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
+    k_tc_head<<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
     AEISU_CUDA(cudaGetLastError());
     *launches += 1;
 }

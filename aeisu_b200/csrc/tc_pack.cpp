@@ -104,23 +104,19 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         for (int i = 0; i < 64; ++i) tb[i] = round_f16(T.bias[i]);  // f16 tail bias (Refine.cuh:494-495)
         P.tail_bias = append_floats(P.floats, tb);
     }
-    // head: phase-major columns n = phase*32 + tap (taps 25..31 of each phase are zero), so
-    // columns [64g, 64g+64) hold the two phases of output row 2y+g; FP32 bank split into
-    // hi + lo f16
+    // head: column n = tap*4 + phase (100 used of 128); FP32 bank split into hi + lo f16
     {
         auto bank = [&](int n, int k, bool lo) -> uint32_t {
-            const int p = n / 32, tap = n % 32;
-            if (tap >= 25) return 0;
-            const float v = m.basis[(tap * 16 + k) * 4 + p];
+            if (n >= 100) return 0;
+            const float v = m.basis[((n / 4) * 16 + k) * 4 + n % 4];
             const uint16_t hi = f32_to_f16_bits(v);
             return lo ? f32_to_f16_bits(v - f16_bits_to_f32(hi)) : hi;
         };
         auto hi = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, false); });
         auto lo = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, true); });
         auto base = pack_operand(128, 16, 2, [&](int n, int k) -> uint32_t {
-            const int p = n / 32, tap = n % 32;
-            if (tap >= 25 || k > 1) return 0;
-            const float v = m.base[tap * 4 + p];
+            if (n >= 100 || k > 1) return 0;
+            const float v = m.base[(n / 4) * 4 + n % 4];
             const uint16_t h = f32_to_f16_bits(v);
             return k == 0 ? h : f32_to_f16_bits(v - f16_bits_to_f32(h));
         });
