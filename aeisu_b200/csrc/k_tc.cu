@@ -739,7 +739,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
             if (src.kind == 0) {
                 const uint8_t* p = static_cast<const uint8_t*>(src.ptr) + ((size_t(reg.x) * src.H + sy) * src.W + sx[j]) * 3;
-                return make_uint3(uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16), 0u, 0u);
+                return make_uint3(p[0], p[1], p[2]);
             }
             const size_t plane = size_t(src.H) * src.W;
             const float* p = static_cast<const float*>(src.ptr) + size_t(reg.x) * 3 * plane + size_t(sy) * src.W + sx[j];

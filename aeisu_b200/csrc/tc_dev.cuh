@@ -38,20 +38,20 @@ __device__ __forceinline__ float3 load_src(const SrcDesc& s, int f, int py, int 
 }
 
 // Two-step form of load_src for prefetching: fetch_src_raw issues the global loads and
-// returns the raw sample (three uint8 packed in .x, or three float bits); finish_src converts
-// it later, once the loads have had time to land.
+// returns the raw sample (three uint8 or three float bits, one per component, so nothing
+// consumes the loads yet); finish_src converts it later, once the loads have had time to land.
 __device__ __forceinline__ uint3 fetch_src_raw(const SrcDesc& s, int f, int py, int px) {
     const int y = clampi(py - s.pad_y, 0, s.H - 1), x = clampi(px - s.pad_x, 0, s.W - 1);
     if (s.kind == 0) {
         const uint8_t* p = static_cast<const uint8_t*>(s.ptr) + ((size_t(f) * s.H + y) * s.W + x) * 3;
-        return make_uint3(uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16), 0u, 0u);
+        return make_uint3(p[0], p[1], p[2]);
     }
     const size_t plane = size_t(s.H) * s.W;
     const float* p = static_cast<const float*>(s.ptr) + size_t(f) * 3 * plane + size_t(y) * s.W + x;
     return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
 }
 __device__ __forceinline__ float3 finish_src(const SrcDesc& s, uint3 raw, const float* lut) {
-    if (s.kind == 0) return make_float3(lut[raw.x & 255u], lut[(raw.x >> 8) & 255u], lut[raw.x >> 16]);
+    if (s.kind == 0) return make_float3(lut[raw.x], lut[raw.y], lut[raw.z]);
     return make_float3(__uint_as_float(raw.x), __uint_as_float(raw.y), __uint_as_float(raw.z));
 }
 
