@@ -157,6 +157,8 @@ Engine::Engine(HostModel model, int precision, int device)
     int lo = 0, hi = 0;
     AEISU_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
     AEISU_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
+    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking));
+    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking));
     for (auto& e : ev_) AEISU_CUDA(cudaEventCreate(&e));
     upload_weights();
     cudaDeviceProp prop{};
@@ -177,6 +179,8 @@ Engine::~Engine() {
     cudaGetDevice(&prev);
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    for (cudaStream_t c : {copy_in_, copy_out_})
+        if (c) cudaStreamSynchronize(c);
     DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_,
                      &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
     for (DevBuf* b : all) b->reset();
@@ -185,7 +189,10 @@ Engine::~Engine() {
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
     for (auto& e : pool_) cudaEventDestroy(e);
+    for (auto& e : chunk_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
+    for (cudaStream_t c : {copy_in_, copy_out_})
+        if (c) cudaStreamDestroy(c);
     if (prev >= 0) cudaSetDevice(prev);
 }
 
@@ -410,11 +417,77 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
     (void)g;
 }
 
+// Host-buffer upscale of several frames from and to page-locked memory: frames go through in
+// chunks, so the upload of chunk i+1 and the download of chunk i-1 (two copy streams) overlap
+// the kernels of chunk i on the compute stream.  Frames are independent, so a chunk is a
+// complete upscale call of its own; the device buffers hold the whole batch, so no chunk waits
+// for a buffer slot.
+void Engine::run_pipelined(const Call& c, cudaStream_t s) {
+    const int chunks = std::min(c.n, 8);
+    const int per = (c.n + chunks - 1) / chunks;
+    const size_t in_frame = size_t(3) * c.h * c.w, out_frame = size_t(12) * c.h * c.w;
+    src_.ensure(in_frame * c.n, s);
+    dst_.ensure(out_frame * c.n, s);
+    while (chunk_ev_.size() < size_t(2 * chunks + 1)) {
+        cudaEvent_t e;
+        AEISU_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        chunk_ev_.push_back(e);
+    }
+    // the copy streams start after everything already queued on the compute stream
+    AEISU_CUDA(cudaStreamWaitEvent(copy_in_, ev_[0], 0));
+    AEISU_CUDA(cudaStreamWaitEvent(copy_out_, ev_[0], 0));
+    AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, 2 * sizeof(int), s));  // [0] non-finite, [1] pipeline error
+    const uint8_t* hsrc = static_cast<const uint8_t*>(c.src);
+    uint8_t* hdst = static_cast<uint8_t*>(c.dst);
+    for (int i = 0, f0 = 0; f0 < c.n; ++i, f0 += per) {
+        const int k = std::min(per, c.n - f0);
+        cudaEvent_t uploaded = chunk_ev_[2 * i], computed = chunk_ev_[2 * i + 1];
+        uint8_t* dsrc = src_.as<uint8_t>() + in_frame * f0;
+        uint8_t* ddst = dst_.as<uint8_t>() + out_frame * f0;
+        AEISU_CUDA(cudaMemcpyAsync(dsrc, hsrc + in_frame * f0, in_frame * k, cudaMemcpyHostToDevice, copy_in_));
+        AEISU_CUDA(cudaEventRecord(uploaded, copy_in_));
+        AEISU_CUDA(cudaStreamWaitEvent(s, uploaded, 0));
+        record(0, s);
+        Call part = c;
+        part.n = k;
+        const Geometry g = plan_upscale(k, c.h, c.w, c.tile);
+        SrcDesc src{dsrc, 0, c.h, c.w, g.pad_y, g.pad_x};
+        DstDesc dst{ddst, 0, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
+        for (const auto& grp : g.groups) run_group(part, g, grp, src, dst, s);
+        AEISU_CUDA(cudaEventRecord(computed, s));
+        AEISU_CUDA(cudaStreamWaitEvent(copy_out_, computed, 0));
+        AEISU_CUDA(cudaMemcpyAsync(hdst + out_frame * f0, ddst, out_frame * k, cudaMemcpyDeviceToHost, copy_out_));
+    }
+    // the call ends on the compute stream once the last download has landed
+    AEISU_CUDA(cudaEventRecord(chunk_ev_[2 * chunks], copy_out_));
+    AEISU_CUDA(cudaStreamWaitEvent(s, chunk_ev_[2 * chunks], 0));
+    AEISU_CUDA(cudaEventRecord(ev_[6], s));
+    finish_host_call(c, s, false, 0);
+}
+
+void Engine::finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t dst_bytes) {
+    wait(s, timeout_ms_);
+    if (staged) std::memcpy(c.dst, staging_.get(), dst_bytes);
+    int flag[2] = {0, 0};
+    AEISU_CUDA(cudaMemcpy(flag, flag_.get(), sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag[1]) fail(AEISU_ERR_CUDA, "tensor-core pipeline wait expired inside a kernel (code " +
+                                          std::to_string(flag[1]) + ")");
+    if (flag[0] && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
+}
+
 void Engine::run(const Call& c) {
     DeviceGuard guard(device_);
     require(c.src != nullptr && c.dst != nullptr, "source and destination must not be null");
     const Geometry g = (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile) : plan_whole(c.n, c.h, c.w);
     cudaStream_t s = c.stream ? c.stream : stream_;
+    if (c.host && c.mode == Mode::Upscale && c.src_kind == 0 && c.dst_kind == 0 && c.n >= 2 && is_pinned(c.src) &&
+        is_pinned(c.dst)) {
+        marks_.clear();
+        timings_pending_ = true;
+        AEISU_CUDA(cudaEventRecord(ev_[0], s));
+        run_pipelined(c, s);
+        return;
+    }
     const size_t src_elem = c.src_kind == 0 ? 1 : 4;
     const size_t src_bytes = size_t(c.n) * 3 * c.h * c.w * src_elem;
     size_t dst_bytes;
@@ -446,15 +519,7 @@ void Engine::run(const Call& c) {
         AEISU_CUDA(cudaMemcpyAsync(out, dst_.get(), dst_bytes, cudaMemcpyDeviceToHost, s));
     }
     AEISU_CUDA(cudaEventRecord(ev_[6], s));
-    if (c.host) {
-        wait(s, timeout_ms_);
-        if (staged) std::memcpy(c.dst, staging_.get(), dst_bytes);
-        int flag[2] = {0, 0};
-        AEISU_CUDA(cudaMemcpy(flag, flag_.get(), sizeof(flag), cudaMemcpyDeviceToHost));
-        if (flag[1]) fail(AEISU_ERR_CUDA, "tensor-core pipeline wait expired inside a kernel (code " +
-                                              std::to_string(flag[1]) + ")");
-        if (flag[0] && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
-    }
+    if (c.host) finish_host_call(c, s, staged, dst_bytes);
 }
 
 }  // namespace aeisu

@@ -125,12 +125,15 @@ private:
     void upload_weights();
     void run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
                    const DstDesc& dst, cudaStream_t s);
+    void run_pipelined(const Call& c, cudaStream_t s);
+    void finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t dst_bytes);
     void wait(cudaStream_t s, double timeout_ms);
     void record(int stage, cudaStream_t s);
 
     HostModel model_;
     int precision_, device_;
     cudaStream_t stream_ = nullptr;
+    cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;   // host<->device copies of pipelined calls
     std::string report_;
     double timeout_ms_ = 60000.0;
     bool detailed_ = false;
@@ -160,6 +163,7 @@ private:
     // timing events: [0] call start, [1]/[2] detailed stage marks, [6] call end, [7] waits
     cudaEvent_t ev_[8] = {};
     std::vector<cudaEvent_t> pool_;                // stage-mark events, reused across calls
+    std::vector<cudaEvent_t> chunk_ev_;            // pipelined calls: 2 events per frame chunk
     std::vector<std::pair<int, int>> marks_;       // (stage closed by this mark, pool index)
     bool timings_pending_ = false;
 };
