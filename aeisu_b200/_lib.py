@@ -47,6 +47,8 @@ _SIGNATURES = {
                                     C.c_uint, C.c_void_p]),
     "aeisu_upscale_u8_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                            C.c_void_p]),
+    "aeisu_upscale_u8_band": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                        C.c_uint, C.c_void_p]),
     "aeisu_forward_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_uint,
                                     C.c_void_p]),
     "aeisu_predict_coefficients": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,

@@ -111,6 +111,19 @@ int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, i
     });
 }
 
+int aeisu_upscale_u8_band(aeisu_t* handle, const uint8_t* src, int h, int w, int band, int bands, uint8_t* dst,
+                          unsigned flags, void* stream) {
+    return guarded([&] {
+        check_io(1, h, w, flags);
+        aeisu::Call c{aeisu::Mode::Upscale, src, 0, dst, 0, 1, h, w, 0, flags == AEISU_IO_HOST,
+                      static_cast<cudaStream_t>(stream)};
+        c.band = band;
+        c.bands = bands;
+        aeisu::require(bands >= 1 && band >= 0 && band < bands, "band index out of range");
+        engine_of(handle).run(c);
+    });
+}
+
 int aeisu_upscale_u8_noalloc(aeisu_t* handle, const uint8_t* src, int n, int h, int w, uint8_t* dst,
                              void* stream) {
     return guarded([&] {

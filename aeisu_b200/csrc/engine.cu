@@ -127,6 +127,19 @@ Geometry plan_whole(int n, int h, int w) {
     return g;
 }
 
+Geometry plan_band(int h, int w, int band, int bands) {
+    require(bands >= 1 && bands <= 4096 && band >= 0 && band < bands, "band index out of range");
+    Geometry g = plan_upscale(1, h, w, 0);
+    g.groups.clear();
+    const int per = (g.ph / 32 + bands - 1) / bands * 32;
+    const int y = band * per, y1 = std::min(g.ph, y + per);
+    if (y >= y1) return g;   // more bands than 32-row groups: nothing left for this one
+    const int sy = std::max(0, y - 32), ey = std::min(g.ph, y1 + 32);
+    const int cy0 = std::max(y, g.pad_y), cy1 = std::min(y1, g.pad_y + h);
+    if (cy0 < cy1) g.groups.push_back({ey - sy, g.pw, {{0, sy, 0, cy0 - sy, g.pad_x, cy1 - sy, g.pad_x + w}}});
+    return g;
+}
+
 // ---- engine -------------------------------------------------------------------------
 
 struct Engine::DeviceGuard {
@@ -357,7 +370,7 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
         }
         // Region tables are uploaded once per call geometry and kept on the device: an upload
         // from pageable memory would wait for the stream to drain on every call.
-        const TableKey key{int(c.mode), c.n, c.h, c.w, c.tile, rh * 65536 + rw, int(first)};
+        const TableKey key{int(c.mode), c.n, c.h, c.w, c.tile, rh * 65536 + rw, int(first), c.band, c.bands};
         auto it = table_cache_.find(key);
         if (it == table_cache_.end()) {
             if (table_cache_.size() >= 256) {
@@ -478,10 +491,12 @@ void Engine::finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t
 void Engine::run(const Call& c) {
     DeviceGuard guard(device_);
     require(c.src != nullptr && c.dst != nullptr, "source and destination must not be null");
-    const Geometry g = (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile) : plan_whole(c.n, c.h, c.w);
+    const Geometry g = c.bands > 0                ? plan_band(c.h, c.w, c.band, c.bands)
+                       : (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile)
+                                                   : plan_whole(c.n, c.h, c.w);
     cudaStream_t s = c.stream ? c.stream : stream_;
-    if (c.host && c.mode == Mode::Upscale && c.src_kind == 0 && c.dst_kind == 0 && c.n >= 2 && is_pinned(c.src) &&
-        is_pinned(c.dst)) {
+    if (c.bands == 0 && c.host && c.mode == Mode::Upscale && c.src_kind == 0 && c.dst_kind == 0 && c.n >= 2 &&
+        is_pinned(c.src) && is_pinned(c.dst)) {
         marks_.clear();
         timings_pending_ = true;
         AEISU_CUDA(cudaEventRecord(ev_[0], s));
@@ -499,10 +514,29 @@ void Engine::run(const Call& c) {
     AEISU_CUDA(cudaEventRecord(ev_[0], s));
     const void* src_ptr = c.src;
     void* dst_ptr = c.dst;
+    // byte ranges of the host buffers a call reads and writes: whole buffers, or for a row
+    // band the source rows its crop can touch and the output rows of its core
+    size_t src_off = 0, src_len = src_bytes, dst_off = 0, dst_len = dst_bytes;
+    if (c.bands > 0) {
+        src_len = dst_len = 0;
+        if (!g.groups.empty()) {
+            const Region& r = g.groups[0].regions[0];
+            const int rh = g.groups[0].rh;
+            const int r0 = std::clamp(r.oy - g.pad_y, 0, c.h - 1), r1 = std::clamp(r.oy + rh - 1 - g.pad_y, 0, c.h - 1);
+            const size_t src_row = size_t(3) * c.w * src_elem, dst_row = size_t(6) * c.w * (c.dst_kind == 0 ? 1 : 4);
+            src_off = src_row * r0;
+            src_len = src_row * (r1 - r0 + 1);
+            dst_off = dst_row * 2 * (r.oy + r.cy0 - g.pad_y);
+            dst_len = dst_row * 2 * (r.cy1 - r.cy0);
+            require(c.src_kind == 0, "row bands take uint8 frames");
+        }
+    }
     if (c.host) {
         src_.ensure(src_bytes, s);
         dst_.ensure(dst_bytes, s);
-        AEISU_CUDA(cudaMemcpyAsync(src_.get(), c.src, src_bytes, cudaMemcpyHostToDevice, s));
+        if (src_len)
+            AEISU_CUDA(cudaMemcpyAsync(src_.as<char>() + src_off, static_cast<const char*>(c.src) + src_off, src_len,
+                                       cudaMemcpyHostToDevice, s));
         src_ptr = src_.get();
         dst_ptr = dst_.get();
     }
@@ -514,12 +548,16 @@ void Engine::run(const Call& c) {
     // Pageable destinations go through page-locked staging: a direct copy into pageable
     // memory would block the host without the completion bound.
     const bool staged = c.host && !is_pinned(c.dst);
-    if (c.host) {
-        void* out = staged ? staging_.ensure(dst_bytes, s) : c.dst;
-        AEISU_CUDA(cudaMemcpyAsync(out, dst_.get(), dst_bytes, cudaMemcpyDeviceToHost, s));
+    if (c.host && dst_len) {
+        char* out = staged ? static_cast<char*>(staging_.ensure(dst_len, s)) : static_cast<char*>(c.dst) + dst_off;
+        AEISU_CUDA(cudaMemcpyAsync(out, dst_.as<char>() + dst_off, dst_len, cudaMemcpyDeviceToHost, s));
     }
     AEISU_CUDA(cudaEventRecord(ev_[6], s));
-    if (c.host) finish_host_call(c, s, staged, dst_bytes);
+    if (c.host) {
+        wait(s, timeout_ms_);
+        if (staged && dst_len) std::memcpy(static_cast<char*>(c.dst) + dst_off, staging_.get(), dst_len);
+        finish_host_call(c, s, false, 0);
+    }
 }
 
 }  // namespace aeisu

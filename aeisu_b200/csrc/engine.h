@@ -70,6 +70,11 @@ struct Geometry {
 Geometry plan_upscale(int n, int h, int w, int tile);
 // One region per frame covering an already padded image (FoldedAEISU.forward semantics).
 Geometry plan_whole(int n, int h, int w);
+// Row band `band` of `bands` of one frame: the padded grid's rows split into equal bands of a
+// multiple of 32 rows; the band's crop adds 32 rows above and below (clipped), like the tile
+// halos of runtime.py:92-99, over the full padded width.  Its core pixels equal the
+// whole-frame result (the controller's receptive field is smaller than the halo).
+Geometry plan_band(int h, int w, int band, int bands);
 
 enum class Mode { Upscale, Forward, Predict };
 
@@ -80,6 +85,7 @@ struct Call {
     int n, h, w, tile;
     bool host;
     cudaStream_t stream;
+    int band = 0, bands = 0;        // bands > 0: one row band of a single frame (plan_band)
 };
 
 class Engine {
@@ -150,8 +156,8 @@ private:
     TcWeights tcw_{};
     size_t tc_head_off_ = 0;
 
-    // region tables per call geometry (mode, n, h, w, tile, group shape, first region)
-    using TableKey = std::array<int, 7>;
+    // region tables per call geometry (mode, n, h, w, tile, group shape, first region, band, bands)
+    using TableKey = std::array<int, 9>;
     std::map<TableKey, std::unique_ptr<DevBuf>> table_cache_;
 
     // workspace

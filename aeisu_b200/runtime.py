@@ -262,6 +262,26 @@ class Model:
             _lib.IO_DEVICE if a.device else _lib.IO_HOST, a.stream))
         return self._wrap(a, out)
 
+    def upscale_u8_band(self, frame, band, bands, out=None):
+        """Row band `band` of `bands` of one uint8 HWC frame (aeisu_upscale_u8_band): writes that
+        band's output rows of the 2x frame into `out` (allocated, zero-filled, when None) and
+        returns it.  The bands of 0..bands-1 together give exactly upscale_u8(frame, 0)."""
+        a = _Array(frame, np.uint8, self.device_index)
+        x = a.keep
+        if x.ndim != 3 or x.shape[-1] != 3:
+            raise ValueError("Expected one HWC RGB uint8 frame")
+        h, w = x.shape[:2]
+        shape = (2 * h, 2 * w, 3)
+        if out is None:
+            out = self._out(a, shape, np.uint8)
+            out[...] = 0
+        elif tuple(out.shape) != shape:
+            raise ValueError(f"out must have shape {shape}")
+        _lib.check(_lib.lib().aeisu_upscale_u8_band(
+            self._handle(), a.ptr, h, w, int(band), int(bands), self._ptr(out),
+            _lib.IO_DEVICE if a.device else _lib.IO_HOST, a.stream))
+        return self._wrap(a, out)
+
 
 def load_model(path, device="cuda", precision=None) -> Model:
     """runtime.load_model (aeisu/runtime.py:45-56) for folded ``.pt`` checkpoints, plus

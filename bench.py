@@ -40,10 +40,16 @@ WORKLOADS = {
     "mixed1080": (1, 1080, 1920, 0, "mixed", "adaptive_fp8.bin", "area"),
     "tiled1080": (32, 1080, 1920, 256, "fp16", "aeisu_bicubic.pt", "bicubic"),
     "stream4k": (8, 2160, 3840, 0, "mixed", "adaptive_fp8.bin", "area"),
+    # one 7680x4320 input frame split into one row band per GPU (strong scaling)
+    "band8k": (1, 4320, 7680, 0, "mixed", "adaptive_fp8.bin", "area"),
 }
+BAND_WORKLOADS = {"band8k"}
 # controller FLOPs per padded LR pixel (paper MAC table: 11,520 MAC) and head bytes per LR pixel
 CONTROLLER_FLOP_PER_PX = 2 * 11520
 HEAD_BYTES_PER_PX = 3 + 32 + 12
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of the
+# workload (profiles/k_tc_head_mixed720_traffic.md); reported as roofline.traffic
+RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.687e9)}
 
 
 def padded(h, w):
@@ -274,10 +280,17 @@ def main():
     stream = torch.cuda.Stream(dev)
     src = torch.from_numpy(frames).to(dev)
     out = torch.empty((n, 2 * h, 2 * w, 3), dtype=torch.uint8, device=dev)
+    band = args.workload in BAND_WORKLOADS   # every rank computes its own row band of the frame
+
+    def upscale(x, o):
+        if band:
+            model.upscale_u8_band(x[0], rank, world, out=o[0])
+        else:
+            model.upscale_u8(x, tile, out=o)
 
     def step():
         with torch.cuda.stream(stream):
-            model.upscale_u8(src, tile, out=out)
+            upscale(src, out)
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -310,7 +323,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    out_mpix = 4 * h * w * n * world
+    out_mpix = 4 * h * w * n * (1 if band else world)
     value = out_mpix / (ms_per_step / 1e3) / 1e6
 
     # detailed per-stage pass over the timed steps for the roofline (separate, same stream)
@@ -329,12 +342,12 @@ def main():
     # end-to-end through the public API with pinned host buffers
     host_src = torch.from_numpy(frames).pin_memory()
     host_out = torch.empty((n, 2 * h, 2 * w, 3), dtype=torch.uint8).pin_memory()
-    model.upscale_u8(host_src, tile, out=host_out)
+    upscale(host_src, host_out)
     barrier()
     t0 = time.perf_counter()
     e2e_steps = max(2, min(args.steps, 5))
     for _ in range(e2e_steps):
-        model.upscale_u8(host_src, tile, out=host_out)
+        upscale(host_src, host_out)
     e2e_dt = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_dt], device=dev)
@@ -350,13 +363,17 @@ def main():
     # per-stage MAC per padded LR pixel (aeisu/model.py CONVOLUTIONS x pixel rates)
     macs = {"analysis_project_ms": 256, "compress_core_ms": 512 + 4608, "expand_ms": 512,
             "refine_tail_ms": 4608 + 1024}
+    share = 1.0 / world if band else 1.0   # rank 0 times its own band: about 1/N of the frame
     if dom == "reconstruction_ms":
-        algo = HEAD_BYTES_PER_PX * h * w * n
+        algo = HEAD_BYTES_PER_PX * h * w * n * share
         achieved = algo / (stage_ms[dom] / 1e3) / 1e9
+        rec = RECORDED_TRAFFIC.get(args.workload)
+        traffic = rec[1] if rec and rec[0] == dom and not args.precision else None
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "stage": "reconstruction head", "peak_kind": peak_kind}
+                "traffic": traffic, "algorithmic_bytes": algo, "stage": "reconstruction head",
+                "kernel": "k_tc_head" if precision != "fp32" else "k_f32_head", "peak_kind": peak_kind}
     else:
-        algo = 2 * macs[dom] * hp * wp * n
+        algo = 2 * macs[dom] * hp * wp * n * share
         achieved = algo / (stage_ms[dom] / 1e3) / 1e12
         peak = tf_burst if precision != "mixed" else tf_burst  # FP8 peak not measured: bf16 figure
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -366,18 +383,20 @@ def main():
         line = {
             "metric": "2x output Mpix/s per B200 (FP8 mixed) frame-parallel; whole-job aggregate",
             "value": value, "unit": "output Mpix/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if band else "weak",
             "vs_baseline": None, "dtype": {"fp32": "f32", "fp16": "f16", "mixed": "e4m3+f16"}[precision],
             "data": "synthetic (seeded procedural scenes, 2x2 area / bicubic degradation)",
             "config": {"workload": args.workload, "frames_per_step_per_gpu": n, "frame": f"{w}x{h}",
                        "output": f"{2 * w}x{2 * h}", "tile": tile, "precision": precision, "checkpoint": ckpt,
                        "l2": "inputs+outputs per step exceed the 126 MB L2; no flush needed",
-                       "parallelism": f"frame-parallel x{world}"},
+                       "parallelism": (f"row bands x{world} (32-row halos recomputed, no exchange)" if band
+                                       else f"frame-parallel x{world}")},
             "stage_ms": stage_ms,
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "output Mpix/s",
-                    "h2d_bytes_per_step": int(n * h * w * 3), "d2h_bytes_per_step": int(n * 4 * h * w * 3),
+                    "h2d_bytes_per_step": int(n * h * w * 3 * share), "d2h_bytes_per_step": int(n * 4 * h * w * 3 * share),
                     "steps": e2e_steps},
             "gpu_launches": int(launches),
             "latency_1080p": latency,

@@ -98,6 +98,18 @@ void aeisu_close(aeisu_t* handle);
 int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, int tile,
                      uint8_t* dst, unsigned flags, void* stream);
 
+/* One row band of a single frame: aeisu_upscale_u8 with n = 1 and tile = 0, restricted to band
+ * `band` of `bands`.  The padded grid's rows are split into `bands` equal bands (a multiple of
+ * 32 rows each, the last one shorter); a band is computed on its rows plus 32 halo rows above
+ * and below (clipped to the grid), over the full width, like one tile of the reference's tiled
+ * path (aeisu/runtime.py:89-99).  The controller's receptive field is smaller than the halo,
+ * so the band's output rows equal those of the whole-frame call bit for bit.  src and dst are
+ * the whole frame (h x w x 3 in, 2h x 2w x 3 out); only the band's output rows are written,
+ * and with host I/O only the source rows the band reads are copied.  No reference counterpart:
+ * this is the single-huge-frame split across GPUs (one band per GPU, no data exchange). */
+int aeisu_upscale_u8_band(aeisu_t* handle, const uint8_t* src, int h, int w, int band, int bands,
+                          uint8_t* dst, unsigned flags, void* stream);
+
 /* Allocation-free variant of aeisu_upscale_u8 with device I/O and tile = 0 (no counterpart
  * in the reference).  For hosts that must not allocate GPU memory when they submit a frame
  * (a presentation loop that cannot stall on cudaMalloc, a process with a fixed memory budget,
