@@ -677,10 +677,13 @@ constexpr int kHeadRing = 8;
 constexpr int kHeadTW = kM + 4;
 
 // floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add (runtime.py:24-25 in
-// float32).  The sum lies in [0.5, 255.5]; adding 2^23 with round-down leaves floor(sum) in
-// the low mantissa bits, so byte 0 of the result is the output code.
-__device__ __forceinline__ uint32_t u8_code_bits(float v) {
-    return __float_as_uint(__fadd_rd(__fadd_rn(__fmul_rn(__saturatef(v), 255.f), 0.5f), 8388608.f));
+// float32), for two values at once (packed f32x2 arithmetic rounds each lane as the scalar
+// operation does).  The sum lies in [0.5, 255.5]; adding 2^23 with round-down leaves
+// floor(sum) in the low mantissa bits, so byte 0 of each result is the output code.
+__device__ __forceinline__ uint2 u8_code_bits2(float a, float b) {
+    const float2 m = __fmul2_rn(make_float2(__saturatef(a), __saturatef(b)), make_float2(255.f, 255.f));
+    const float2 f = __fadd2_rd(__fadd2_rn(m, make_float2(0.5f, 0.5f)), make_float2(8388608.f, 8388608.f));
+    return make_uint2(__float_as_uint(f.x), __float_as_uint(f.y));
 }
 
 __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
@@ -812,12 +815,10 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             // floats per channel plane
             if (x0 + t < xe) {
                 // one test for all twelve values: a non-finite term makes the sum non-finite
-                float all = 0.f;
-#pragma unroll
-                for (int p = 0; p < 4; ++p)
-#pragma unroll
-                    for (int ch = 0; ch < 3; ++ch) all += acc[p][ch];
-                if (!isfinite(all)) atomicOr(nonfinite, 1);
+                float2 all = __fadd2_rn(make_float2(acc[0][0], acc[0][1]), make_float2(acc[0][2], acc[1][0]));
+                all = __fadd2_rn(all, __fadd2_rn(make_float2(acc[1][1], acc[1][2]), make_float2(acc[2][0], acc[2][1])));
+                all = __fadd2_rn(all, __fadd2_rn(make_float2(acc[2][2], acc[3][0]), make_float2(acc[3][1], acc[3][2])));
+                if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
                 const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -829,14 +830,15 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                                                        ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
                                 make_float2(acc[2 * i][ch], acc[2 * i + 1][ch]);
                     } else {
-                        uint32_t q[6];
-#pragma unroll
-                        for (int k = 0; k < 6; ++k) q[k] = u8_code_bits(acc[2 * i + k / 3][k % 3]);
+                        // bytes r0 g0 b0 r1 g1 b1 of the two output pixels (phases 2i, 2i+1)
+                        const uint2 q01 = u8_code_bits2(acc[2 * i][0], acc[2 * i][1]);
+                        const uint2 q23 = u8_code_bits2(acc[2 * i][2], acc[2 * i + 1][0]);
+                        const uint2 q45 = u8_code_bits2(acc[2 * i + 1][1], acc[2 * i + 1][2]);
                         uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
                                                                   ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
-                        o[0] = uint16_t(__byte_perm(q[0], q[1], 0x0040));
-                        o[1] = uint16_t(__byte_perm(q[2], q[3], 0x0040));
-                        o[2] = uint16_t(__byte_perm(q[4], q[5], 0x0040));
+                        o[0] = uint16_t(__byte_perm(q01.x, q01.y, 0x0040));
+                        o[1] = uint16_t(__byte_perm(q23.x, q23.y, 0x0040));
+                        o[2] = uint16_t(__byte_perm(q45.x, q45.y, 0x0040));
                     }
                 }
             }

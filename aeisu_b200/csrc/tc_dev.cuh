@@ -17,7 +17,9 @@ constexpr int kThreads = 128;   // one thread per tile pixel / TMEM lane
 constexpr int kErrTimeout = 1;  // device error code: an mbarrier wait expired
 
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
-__device__ __forceinline__ float leaky(float v, float s) { return v > 0.f ? v : v * s; }
+// LeakyReLU for a negative slope s in [0, 1] (checked when the weights are packed): then
+// max(v, s*v) equals (v > 0 ? v : s*v) for every input, signed zeros and NaN included.
+__device__ __forceinline__ float leaky(float v, float s) { return fmaxf(v, v * s); }
 
 // (a*w0 + b*w1) + c*w2 without contraction, as the reference's separate tensor ops.
 __device__ __forceinline__ float mix3(float a, float b, float c, float w0, float w1, float w2) {

@@ -34,7 +34,15 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
     // bottleneck layers).
     float s[10];
     for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * kFp8ActivationHeadroom;
+    // one LeakyReLU slope for every activated layer (the tail is linear), in [0, 1] so that the
+    // kernels may evaluate it as max(v, slope * v)
     P.slope = m.layers[kProject].slope[0];
+    require(P.slope >= 0.f && P.slope <= 1.f, "activation slope outside [0, 1]", AEISU_ERR_UNSUPPORTED);
+    for (int l = 0; l < kLayerCount; ++l)
+        if (l != kTail)
+            for (float v : m.layers[l].slope)
+                require(v == P.slope, "the tensor-core routes need one activation slope for all layers",
+                        AEISU_ERR_UNSUPPORTED);
     P.inv_s1 = fp8 ? 1.0f / s[1] : 1.f;
     P.stencil = append_floats(P.floats, std::vector<float>(m.stencil, m.stencil + 24));
 
