@@ -403,11 +403,19 @@ struct Ring {
     __device__ uint32_t addr(int row) const { return base_addr + slot(row) * slot_bytes; }
 };
 
-// Grouped (2 x 32->32) 3x3 bottleneck layer.
+// Grouped (2 x 32->32) 3x3 bottleneck layer, warp-specialised: warp 4 is the producer (TMA
+// row loads and MMA issue, lane 0 issuing), warps 0-3 are the epilogue (warp w drains TMEM
+// lanes 32w..32w+31).  The two sides meet only on mbarriers:
+//   acc_full[b]  tcgen05.commit of row y's MMAs into TMEM buffer b  -> epilogue, producer
+//   acc_empty[b] one arrive per epilogue warp once it has read buffer b -> producer
+// so the epilogue never waits for MMA issue and there is no CTA-wide barrier per row.  The
+// producer refills the ring slot of row y-1 with row y+3 once MMA(y) has completed.
+constexpr int kWsThreads = 160;
+
 template <bool FP8>
-__global__ void __launch_bounds__(kThreads) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
-                                                      const uint8_t* __restrict__ wimg, EpiParams ep,
-                                                      void* __restrict__ out, int band, int* err) {
+__global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+                                                        const uint8_t* __restrict__ wimg, EpiParams ep,
+                                                        void* __restrict__ out, int band, int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
     constexpr int CPG = ICH / 2;              // chunks per group
     constexpr int WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
@@ -418,96 +426,125 @@ __global__ void __launch_bounds__(kThreads) k_tc_core(const __grid_constant__ CU
     float* s_scale = reinterpret_cast<float*>(sB + 2 * BG);
     float* s_bias = s_scale + 64;
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar[kRing + 2];   // ring slots, then MMA-done per TMEM buffer
+    __shared__ alignas(8) uint64_t s_bar[kRing + 4];   // ring slots, acc_full x2, acc_empty x2
+    uint64_t* acc_full = s_bar + kRing;
+    uint64_t* acc_empty = s_bar + kRing + 2;
     copy_image(sB, wimg, 2 * BG);
     if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
+    if (threadIdx.x == 0)
+        for (int b = 0; b < 2; ++b) mbar_init(&acc_empty[b], 4);
     fence_async_smem();
     cta_setup(&s_tmem, s_bar, kRing + 2, 128);
     const uint32_t tmem = s_tmem;
-    Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-    uint32_t mma_phase = 0, mma_pend = 0;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
     const int nstrip = (lw + kM - 1) / kM, nband = (lh + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
-    const int t = threadIdx.x, warp = t >> 5;
-    const uint32_t b0 = smem_addr(sB);
-    constexpr uint32_t idesc = idesc_m128(32);
-    auto issue = [&](int y, int buf) {   // MMAs of output row y into TMEM buffer buf
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+
+    if (warp == 4) {
+        // ---- producer: the whole warp follows the control flow, lane 0 issues ----
+        const bool leader = lane == 0;
+        const uint32_t b0 = smem_addr(sB);
+        constexpr uint32_t idesc = idesc_m128(32);
+        Ring ring{smem, smem_addr(smem), SLOT, s_bar};
+        uint32_t it = 0, pend = 0;   // rows issued; bit b: a commit into buffer b not yet observed here
+        bool ok = true;
+        auto load = [&](int row, const StripBand& sb) {
+            if (leader) {
+                mbar_arrive_expect_tx(&s_bar[Ring::slot(row)], uint32_t(SLOT));
+                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, 0, row, sb.r, &s_bar[Ring::slot(row)]);
+            }
+            ring.pending |= 1u << Ring::slot(row);
+        };
+        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            const StripBand sb = strip_band(item, nstrip, nband, band, lh);
+            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
+            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = ring.wait(row, err);
+            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
+                const int b = it & 1;
+                const uint32_t k = it >> 1;
+                // buffer b free (its previous row drained) and input row y+1 landed
+                if (k > 0) ok = mbar_wait_bounded(&acc_empty[b], (k - 1) & 1, err, kErrTimeout);
+                if (ok) ok = ring.wait(y + 1, err);
+                if (!ok) break;
+                fence_after_sync();
+                if (leader) {
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-            int step = 0;
+                    for (int g = 0; g < 2; ++g) {
+                        int step = 0;
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-                const uint32_t row = ring.addr(y - 1 + ky);
+                        for (int ky = 0; ky < 3; ++ky) {
+                            const uint32_t row = ring.addr(y - 1 + ky);
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx)
+                            for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-                    for (int k = 0; k < CPG / 2; ++k, ++step) {
-                        const uint64_t a = sdesc(row + (g * CPG + 2 * k) * LBO + kx * 16, LBO, 128);
-                        const uint64_t b = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * k) * 32 * 16, 32 * 16, 128);
-                        const uint32_t d = tmem + buf * 64 + g * 32;
-                        if (FP8) mma_e4m3(d, a, b, idesc, step > 0); else mma_f16(d, a, b, idesc, step > 0);
+                                for (int kk = 0; kk < CPG / 2; ++kk, ++step) {
+                                    const uint64_t a = sdesc(row + (g * CPG + 2 * kk) * LBO + kx * 16, LBO, 128);
+                                    const uint64_t bd = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * kk) * 32 * 16, 32 * 16, 128);
+                                    const uint32_t d = tmem + b * 64 + g * 32;
+                                    if (FP8) mma_e4m3(d, a, bd, idesc, step > 0); else mma_f16(d, a, bd, idesc, step > 0);
+                                }
+                        }
                     }
-            }
-        }
-        commit(&s_bar[kRing + buf]);
-        mma_pend |= 1u << buf;
-    };
-    bool ok = true;
-    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const StripBand sb = strip_band(item, nstrip, nband, band, lh);
-        if (t == 0) {
-            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) ring.load(&tin, sb.x0, row, sb.r);
-            for (int row = sb.y0 - 1; row <= sb.y0 + 1 && ok; ++row) ok = ring.wait(row, err);
-            fence_after_sync();
-            if (ok) issue(sb.y0, 0);
-        }
-        for (int y = sb.y0; y < sb.y1; ++y) {
-            const int buf = (y - sb.y0) & 1;
-            bool good = mbar_wait_bounded(&s_bar[kRing + buf], (mma_phase >> buf) & 1u, err, kErrTimeout);
-            if (good) {
-                mma_phase ^= 1u << buf;
-                mma_pend &= ~(1u << buf);
-            }
-            fence_after_sync();
-            if (t == 0 && good && ok) {
-                if (y + 3 <= sb.y1) ring.load(&tin, sb.x0, y + 3, sb.r);
-                if (y + 1 < sb.y1) {
-                    good = ring.wait(y + 2, err);
-                    if (good) issue(y + 1, buf ^ 1);
+                    commit(&acc_full[b]);
+                }
+                __syncwarp();
+                pend |= 1u << b;
+                // refill the slot of row y-1 with row y+3 once MMA(y) has read it
+                if (y + 3 <= sb.y1) {
+                    ok = mbar_wait_bounded(&acc_full[b], k & 1, err, kErrTimeout);
+                    if (!ok) break;
+                    pend &= ~(1u << b);
+                    load(y + 3, sb);
                 }
             }
-            const int x = sb.x0 + t;
-            float vv[2][32];
-            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 64, tmem + (uint32_t(32 * warp) << 16) + buf * 64 + 32,
-                        vv[0], vv[1]);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float (&v)[32] = vv[h];
-#pragma unroll
-                for (int n = 0; n < 32; ++n)
-                    v[n] = leaky(fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
-                if (x < lw) {
-                    if (FP8) {
-                        uint4 q[2];
-                        pack_e4m3x32(v, q);
-                        for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 2 + c, lw, x) = q[c];
-                    } else {
-                        uint4 q[4];
-                        pack_f16x32(v, q);
-                        for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 4 + c, lw, x) = q[c];
-                    }
-                }
-            }
-            fence_before_sync();
-            if (__syncthreads_or(!(good && ok))) { ok = false; break; }
         }
-    }
-    if (!ok && t == 0) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
+        // let copies and MMAs still in flight land before TMEM is released
         ring.drain(err);
         for (int b = 0; b < 2; ++b)
-            if (mma_pend & (1u << b))
-                mbar_wait_bounded(&s_bar[kRing + b], (mma_phase >> b) & 1u, err, kErrTimeout, 200000000LL);
+            if (pend & (1u << b)) {
+                // the last commit into buffer b: row it-1 or it-2
+                const uint32_t last = ((it - 1) & 1) == uint32_t(b) ? it - 1 : it - 2;
+                mbar_wait_bounded(&acc_full[b], (last >> 1) & 1, err, kErrTimeout, 200000000LL);
+            }
+    } else {
+        // ---- epilogue warps ----
+        uint32_t it = 0;
+        bool ok = true;
+        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            const StripBand sb = strip_band(item, nstrip, nband, band, lh);
+            const int x = sb.x0 + t;
+            for (int y = sb.y0; y < sb.y1; ++y, ++it) {
+                const int b = it & 1;
+                ok = mbar_wait_bounded(&acc_full[b], (it >> 1) & 1, err, kErrTimeout);
+                if (!ok) break;
+                fence_after_sync();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float v[32];
+                    tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 64 + h * 32, v);
+                    if (h == 1) {   // both halves read: hand the buffer back to the producer
+                        fence_before_sync();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[b]);
+                    }
+#pragma unroll
+                    for (int n = 0; n < 32; ++n)
+                        v[n] = leaky(fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
+                    if (x < lw) {
+                        if (FP8) {
+                            uint4 q[2];
+                            pack_e4m3x32(v, q);
+                            for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 2 + c, lw, x) = q[c];
+                        } else {
+                            uint4 q[4];
+                            pack_f16x32(v, q);
+                            for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 4 + c, lw, x) = q[c];
+                        }
+                    }
+                }
+            }
+        }
     }
     cta_teardown(tmem, 128);
 }
@@ -935,8 +972,8 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const CUtensorMap* maps[2] = {&map_a, &map_b};
         if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else k_tc_core<false><<<grid_for(items, per_sm, sms), kThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kWsThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else k_tc_core<false><<<grid_for(items, per_sm, sms), kWsThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);
