@@ -549,154 +549,210 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     cta_teardown(tmem, 128);
 }
 
-// refine_540 (3x3 32->64) + metadata_head (1x1 64->64), pipelined like k_tc_core.  The
-// refine output (LeakyReLU, f16) goes back to shared memory as the tail GEMM's A operand and
-// never reaches HBM.  The tail epilogue writes clamped f16 coefficients in the head's
-// layout meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
+// refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core.
+// The refine output (LeakyReLU, f16) goes to shared memory as the tail GEMM's A operand and
+// never reaches HBM.  Warp 4 (producer) issues, per row y: refine(y) into TMEM buffer b, then
+// tail(y-1) once the epilogue has written row y-1's operand, then the TMA refill of row y+3.
+// Warps 0-3 (epilogue) alternate: refine epilogue of row y, tail epilogue of row y-1, so the
+// tail MMA of a row runs while the next row's refine epilogue does.  Refine and tail
+// accumulators and the tail operand are double-buffered; every hand-over is an mbarrier.
+// The tail epilogue writes clamped f16 coefficients in the head's layout
+// meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
-__global__ void __launch_bounds__(kThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
-                                                             const uint8_t* __restrict__ wref,
-                                                             const uint8_t* __restrict__ wtail,
-                                                             const float* __restrict__ rbias,
-                                                             const float* __restrict__ tbias, float slope,
-                                                             void* __restrict__ meta, float* __restrict__ raw,
-                                                             int band, int* err) {
+__global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+                                                               const uint8_t* __restrict__ wref,
+                                                               const uint8_t* __restrict__ wtail,
+                                                               const float* __restrict__ rbias,
+                                                               const float* __restrict__ tbias, float slope,
+                                                               void* __restrict__ meta, float* __restrict__ raw,
+                                                               int band, int* err) {
     constexpr int ICH = 4, WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
     constexpr int BREF = 36 * 64 * 16, BTAIL = 8 * 64 * 16, A2 = 8 * kM * 16;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;   // refine weights
     uint8_t* sT = sB + BREF;             // tail weights
-    uint8_t* sA2 = sT + BTAIL;           // tail operand (one row)
-    float* s_rb = reinterpret_cast<float*>(sA2 + A2);
+    uint8_t* sA2 = sT + BTAIL;           // tail operands, one per buffer
+    float* s_rb = reinterpret_cast<float*>(sA2 + 2 * A2);
     float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar[kRing + 3];   // ring, refine-done x2, tail-done
+    // ring slots, then per buffer b: ref_full, tail_full (count 1); ref_empty, a2_full, tail_empty (count 4)
+    __shared__ alignas(8) uint64_t s_bar[kRing + 10];
+    uint64_t* ref_full = s_bar + kRing;
+    uint64_t* tail_full = s_bar + kRing + 2;
+    uint64_t* ref_empty = s_bar + kRing + 4;
+    uint64_t* a2_full = s_bar + kRing + 6;
+    uint64_t* tail_empty = s_bar + kRing + 8;
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
     if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
+    if (threadIdx.x == 0)
+        for (int i = kRing + 4; i < kRing + 10; ++i) mbar_init(&s_bar[i], 4);
     fence_async_smem();
-    cta_setup(&s_tmem, s_bar, kRing + 3, 256);
+    cta_setup(&s_tmem, s_bar, kRing + 4, 256);
     const uint32_t tmem = s_tmem;
-    Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-    uint32_t mma_phase = 0, tail_phase = 0, mma_pend = 0;   // pend bits: refine buf 0/1, tail (bit 2)
     const int ph = rs.rh / 2, pw = rs.rw / 2;
     const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
-    const int t = threadIdx.x, warp = t >> 5;
-    const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     constexpr uint32_t idesc = idesc_m128(64);
-    auto issue_refine = [&](int y, int buf) {
-        int step = 0;
-#pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-            const uint32_t row = ring.addr(y - 1 + ky);
-#pragma unroll
-            for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                for (int k = 0; k < 2; ++k, ++step)
-                    mma_f16(tmem + buf * 128, sdesc(row + 2 * k * LBO + kx * 16, LBO, 128),
-                            sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * k) * 64 * 16, 64 * 16, 128), idesc, step > 0);
-        }
-        commit(&s_bar[kRing + buf]);
-        mma_pend |= 1u << buf;
-    };
-    bool ok = true;
-    for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const StripBand sb = strip_band(item, nstrip, nband, band, ph);
-        if (t == 0) {
-            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) ring.load(&tin, sb.x0, row, sb.r);
-            for (int row = sb.y0 - 1; row <= sb.y0 + 1 && ok; ++row) ok = ring.wait(row, err);
-            fence_after_sync();
-            if (ok) issue_refine(sb.y0, 0);
-        }
-        for (int y = sb.y0; y < sb.y1; ++y) {
-            const int buf = (y - sb.y0) & 1;
-            bool good = mbar_wait_bounded(&s_bar[kRing + buf], (mma_phase >> buf) & 1u, err, kErrTimeout);
-            if (good) {
-                mma_phase ^= 1u << buf;
-                mma_pend &= ~(1u << buf);
+
+    if (warp == 4) {
+        // ---- producer: the whole warp follows the control flow, lane 0 issues ----
+        const bool leader = lane == 0;
+        const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
+        Ring ring{smem, smem_addr(smem), SLOT, s_bar};
+        uint32_t it = 0;             // rows whose refine was issued
+        uint32_t pend = 0;           // bits 0/1 refine, 2/3 tail: committed, not observed here
+        uint32_t last[4] = {0, 0, 0, 0};
+        bool ok = true;
+        auto load = [&](int row, const StripBand& sb) {
+            if (leader) {
+                mbar_arrive_expect_tx(&s_bar[Ring::slot(row)], uint32_t(SLOT));
+                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, 0, row, sb.r, &s_bar[Ring::slot(row)]);
             }
+            ring.pending |= 1u << Ring::slot(row);
+        };
+        auto tail = [&](uint32_t row_it) {   // tail GEMM of the row with counter row_it
+            const int pb = row_it & 1;
+            const uint32_t pk = row_it >> 1;
+            ok = mbar_wait_bounded(&a2_full[pb], pk & 1, err, kErrTimeout);
+            if (ok && pk > 0) ok = mbar_wait_bounded(&tail_empty[pb], (pk - 1) & 1, err, kErrTimeout);
+            if (!ok) return;
             fence_after_sync();
-            if (t == 0 && good && ok && y + 3 <= sb.y1) ring.load(&tin, sb.x0, y + 3, sb.r);
-            // refine epilogue -> tail operand
-            float vr[2][32];
-            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 128, tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 32,
-                        vr[0], vr[1]);
+            if (leader) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float (&v)[32] = vr[h];
-#pragma unroll
-                for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_rb[h * 32 + n], slope);
-                uint4 q[4];
-                pack_f16x32(v, q);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA2 + ((h * 4 + c) * kM + t) * 16) = q[c];
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16(tmem + pb * 128 + 64, sdesc(a20 + pb * A2 + kk * 2 * kM * 16, kM * 16, 128),
+                            sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc, kk > 0);
+                commit(&tail_full[pb]);
             }
-            fence_async_smem();
-            fence_before_sync();
-            __syncthreads();
-            if (t == 0 && good && ok) {
+            __syncwarp();
+            pend |= 4u << pb;
+            last[2 + pb] = pk;
+        };
+        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            const StripBand sb = strip_band(item, nstrip, nband, band, ph);
+            for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
+            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = ring.wait(row, err);
+            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
+                const int b = it & 1;
+                const uint32_t k = it >> 1;
+                if (k > 0) ok = mbar_wait_bounded(&ref_empty[b], (k - 1) & 1, err, kErrTimeout);
+                if (ok) ok = ring.wait(y + 1, err);
+                if (!ok) break;
                 fence_after_sync();
+                if (leader) {
+                    int step = 0;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    mma_f16(tmem + buf * 128 + 64, sdesc(a20 + k * 2 * kM * 16, kM * 16, 128),
-                            sdesc(t0 + k * 2 * 64 * 16, 64 * 16, 128), idesc, k > 0);
-                commit(&s_bar[kRing + 2]);
-                mma_pend |= 4u;
-                if (y + 1 < sb.y1) {
-                    good = ring.wait(y + 2, err);
-                    if (good) issue_refine(y + 1, buf ^ 1);
+                    for (int ky = 0; ky < 3; ++ky) {
+                        const uint32_t row = ring.addr(y - 1 + ky);
+#pragma unroll
+                        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                            for (int kk = 0; kk < 2; ++kk, ++step)
+                                mma_f16(tmem + b * 128, sdesc(row + 2 * kk * LBO + kx * 16, LBO, 128),
+                                        sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * kk) * 64 * 16, 64 * 16, 128), idesc, step > 0);
+                    }
+                    commit(&ref_full[b]);
+                }
+                __syncwarp();
+                pend |= 1u << b;
+                last[b] = k;
+                if (y > sb.y0) {   // tail of the previous row, queued behind refine(y)
+                    tail(it - 1);
+                    if (!ok) break;
+                }
+                if (y + 3 <= sb.y1) {   // refill the slot of row y-1 once refine(y) has read it
+                    ok = mbar_wait_bounded(&ref_full[b], k & 1, err, kErrTimeout);
+                    if (!ok) break;
+                    pend &= ~(1u << b);
+                    load(y + 3, sb);
                 }
             }
-            const bool tail_ok = mbar_wait_bounded(&s_bar[kRing + 2], tail_phase, err, kErrTimeout);
-            if (tail_ok) {
-                tail_phase ^= 1u;
-                mma_pend &= ~4u;
-            }
-            fence_after_sync();
-            const int x = sb.x0 + t;
-            float vt[2][32];
-            tmem_ld32x2(tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 64,
-                        tmem + (uint32_t(32 * warp) << 16) + buf * 128 + 96, vt[0], vt[1]);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float (&v)[32] = vt[h];
-                if (x < pw) {
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) v[n] += s_tb[h * 32 + n];
-                    if (raw) {
-                        float* rp = raw + (((size_t)sb.r * ph + y) * pw + x) * 64 + h * 32;
-#pragma unroll
-                        for (int n = 0; n < 32; ++n) rp[n] = v[n];
-                    }
-#pragma unroll
-                    for (int n = 0; n < 32; ++n) {   // coefficient_clamp
-                        const float m = fabsf(v[n]);
-                        const float s = fminf(fmaf(0.05f, m - 2.f, 2.f), 2.5f);
-                        v[n] = m <= 2.f ? v[n] : copysignf(s, v[n]);
-                    }
-                    uint4 q[4];
-                    pack_f16x32(v, q);
-#pragma unroll
-                    for (int pp = 0; pp < 2; ++pp) {
-                        const int parity = h * 2 + pp;
-                        const int Y = 2 * y + (parity >> 1), X = 2 * x + (parity & 1);
-#pragma unroll
-                        for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
-                    }
-                }
-            }
-            fence_before_sync();
-            if (__syncthreads_or(!(good && ok && tail_ok))) { ok = false; break; }
+            if (ok && sb.y1 > sb.y0) tail(it - 1);   // tail of the band's last row
         }
-    }
-    if (!ok && t == 0) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
+        // let copies and MMAs still in flight land before TMEM is released
         ring.drain(err);
-        for (int b = 0; b < 2; ++b)
-            if (mma_pend & (1u << b))
-                mbar_wait_bounded(&s_bar[kRing + b], (mma_phase >> b) & 1u, err, kErrTimeout, 200000000LL);
-        if (mma_pend & 4u) mbar_wait_bounded(&s_bar[kRing + 2], tail_phase, err, kErrTimeout, 200000000LL);
+        for (int i = 0; i < 4; ++i)
+            if (pend & (1u << i))
+                mbar_wait_bounded(i < 2 ? &ref_full[i] : &tail_full[i - 2], last[i] & 1, err, kErrTimeout, 200000000LL);
+    } else {
+        // ---- epilogue warps: refine epilogue of row y, then tail epilogue of row y-1 ----
+        const uint32_t lrow = uint32_t(32 * warp) << 16;
+        uint32_t it = 0;
+        bool ok = true;
+        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            const StripBand sb = strip_band(item, nstrip, nband, band, ph);
+            const int x = sb.x0 + t;
+            for (int y = sb.y0; y <= sb.y1 && ok; ++y) {
+                if (y < sb.y1) {
+                    const int b = it & 1;
+                    ok = mbar_wait_bounded(&ref_full[b], (it >> 1) & 1, err, kErrTimeout);
+                    if (!ok) break;
+                    fence_after_sync();
+                    float vr[2][32];
+                    tmem_ld32x2(tmem + lrow + b * 128, tmem + lrow + b * 128 + 32, vr[0], vr[1]);
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ref_empty[b]);
+                    uint8_t* a2 = sA2 + b * A2;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                        for (int n = 0; n < 32; ++n) vr[h][n] = leaky(vr[h][n] + s_rb[h * 32 + n], slope);
+                        uint4 q[4];
+                        pack_f16x32(vr[h], q);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + t) * 16) = q[c];
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a2_full[b]);
+                    ++it;
+                }
+                if (y > sb.y0) {   // tail epilogue of row y-1
+                    const uint32_t pit = it - 1 - (y < sb.y1 ? 1 : 0);
+                    const int pb = pit & 1, yt = y - 1;
+                    ok = mbar_wait_bounded(&tail_full[pb], (pit >> 1) & 1, err, kErrTimeout);
+                    if (!ok) break;
+                    fence_after_sync();
+                    float vt[2][32];
+                    tmem_ld32x2(tmem + lrow + pb * 128 + 64, tmem + lrow + pb * 128 + 96, vt[0], vt[1]);
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tail_empty[pb]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float (&v)[32] = vt[h];
+                        if (x < pw) {
+#pragma unroll
+                            for (int n = 0; n < 32; ++n) v[n] += s_tb[h * 32 + n];
+                            if (raw) {
+                                float* rp = raw + (((size_t)sb.r * ph + yt) * pw + x) * 64 + h * 32;
+#pragma unroll
+                                for (int n = 0; n < 32; ++n) rp[n] = v[n];
+                            }
+#pragma unroll
+                            for (int n = 0; n < 32; ++n) {   // coefficient_clamp
+                                const float m = fabsf(v[n]);
+                                const float s = fminf(fmaf(0.05f, m - 2.f, 2.f), 2.5f);
+                                v[n] = m <= 2.f ? v[n] : copysignf(s, v[n]);
+                            }
+                            uint4 q[4];
+                            pack_f16x32(v, q);
+#pragma unroll
+                            for (int pp = 0; pp < 2; ++pp) {
+                                const int parity = h * 2 + pp;
+                                const int Y = 2 * yt + (parity >> 1), X = 2 * x + (parity & 1);
+#pragma unroll
+                                for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
+                            }
+                        }
+                    }
+                }
+            }
+        }
     }
     cta_teardown(tmem, 256);
 }
@@ -985,13 +1041,13 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
     }
     mark(3);
     {
-        const int bytes = 1024 + kRing * 4 * (kM + 2) * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 8 * kM * 16 + 2 * 64 * 4;
+        const int bytes = 1024 + kRing * 4 * (kM + 2) * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
         const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
         const int band = pick_band(strips, ph, sms * 2);
         const long long items = strips * ((ph + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
         smem_attr(k_tc_refine_tail, bytes);
-        k_tc_refine_tail<<<grid_for(items, 2, sms), kThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
+        k_tc_refine_tail<<<grid_for(items, 2, sms), kWsThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;
