@@ -229,12 +229,21 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
     const long long ntiles = (long long)rs.R * lh * nseg;
     const int t = threadIdx.x, warp = t >> 5;
     const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
+    // A operand of a tile: this thread's pixel in every K chunk; the next tile's is loaded into
+    // registers while the current tile's MMA and epilogue run
+    uint4 pre[KCH];
+    auto fetch = [&](long long tile) {
+        const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
+        const int xc = min(seg * kM + t, lw - 1);
+#pragma unroll
+        for (int c = 0; c < KCH; ++c) pre[c] = *cp_at(encu, r, lh, y, KCH, c, lw, xc);
+    };
+    if (blockIdx.x < ntiles) fetch(blockIdx.x);
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
-        const int x = seg * kM + t, xc = min(x, lw - 1);
+        const int x = seg * kM + t;
 #pragma unroll
-        for (int c = 0; c < KCH; ++c)
-            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(encu, r, lh, y, KCH, c, lw, xc);
+        for (int c = 0; c < KCH; ++c) *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = pre[c];
         fence_async_smem();
         __syncthreads();
         if (t == 0) {
@@ -247,6 +256,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
             }
             commit(&s_bar);
         }
+        if (tile + gridDim.x < ntiles) fetch(tile + gridDim.x);
         if (!mma_wait_all(&s_bar, phase, err)) break;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -279,7 +289,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
 // Output channel order of B is phase-major (n = phase*32 + c), so TMEM columns
 // [32p, 32p+32) are the 32 channels of output pixel (2y + p/2, 2x + p%2).
 template <bool FP8>
-__global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
+__global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
                                                         const void* __restrict__ low, const void* __restrict__ enc540,
                                                         void* __restrict__ dec, int* err) {
     constexpr int KCH = FP8 ? 4 : 8;   // chunks of K = 64
@@ -301,12 +311,21 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
     const long long ntiles = (long long)rs.R * lh * nseg;
     const int t = threadIdx.x, warp = t >> 5;
     const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
+    // A operand of a tile: this thread's pixel in every K chunk; the next tile's is loaded into
+    // registers while the current tile's MMA and epilogue run
+    uint4 pre[KCH];
+    auto fetch = [&](long long tile) {
+        const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
+        const int xc = min(seg * kM + t, lw - 1);
+#pragma unroll
+        for (int c = 0; c < KCH; ++c) pre[c] = *cp_at(low, r, lh, y, KCH, c, lw, xc);
+    };
+    if (blockIdx.x < ntiles) fetch(blockIdx.x);
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
         const int x = seg * kM + t, xc = min(x, lw - 1);
 #pragma unroll
-        for (int c = 0; c < KCH; ++c)
-            *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = *cp_at(low, r, lh, y, KCH, c, lw, xc);
+        for (int c = 0; c < KCH; ++c) *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = pre[c];
         fence_async_smem();
         __syncthreads();
         if (t == 0) {
@@ -319,17 +338,21 @@ __global__ void __launch_bounds__(kThreads) k_tc_expand(RegionSet rs, const uint
             }
             commit(&s_bar);
         }
+        // skip values of the tile's four output pixels, in flight during the MMA
+        uint4 sk[4][4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) sk[p][c] = *cp_at(enc540, r, ph, 2 * y + (p >> 1), 4, c, pw, 2 * xc + (p & 1));
+        if (tile + gridDim.x < ntiles) fetch(tile + gridDim.x);
         if (!mma_wait_all(&s_bar, phase, err)) break;
-#pragma unroll 1
+#pragma unroll
         for (int p = 0; p < 4; ++p) {
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + p * 32, v);
             if (x < lw) {
                 const int oy = 2 * y + (p >> 1), ox = 2 * x + (p & 1);
-                uint4 sk[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) sk[c] = *cp_at(enc540, r, ph, oy, 4, c, pw, ox);
-                const __half* skh = reinterpret_cast<const __half*>(sk);
+                const __half* skh = reinterpret_cast<const __half*>(sk[p]);
 #pragma unroll
                 for (int n = 0; n < 32; ++n) {
                     const int col = p * 32 + n;
