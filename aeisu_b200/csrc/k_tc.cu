@@ -42,13 +42,15 @@ using namespace tcd;
 
 // ---- stage 1: feature analysis + unshuffle + project_540 ------------------------------------
 // Work item: a strip of 128 packed pixels and a band of packed rows.  The LR source rows the
-// strip needs (2qy-1 .. 2qy+2, 258 columns) slide through a 6-row ring in shared memory as
-// (r, g, b, luma) float4, so each source pixel is read and mixed once per strip; the next two
-// rows are loaded into registers while the current row's features and MMA run.
+// strip needs (2qy-1 .. 2qy+2, 258 columns) slide through an 8-row ring in shared memory as
+// (r, g, b, luma) float4, so each source pixel is read and mixed once per strip.  Per packed
+// row qy: the raw loads of rows 2qy+5, 2qy+6 are issued, the features of row qy are computed
+// into the A operand, the rows loaded during the previous step enter the ring, one barrier,
+// then the MMA of row qy runs while the epilogue of row qy-1 drains the other TMEM buffer.
 // A = 32 features (f16) of the strip's packed pixels; B = project weights [32][32].
 // Writes enc540 (f16, 4 chunks, packed grid: the skip input of expand) and the compress
 // input at low resolution, unshuffled with K order phase*32 + c (f16: 16 chunks, e4m3: 8).
-constexpr int kProjRing = 6;
+constexpr int kProjRing = 8;
 constexpr int kProjTW = 2 * kM + 2;   // 258 LR columns per strip
 
 template <bool FP8>
@@ -56,122 +58,84 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                                                          const uint8_t* __restrict__ wimg, const float* __restrict__ bias,
                                                          float slope, float inv_s1, void* __restrict__ enc540,
                                                          void* __restrict__ encu, int band, int* err) {
-    __shared__ alignas(128) uint8_t sA[4 * kM * 16];
-    __shared__ alignas(128) uint8_t sB[4 * 32 * 16];
-    __shared__ float4 s_src[kProjRing][kProjTW];
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* sA = smem;                                        // [2][4 chunks][128][16 B]
+    uint8_t* sB = smem + 2 * 4 * kM * 16;                      // [4][32][16 B]
+    float4 (*s_src)[kProjTW] = reinterpret_cast<float4 (*)[kProjTW]>(sB + 4 * 32 * 16);
     __shared__ float s_st[24];
     __shared__ float s_bias[32];
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar;
-    copy_image(sB, wimg, sizeof(sB));
+    __shared__ alignas(8) uint64_t s_bar[2];
+    copy_image(sB, wimg, 4 * 32 * 16);
     if (threadIdx.x < 24) s_st[threadIdx.x] = stencil[threadIdx.x];
     if (threadIdx.x < 32) s_bias[threadIdx.x] = bias[threadIdx.x];
     fill_lut(s_lut);
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 1, 32);
+    cta_setup(&s_tmem, s_bar, 2, 64);
     const uint32_t tmem = s_tmem;
-    uint32_t phase = 0;
+    uint32_t phase = 0, pend = 0;   // bit b: parity of buffer b's next commit / a commit not yet waited for
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
     const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5;
     const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
     constexpr int PER = (kProjTW + kThreads - 1) / kThreads;   // staged columns per thread (3)
-    auto slot = [](int row) { return (row + 4 * kProjRing) % kProjRing; };
     bool ok = true;
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
         const StripBand sb = strip_band(item, nstrip, nband, band, ph);
         const int4 reg = rs.regions[sb.r];
-        // source pixel (region-local LR row, strip column c) -> (r, g, b, luma)
-        auto fetch = [&](int row, int c) {
-            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(2 * sb.x0 - 1 + c, 0, rs.rw - 1);
-            const float3 v = load_src(src, reg.x, reg.y + ly, reg.z + lx, s_lut);
-            return make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
-        };
-        auto fetch_raw = [&](int row, int c) {
-            const int ly = clampi(row, 0, rs.rh - 1), lx = clampi(2 * sb.x0 - 1 + c, 0, rs.rw - 1);
-            return fetch_src_raw(src, reg.x, reg.y + ly, reg.z + lx);
-        };
-        for (int row = 2 * sb.y0 - 1; row <= 2 * sb.y0 + 2; ++row)
-            for (int c = t; c < kProjTW; c += kThreads) s_src[slot(row)][c] = fetch(row, c);
-        __syncthreads();
-        for (int qy = sb.y0; qy < sb.y1; ++qy) {
-            // prefetch the two source rows the next packed row adds
-            uint3 pre[2][PER];
-            const bool more = qy + 1 < sb.y1;
-            if (more)
+        const int base_row = 2 * sb.y0 - 1;
+        auto slot = [&](int row) { return (row - base_row) & (kProjRing - 1); };
+        // source columns this thread stages, clamped once per item
+        int sx[PER];
 #pragma unroll
-                for (int k = 0; k < 2; ++k)
-#pragma unroll
-                    for (int j = 0; j < PER; ++j)
-                        if (t + j * kThreads < kProjTW) pre[k][j] = fetch_raw(2 * qy + 3 + k, t + j * kThreads);
-            // features of packed pixel (qy, qx), exactly as the FP32 route
-            const int qx = sb.x0 + t, lc = 2 * (min(qx, pw - 1) - sb.x0);   // strip column of LR 2qx-1
-            float g[4][4];
-            float3 rgb[2][2];
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const float4 v = s_src[slot(2 * qy - 1 + a)][lc + b];
-                    g[a][b] = v.w;
-                    if (a >= 1 && a <= 2 && b >= 1 && b <= 2) rgb[a - 1][b - 1] = make_float3(v.x, v.y, v.z);
-                }
-            float f[32];
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int p = i * 2 + j;
-                    const float3 c = rgb[i][j];
-                    f[0 * 4 + p] = mix3(c.x, c.y, c.z, s_st[0], s_st[1], s_st[2]);
-                    f[1 * 4 + p] = mix3(c.x, c.y, c.z, s_st[3], s_st[4], s_st[5]);
-                    f[2 * 4 + p] = mix3(c.x, c.y, c.z, s_st[6], s_st[7], s_st[8]);
-                    f[3 * 4 + p] = g[i + 1][j + 1];
-                    const float ul = g[i][j], uc = g[i][j + 1], ur = g[i][j + 2];
-                    const float cl = g[i + 1][j], cr = g[i + 1][j + 2];
-                    const float dl = g[i + 2][j], dc = g[i + 2][j + 1], dr = g[i + 2][j + 2];
-                    const float hmid = __fsub_rn(cr, cl), vmid = __fsub_rn(dc, uc);
-                    f[4 * 4 + p] = mix3(__fsub_rn(ur, ul), hmid, __fsub_rn(dr, dl), s_st[12], s_st[13], s_st[14]);
-                    f[5 * 4 + p] = mix3(__fsub_rn(dl, ul), vmid, __fsub_rn(dr, ur), s_st[15], s_st[16], s_st[17]);
-                    f[6 * 4 + p] = mix3(__fsub_rn(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
-                    f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
-                                             __fmul_rn(hmid, s_st[23]));
-                }
-            uint4 fa[4];
-            pack_f16x32(f, fa);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sA + (c * kM + t) * 16) = fa[c];
-            fence_async_smem();
-            __syncthreads();
-            if (t == 0) {
-                fence_after_sync();
-                constexpr uint32_t idesc = idesc_m128(32);
-#pragma unroll
-                for (int k = 0; k < 2; ++k)
-                    mma_f16(tmem, sdesc(a0 + k * 2 * kM * 16, kM * 16, 128), sdesc(b0 + k * 2 * 32 * 16, 32 * 16, 128),
-                            idesc, k);
-                commit(&s_bar);
+        for (int j = 0; j < PER; ++j)
+            sx[j] = clampi(reg.z + clampi(2 * sb.x0 - 1 + t + j * kThreads, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+        auto raw_at = [&](int row, int j) -> uint3 {
+            const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
+            if (src.kind == 0) {
+                const uint8_t* p = static_cast<const uint8_t*>(src.ptr) + ((size_t(reg.x) * src.H + sy) * src.W + sx[j]) * 3;
+                return make_uint3(p[0], p[1], p[2]);
             }
-            if (more)
+            const size_t plane = size_t(src.H) * src.W;
+            const float* p = static_cast<const float*>(src.ptr) + size_t(reg.x) * 3 * plane + size_t(sy) * src.W + sx[j];
+            return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
+        };
+        auto put = [&](int row, int j, uint3 raw) {
+            const float3 v = finish_src(src, raw, s_lut);
+            s_src[slot(row)][t + j * kThreads] = make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
+        };
+        auto fetch2 = [&](int row, uint3 (&pre)[2][PER]) {   // raw loads of rows row, row+1
 #pragma unroll
-                for (int k = 0; k < 2; ++k)
+            for (int k = 0; k < 2; ++k)
 #pragma unroll
-                    for (int j = 0; j < PER; ++j)
-                        if (t + j * kThreads < kProjTW) {
-                            const float3 v = finish_src(src, pre[k][j], s_lut);
-                            s_src[slot(2 * qy + 3 + k)][t + j * kThreads] =
-                                make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
-                        }
-            if (!mma_wait_all(&s_bar, phase, err)) { ok = false; break; }
+                for (int j = 0; j < PER; ++j)
+                    if (t + j * kThreads < kProjTW) pre[k][j] = raw_at(row + k, j);
+        };
+        auto put2 = [&](int row, const uint3 (&pre)[2][PER]) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                for (int j = 0; j < PER; ++j)
+                    if (t + j * kThreads < kProjTW) put(row + k, j, pre[k][j]);
+        };
+        // epilogue of packed row qy from TMEM buffer b: enc540 and the compress input
+        auto epilogue = [&](int qy, int b) {
+            bool good = mbar_wait_bounded(&s_bar[b], (phase >> b) & 1u, err, kErrTimeout);
+            if (good) {
+                phase ^= 1u << b;
+                pend &= ~(1u << b);
+            }
+            fence_after_sync();
+            const int qx = sb.x0 + t;
             float v[32];
-            tmem_ld32(tmem + (uint32_t(32 * warp) << 16), v);
+            tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 32, v);
 #pragma unroll
             for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_bias[n], slope);
             uint4 o[4];
             pack_f16x32(v, o);
-            if (qx < pw) {
+            if (qx < pw && good) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) *cp_at(enc540, sb.r, ph, qy, 4, c, pw, qx) = o[c];
                 const int p = (qy & 1) * 2 + (qx & 1);
@@ -196,11 +160,86 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                     for (int c = 0; c < 4; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 16, p * 4 + c, lw, qx >> 1) = o[c];
                 }
             }
+            return good;
+        };
+        // prologue: rows 2y0-1 .. 2y0+2 converted now, rows 2y0+3, 2y0+4 in flight
+        for (int row = base_row; row <= 2 * sb.y0 + 2; ++row)
+#pragma unroll
+            for (int j = 0; j < PER; ++j)
+                if (t + j * kThreads < kProjTW) put(row, j, raw_at(row, j));
+        uint3 pre_cur[2][PER];
+        if (sb.y0 + 1 < sb.y1) fetch2(2 * sb.y0 + 3, pre_cur);
+        __syncthreads();
+        for (int qy = sb.y0; qy < sb.y1; ++qy) {
+            const int b = (qy - sb.y0) & 1;
+            uint3 pre_next[2][PER];
+            if (qy + 2 < sb.y1) fetch2(2 * qy + 5, pre_next);
+            // features of packed pixel (qy, qx), exactly as the FP32 route
+            const int qx = sb.x0 + t, lc = 2 * (min(qx, pw - 1) - sb.x0);   // strip column of LR 2qx-1
+            float g[4][4];
+            float3 rgb[2][2];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float4 v = s_src[slot(2 * qy - 1 + a)][lc + c];
+                    g[a][c] = v.w;
+                    if (a >= 1 && a <= 2 && c >= 1 && c <= 2) rgb[a - 1][c - 1] = make_float3(v.x, v.y, v.z);
+                }
+            float f[32];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int p = i * 2 + j;
+                    const float3 c = rgb[i][j];
+                    f[0 * 4 + p] = mix3(c.x, c.y, c.z, s_st[0], s_st[1], s_st[2]);
+                    f[1 * 4 + p] = mix3(c.x, c.y, c.z, s_st[3], s_st[4], s_st[5]);
+                    f[2 * 4 + p] = mix3(c.x, c.y, c.z, s_st[6], s_st[7], s_st[8]);
+                    f[3 * 4 + p] = g[i + 1][j + 1];
+                    const float ul = g[i][j], uc = g[i][j + 1], ur = g[i][j + 2];
+                    const float cl = g[i + 1][j], cr = g[i + 1][j + 2];
+                    const float dl = g[i + 2][j], dc = g[i + 2][j + 1], dr = g[i + 2][j + 2];
+                    const float hmid = __fsub_rn(cr, cl), vmid = __fsub_rn(dc, uc);
+                    f[4 * 4 + p] = mix3(__fsub_rn(ur, ul), hmid, __fsub_rn(dr, dl), s_st[12], s_st[13], s_st[14]);
+                    f[5 * 4 + p] = mix3(__fsub_rn(dl, ul), vmid, __fsub_rn(dr, ur), s_st[15], s_st[16], s_st[17]);
+                    f[6 * 4 + p] = mix3(__fsub_rn(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
+                    f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
+                                             __fmul_rn(hmid, s_st[23]));
+                }
+            uint4 fa[4];
+            pack_f16x32(f, fa);
+            uint8_t* a_b = sA + b * 4 * kM * 16;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a_b + (c * kM + t) * 16) = fa[c];
+            // rows 2qy+3, 2qy+4 (loaded during the previous step) enter the ring for row qy+1
+            if (qy + 1 < sb.y1) put2(2 * qy + 3, pre_cur);
+            fence_async_smem();
             fence_before_sync();
-            __syncthreads();
+            if (__syncthreads_or(!ok)) { ok = false; break; }   // also spreads an epilogue failure
+            if (t == 0) {
+                fence_after_sync();
+                constexpr uint32_t idesc = idesc_m128(32);
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+                    mma_f16(tmem + b * 32, sdesc(a0 + b * 4 * kM * 16 + k * 2 * kM * 16, kM * 16, 128),
+                            sdesc(b0 + k * 2 * 32 * 16, 32 * 16, 128), idesc, k);
+                commit(&s_bar[b]);
+                pend |= 1u << b;
+            }
+            if (qy > sb.y0 && !epilogue(qy - 1, b ^ 1)) ok = false;
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                for (int j = 0; j < PER; ++j) pre_cur[k][j] = pre_next[k][j];
         }
+        if (ok && sb.y1 > sb.y0 && !epilogue(sb.y1 - 1, (sb.y1 - 1 - sb.y0) & 1)) ok = false;
+        if (__syncthreads_or(!ok)) ok = false;
     }
-    cta_teardown(tmem, 32);
+    if (!ok && t == 0)   // abort path: let committed MMAs land before TMEM is freed
+        for (int b = 0; b < 2; ++b)
+            if (pend & (1u << b)) mbar_wait_bounded(&s_bar[b], (phase >> b) & 1u, err, kErrTimeout, 200000000LL);
+    cta_teardown(tmem, 64);
 }
 
 // ---- 1x1 convolutions at low resolution --------------------------------------------------------
@@ -1028,8 +1067,9 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
         const int band = pick_band(strips, ph, sms * 4);
         const long long items = strips * ((ph + band - 1) / band);
-        if (fp8) k_tc_project<true><<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err);
-        else k_tc_project<false><<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err);
+        const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;
+        if (fp8) { smem_attr(k_tc_project<true>, bytes); k_tc_project<true><<<grid_for(items, 4, sms), kThreads, bytes, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err); }
+        else { smem_attr(k_tc_project<false>, bytes); k_tc_project<false><<<grid_for(items, 4, sms), kThreads, bytes, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err); }
     }
     mark(1);
     {
