@@ -521,13 +521,13 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             const StripBand sb = strip_band(item, nstrip, nband, band, lh);
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
-            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = ring.wait(row, err);
+            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
             for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
                 const int b = it & 1;
                 const uint32_t k = it >> 1;
                 // buffer b free (its previous row drained) and input row y+1 landed
-                if (k > 0) ok = mbar_wait_bounded(&acc_empty[b], (k - 1) & 1, err, kErrTimeout);
-                if (ok) ok = ring.wait(y + 1, err);
+                if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_empty[b], (k - 1) & 1, err, kErrTimeout));
+                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
                 if (!ok) break;
                 fence_after_sync();
                 if (leader) {
@@ -554,7 +554,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                 pend |= 1u << b;
                 // refill the slot of row y-1 with row y+3 once MMA(y) has read it
                 if (y + 3 <= sb.y1) {
-                    ok = mbar_wait_bounded(&acc_full[b], k & 1, err, kErrTimeout);
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[b], k & 1, err, kErrTimeout));
                     if (!ok) break;
                     pend &= ~(1u << b);
                     load(y + 3, sb);
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
             const int x = sb.x0 + t;
             for (int y = sb.y0; y < sb.y1; ++y, ++it) {
                 const int b = it & 1;
-                ok = mbar_wait_bounded(&acc_full[b], (it >> 1) & 1, err, kErrTimeout);
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[b], (it >> 1) & 1, err, kErrTimeout));
                 if (!ok) break;
                 fence_after_sync();
 #pragma unroll
@@ -678,8 +678,8 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
         auto tail = [&](uint32_t row_it) {   // tail GEMM of the row with counter row_it
             const int pb = row_it & 1;
             const uint32_t pk = row_it >> 1;
-            ok = mbar_wait_bounded(&a2_full[pb], pk & 1, err, kErrTimeout);
-            if (ok && pk > 0) ok = mbar_wait_bounded(&tail_empty[pb], (pk - 1) & 1, err, kErrTimeout);
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&a2_full[pb], pk & 1, err, kErrTimeout));
+            if (ok && pk > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_empty[pb], (pk - 1) & 1, err, kErrTimeout));
             if (!ok) return;
             fence_after_sync();
             if (leader) {
@@ -696,12 +696,12 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             const StripBand sb = strip_band(item, nstrip, nband, band, ph);
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
-            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = ring.wait(row, err);
+            for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
             for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
                 const int b = it & 1;
                 const uint32_t k = it >> 1;
-                if (k > 0) ok = mbar_wait_bounded(&ref_empty[b], (k - 1) & 1, err, kErrTimeout);
-                if (ok) ok = ring.wait(y + 1, err);
+                if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_empty[b], (k - 1) & 1, err, kErrTimeout));
+                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
                 if (!ok) break;
                 fence_after_sync();
                 if (leader) {
@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
                     if (!ok) break;
                 }
                 if (y + 3 <= sb.y1) {   // refill the slot of row y-1 once refine(y) has read it
-                    ok = mbar_wait_bounded(&ref_full[b], k & 1, err, kErrTimeout);
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[b], k & 1, err, kErrTimeout));
                     if (!ok) break;
                     pend &= ~(1u << b);
                     load(y + 3, sb);
@@ -750,7 +750,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
             for (int y = sb.y0; y <= sb.y1 && ok; ++y) {
                 if (y < sb.y1) {
                     const int b = it & 1;
-                    ok = mbar_wait_bounded(&ref_full[b], (it >> 1) & 1, err, kErrTimeout);
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[b], (it >> 1) & 1, err, kErrTimeout));
                     if (!ok) break;
                     fence_after_sync();
                     float vr[2][32];
@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
                 if (y > sb.y0) {   // tail epilogue of row y-1
                     const uint32_t pit = it - 1 - (y < sb.y1 ? 1 : 0);
                     const int pb = pit & 1, yt = y - 1;
-                    ok = mbar_wait_bounded(&tail_full[pb], (pit >> 1) & 1, err, kErrTimeout);
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[pb], (pit >> 1) & 1, err, kErrTimeout));
                     if (!ok) break;
                     fence_after_sync();
                     float vt[2][32];
