@@ -830,6 +830,8 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
 // TMEM waits hide behind the others' FMAs.
 constexpr int kHeadRing = 8;
 constexpr int kHeadTW = kM + 4;
+constexpr int kHeadBCH = 2 * 128 * 16;   // one B operand: 2 chunks x 128 rows
+constexpr int kHeadSmem = 3 * kHeadBCH + 2 * 2 * kM * 16 + 2 * kM * 16 + kHeadRing * 3 * kHeadTW * 8;
 
 // floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add (runtime.py:24-25 in
 // float32), for two values at once (packed f32x2 arithmetic rounds each lane as the scalar
@@ -844,11 +846,14 @@ __device__ __forceinline__ uint2 u8_code_bits2(float a, float b) {
 __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
                                                       const void* __restrict__ meta, const uint8_t* __restrict__ bimg,
                                                       int band, int* nonfinite, int* err) {
-    constexpr int BCH = 2 * 128 * 16;   // one B operand: 2 chunks x 128 rows
-    __shared__ alignas(128) uint8_t sA[2][2 * kM * 16];
-    __shared__ alignas(128) uint8_t sOnes[2 * kM * 16];
-    __shared__ alignas(128) uint8_t sB[3 * BCH];
-    __shared__ float4 s_src[kHeadRing][kHeadTW];
+    constexpr int BCH = kHeadBCH;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* sB = smem_raw;                                   // basis hi, basis lo, base
+    uint8_t (*sA)[2 * kM * 16] = reinterpret_cast<uint8_t (*)[2 * kM * 16]>(sB + 3 * BCH);   // [2 rows]
+    uint8_t* sOnes = sB + 3 * BCH + 2 * 2 * kM * 16;          // [2 chunks][128][16 B]
+    // source ring, per slot and channel the pairs (s[x], s[x+1]) of adjacent columns, so a
+    // horizontal tap pair is one 8-byte load that feeds packed f32x2 FMAs directly
+    float2 (*s_pair)[3][kHeadTW] = reinterpret_cast<float2 (*)[3][kHeadTW]>(sOnes + 2 * kM * 16);
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
@@ -904,9 +909,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
         };
         auto slot = [&](int row) { return (row - y0 + 2) & (kHeadRing - 1); };
-        auto put = [&](int row, int j, uint3 raw) {
+        auto put = [&](int row, int j, uint3 raw) {   // value of column col: first of pair col, second of col-1
             const float3 v = finish_src(src, raw, s_lut);
-            s_src[slot(row)][t + j * kThreads] = make_float4(v.x, v.y, v.z, 0.f);
+            const int col = t + j * kThreads;
+            float2(&ps)[3][kHeadTW] = s_pair[slot(row)];
+            ps[0][col].x = v.x; ps[1][col].x = v.y; ps[2][col].x = v.z;
+            if (col > 0) { ps[0][col - 1].y = v.x; ps[1][col - 1].y = v.y; ps[2][col - 1].y = v.z; }
         };
         // coefficients of row y: meta[r][y][chunk][X][16 B], X = this thread's column
         const uint8_t* cbase = static_cast<const uint8_t*>(meta) +
@@ -945,34 +953,57 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                 pend = false;
             }
             fence_after_sync();
-            // epilogue: apply the 25 x 4 filter weights of this pixel
-            float acc[4][3] = {};
+            // apply the 25 x 4 filter weights of this pixel.  acc[p][ch] is a pair of partial sums
+            // (taps with even kx and the fifth column | taps with odd kx); TMEM columns: tap
+            // pairs (ky, 0|1) and (ky, 2|3) at (ky*2 + j)*8 + phase*2 + lane, then (ky, 4) at
+            // 80 + ky*4 + phase
+            float2 acc[4][3];
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+#pragma unroll
+                for (int ch = 0; ch < 3; ++ch) acc[p][ch] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 float w[32];
                 tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + q * 32, w);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int tap = q * 8 + j;
-                    if (tap < 25) {
-                        const float4 s = s_src[slot(y - 2 + tap / 5)][t + tap % 5];
+                for (int i = 0; i < 32; ++i) {
+                    const int n = q * 32 + i;
+                    if (n < 80 && i % 8 == 0) {   // tap pair (ky, 2j), (ky, 2j+1): 12 packed FMAs
+                        const int pair = n / 8, ky = pair / 2, j = pair % 2;
+                        const float2(&ps)[3][kHeadTW] = s_pair[slot(y - 2 + ky)];
 #pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            acc[p][0] = fmaf(s.x, w[j * 4 + p], acc[p][0]);
-                            acc[p][1] = fmaf(s.y, w[j * 4 + p], acc[p][1]);
-                            acc[p][2] = fmaf(s.z, w[j * 4 + p], acc[p][2]);
+                        for (int ch = 0; ch < 3; ++ch) {
+                            const float2 sv = ps[ch][t + 2 * j];
+#pragma unroll
+                            for (int p = 0; p < 4; ++p)
+                                acc[p][ch] = __ffma2_rn(sv, make_float2(w[i + 2 * p], w[i + 2 * p + 1]), acc[p][ch]);
+                        }
+                    } else if (n >= 80 && n < 100 && (n - 80) % 4 == 0) {   // tap (ky, 4): 12 FMAs
+                        const int ky = (n - 80) / 4;
+                        const float2(&ps)[3][kHeadTW] = s_pair[slot(y - 2 + ky)];
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch) {
+                            const float sv = ps[ch][t + 4].x;
+#pragma unroll
+                            for (int p = 0; p < 4; ++p) acc[p][ch].x = fmaf(sv, w[i + p], acc[p][ch].x);
                         }
                     }
                 }
             }
+            float out[4][3];
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+#pragma unroll
+                for (int ch = 0; ch < 3; ++ch) out[p][ch] = acc[p][ch].x + acc[p][ch].y;
             // each thread stores its own 2x2 output pixels: 6 bytes per output row as three
             // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
             // floats per channel plane
             if (x0 + t < xe) {
                 // one test for all twelve values: a non-finite term makes the sum non-finite
-                float2 all = __fadd2_rn(make_float2(acc[0][0], acc[0][1]), make_float2(acc[0][2], acc[1][0]));
-                all = __fadd2_rn(all, __fadd2_rn(make_float2(acc[1][1], acc[1][2]), make_float2(acc[2][0], acc[2][1])));
-                all = __fadd2_rn(all, __fadd2_rn(make_float2(acc[2][2], acc[3][0]), make_float2(acc[3][1], acc[3][2])));
+                float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
+                all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
+                all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
                 if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
                 const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
 #pragma unroll
@@ -983,12 +1014,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                         for (int ch = 0; ch < 3; ++ch)
                             *reinterpret_cast<float2*>(static_cast<float*>(dst.ptr) +
                                                        ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
-                                make_float2(acc[2 * i][ch], acc[2 * i + 1][ch]);
+                                make_float2(out[2 * i][ch], out[2 * i + 1][ch]);
                     } else {
                         // bytes r0 g0 b0 r1 g1 b1 of the two output pixels (phases 2i, 2i+1)
-                        const uint2 q01 = u8_code_bits2(acc[2 * i][0], acc[2 * i][1]);
-                        const uint2 q23 = u8_code_bits2(acc[2 * i][2], acc[2 * i + 1][0]);
-                        const uint2 q45 = u8_code_bits2(acc[2 * i + 1][1], acc[2 * i + 1][2]);
+                        const uint2 q01 = u8_code_bits2(out[2 * i][0], out[2 * i][1]);
+                        const uint2 q23 = u8_code_bits2(out[2 * i][2], out[2 * i + 1][0]);
+                        const uint2 q45 = u8_code_bits2(out[2 * i + 1][1], out[2 * i + 1][2]);
                         uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
                                                                   ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
                         o[0] = uint16_t(__byte_perm(q01.x, q01.y, 0x0040));
@@ -1124,7 +1155,8 @@ void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst,
     const long long strips = (long long)rs.R * ((rs.core_w + kM - 1) / kM);
     const int band = pick_band_balanced(strips, rs.core_h, sms * 4);
     const long long items = strips * ((rs.core_h + band - 1) / band);
-    k_tc_head<<<grid_for(items, 4, sms), kThreads, 0, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
+    smem_attr(k_tc_head, kHeadSmem);
+    k_tc_head<<<grid_for(items, 4, sms), kThreads, kHeadSmem, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
     AEISU_CUDA(cudaGetLastError());
     *launches += 1;
 }

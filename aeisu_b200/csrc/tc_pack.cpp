@@ -112,19 +112,38 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         for (int i = 0; i < 64; ++i) tb[i] = round_f16(T.bias[i]);  // f16 tail bias (Refine.cuh:494-495)
         P.tail_bias = append_floats(P.floats, tb);
     }
-    // head: column n = tap*4 + phase (100 used of 128); FP32 bank split into hi + lo f16
+    // head: 100 of 128 columns, FP32 bank split into hi + lo f16.  Columns 0..79 hold the
+    // horizontally paired taps (ky, 2j) and (ky, 2j+1), j = 0, 1, as n = (ky*2 + j)*8 +
+    // phase*2 + (kx & 1), so one packed f32x2 FMA applies both taps of a pair; columns 80..99
+    // hold the fifth column's taps (ky, 4) as n = 80 + ky*4 + phase.
     {
+        auto tap_phase = [](int n, int& tap, int& phase) {
+            if (n < 80) {
+                const int pair = n / 8;
+                phase = (n / 2) % 4;
+                tap = (pair / 2) * 5 + (pair % 2) * 2 + n % 2;
+                return true;
+            }
+            if (n < 100) {
+                phase = (n - 80) % 4;
+                tap = ((n - 80) / 4) * 5 + 4;
+                return true;
+            }
+            return false;
+        };
         auto bank = [&](int n, int k, bool lo) -> uint32_t {
-            if (n >= 100) return 0;
-            const float v = m.basis[((n / 4) * 16 + k) * 4 + n % 4];
+            int tap, phase;
+            if (!tap_phase(n, tap, phase)) return 0;
+            const float v = m.basis[(tap * 16 + k) * 4 + phase];
             const uint16_t hi = f32_to_f16_bits(v);
             return lo ? f32_to_f16_bits(v - f16_bits_to_f32(hi)) : hi;
         };
         auto hi = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, false); });
         auto lo = pack_operand(128, 16, 2, [&](int n, int k) { return bank(n, k, true); });
         auto base = pack_operand(128, 16, 2, [&](int n, int k) -> uint32_t {
-            if (n >= 100 || k > 1) return 0;
-            const float v = m.base[(n / 4) * 4 + n % 4];
+            int tap, phase;
+            if (!tap_phase(n, tap, phase) || k > 1) return 0;
+            const float v = m.base[tap * 4 + phase];
             const uint16_t h = f32_to_f16_bits(v);
             return k == 0 ? h : f32_to_f16_bits(v - f16_bits_to_f32(h));
         });
