@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <utility>
 
 #include "common.h"
 #include "kernels.h"
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
     constexpr int PER = (kProjTW + kThreads - 1) / kThreads;   // staged columns per thread (3)
     bool ok = true;
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        last_item(item, items);
         const StripBand sb = strip_band(item, nstrip, nband, band, ph);
         const int4 reg = rs.regions[sb.r];
         const int base_row = 2 * sb.y0 - 1;
@@ -279,6 +281,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
     };
     if (blockIdx.x < ntiles) fetch(blockIdx.x);
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        last_item(tile, ntiles);
         const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
         const int x = seg * kM + t;
 #pragma unroll
@@ -361,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
     };
     if (blockIdx.x < ntiles) fetch(blockIdx.x);
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        last_item(tile, ntiles);
         const int seg = int(tile % nseg), y = int((tile / nseg) % lh), r = int(tile / ((long long)nseg * lh));
         const int x = seg * kM + t, xc = min(x, lw - 1);
 #pragma unroll
@@ -519,6 +523,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
             ring.pending |= 1u << Ring::slot(row);
         };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh);
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
@@ -574,6 +579,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         uint32_t it = 0;
         bool ok = true;
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh);
             const int x = sb.x0 + t;
             for (int y = sb.y0; y < sb.y1; ++y, ++it) {
@@ -694,6 +700,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
             last[2 + pb] = pk;
         };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph);
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
@@ -745,6 +752,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
         uint32_t it = 0;
         bool ok = true;
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+            last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph);
             const int x = sb.x0 + t;
             for (int y = sb.y0; y <= sb.y1 && ok; ++y) {
@@ -886,6 +894,8 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
     };
 
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+
+        last_item(item, items);
         const int r = int(item / ((long long)nstrip * nband));
         const int bi = int((item / nstrip) % nband), si = int(item % nstrip);
         const int4 core = rs.cores[r];
@@ -1067,6 +1077,29 @@ void smem_attr(K kernel, int bytes) {
     AEISU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
+// Programmatic stream serialisation for small calls: a kernel's CTAs may then start while the
+// previous kernel of the stream finishes its last work items; each loads its weights and takes
+// its TMEM, then waits for the previous kernel (cta_setup) before it reads any activation.  It
+// shortens a single frame's latency by the launch and set-up of every kernel, but costs
+// throughput on large batches (measured), so it is used up to a few frames' worth of pixels.
+bool use_pdl(const RegionSet& rs) { return (long long)rs.R * rs.rh * rs.rw <= (8ll << 20); }
+
+template <typename... KArgs, typename... Args>
+void launch(bool pdl, void (*kernel)(KArgs...), unsigned grid, unsigned block, int smem, cudaStream_t s,
+            Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    AEISU_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 // Rows per work item: enough items to fill every CTA slot, at most 32 rows.
 int pick_band(long long strips_x_regions, int rows, int slots) {
     const long long per_slot = (strips_x_regions * rows + slots - 1) / slots;
@@ -1092,6 +1125,7 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
                           int* err, cudaStream_t s, int* launches, const StageMark& mark) {
     const int sms = sm_count();
+    const bool pdl = use_pdl(rs);
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
     const long long low_tiles = (long long)rs.R * lh * ((lw + kM - 1) / kM);
     {
@@ -1099,15 +1133,15 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const int band = pick_band(strips, ph, sms * 4);
         const long long items = strips * ((ph + band - 1) / band);
         const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;
-        if (fp8) { smem_attr(k_tc_project<true>, bytes); k_tc_project<true><<<grid_for(items, 4, sms), kThreads, bytes, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err); }
-        else { smem_attr(k_tc_project<false>, bytes); k_tc_project<false><<<grid_for(items, 4, sms), kThreads, bytes, s>>>(src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err); }
+        if (fp8) { smem_attr(k_tc_project<true>, bytes); launch(pdl, k_tc_project<true>, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err); }
+        else { smem_attr(k_tc_project<false>, bytes); launch(pdl, k_tc_project<false>, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err); }
     }
     mark(1);
     {
         const int kch = fp8 ? 8 : 16;
         const int bytes = kch * kM * 16 + kch * 64 * 16 + 2 * 64 * 4;
-        if (fp8) { smem_attr(k_tc_compress<true>, bytes); k_tc_compress<true><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
-        else { smem_attr(k_tc_compress<false>, bytes); k_tc_compress<false><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.compress, w.compress_ep, encu, low_a, err); }
+        if (fp8) { smem_attr(k_tc_compress<true>, bytes); launch(pdl, k_tc_compress<true>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
+        else { smem_attr(k_tc_compress<false>, bytes); launch(pdl, k_tc_compress<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
     }
     {
         const int ich = fp8 ? 4 : 8;
@@ -1122,16 +1156,16 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const CUtensorMap* maps[2] = {&map_a, &map_b};
         if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) k_tc_core<true><<<grid_for(items, per_sm, sms), kWsThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else k_tc_core<false><<<grid_for(items, per_sm, sms), kWsThreads, bytes, s>>>(*maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            if (fp8) launch(pdl, k_tc_core<true>, grid_for(items, per_sm, sms), kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else launch(pdl, k_tc_core<false>, grid_for(items, per_sm, sms), kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);
     {
         const int kch = fp8 ? 4 : 8;
         const int bytes = kch * kM * 16 + kch * 128 * 16 + 2 * 128 * 4;
-        if (fp8) { smem_attr(k_tc_expand<true>, bytes); k_tc_expand<true><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
-        else { smem_attr(k_tc_expand<false>, bytes); k_tc_expand<false><<<grid_for(low_tiles, 4, sms), kThreads, bytes, s>>>(rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
+        if (fp8) { smem_attr(k_tc_expand<true>, bytes); launch(pdl, k_tc_expand<true>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
+        else { smem_attr(k_tc_expand<false>, bytes); launch(pdl, k_tc_expand<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
     }
     mark(3);
     {
@@ -1141,7 +1175,7 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const long long items = strips * ((ph + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
         smem_attr(k_tc_refine_tail, bytes);
-        k_tc_refine_tail<<<grid_for(items, 2, sms), kWsThreads, bytes, s>>>(map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
+        launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kWsThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;
@@ -1152,11 +1186,12 @@ void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst,
                     const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, int* launches) {
     if ((long long)rs.R * rs.core_h * rs.core_w == 0) return;
     const int sms = sm_count();
+    const bool pdl = use_pdl(rs);
     const long long strips = (long long)rs.R * ((rs.core_w + kM - 1) / kM);
     const int band = pick_band_balanced(strips, rs.core_h, sms * 4);
     const long long items = strips * ((rs.core_h + band - 1) / band);
     smem_attr(k_tc_head, kHeadSmem);
-    k_tc_head<<<grid_for(items, 4, sms), kThreads, kHeadSmem, s>>>(src, rs, dst, meta, head_img, band, nonfinite, err);
+    launch(pdl, k_tc_head, grid_for(items, 4, sms), kThreads, kHeadSmem, s, src, rs, dst, meta, head_img, band, nonfinite, err);
     AEISU_CUDA(cudaGetLastError());
     *launches += 1;
 }

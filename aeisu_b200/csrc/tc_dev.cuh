@@ -61,7 +61,12 @@ __device__ __forceinline__ void fill_lut(float* lut) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = __fdiv_rn(float(i), 255.f);
 }
 
-// Per-CTA set-up: TMEM columns (warp 0) and `nbar` mbarriers with arrival count 1.
+// Per-CTA set-up: TMEM columns (warp 0) and `nbar` mbarriers with arrival count 1.  Then the
+// kernel waits for the previous kernel of the stream (everything before this point reads only
+// the model's weights).  The next kernel may launch once every CTA of this one has called
+// last_item() (or exited): after its TMEM allocation, so a dependent CTA never takes TMEM
+// that a CTA of this kernel still needs, and only for the last work item, so the dependents
+// overlap this kernel's tail rather than occupy SMs for its whole duration.
 __device__ __forceinline__ void cta_setup(uint32_t* tmem_slot, uint64_t* bars, int nbar, uint32_t ncols) {
     if (threadIdx.x < 32) tmem_alloc(tmem_slot, ncols);
     if (threadIdx.x == 0) {
@@ -71,6 +76,12 @@ __device__ __forceinline__ void cta_setup(uint32_t* tmem_slot, uint64_t* bars, i
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    grid_dep_wait();
+}
+
+// Called by a CTA when it starts its last work item (see cta_setup).
+__device__ __forceinline__ void last_item(long long item, long long items) {
+    if (item + gridDim.x >= items) grid_dep_launch();
 }
 
 __device__ __forceinline__ void cta_teardown(uint32_t tmem, uint32_t ncols) {
