@@ -463,7 +463,7 @@ void Engine::run_pipelined(const Call& c, cudaStream_t s) {
         record(0, s);
         Call part = c;
         part.n = k;
-        const Geometry g = plan_upscale(k, c.h, c.w, c.tile);
+        const Geometry& g = plan(part);
         SrcDesc src{dsrc, 0, c.h, c.w, g.pad_y, g.pad_x};
         DstDesc dst{ddst, 0, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
         for (const auto& grp : g.groups) run_group(part, g, grp, src, dst, s);
@@ -488,12 +488,21 @@ void Engine::finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t
     if (flag[0] && c.mode == Mode::Upscale) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
 }
 
+const Geometry& Engine::plan(const Call& c) {
+    const std::array<int, 7> key{int(c.mode), c.n, c.h, c.w, c.tile, c.band, c.bands};
+    auto it = plan_cache_.find(key);
+    if (it != plan_cache_.end()) return it->second;
+    Geometry g = c.bands > 0                ? plan_band(c.h, c.w, c.band, c.bands)
+                 : (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile)
+                                             : plan_whole(c.n, c.h, c.w);
+    if (plan_cache_.size() >= 256) plan_cache_.clear();
+    return plan_cache_.emplace(key, std::move(g)).first->second;
+}
+
 void Engine::run(const Call& c) {
     DeviceGuard guard(device_);
     require(c.src != nullptr && c.dst != nullptr, "source and destination must not be null");
-    const Geometry g = c.bands > 0                ? plan_band(c.h, c.w, c.band, c.bands)
-                       : (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile)
-                                                   : plan_whole(c.n, c.h, c.w);
+    const Geometry& g = plan(c);
     cudaStream_t s = c.stream ? c.stream : stream_;
     if (c.bands == 0 && c.host && c.mode == Mode::Upscale && c.src_kind == 0 && c.dst_kind == 0 && c.n >= 2 &&
         is_pinned(c.src) && is_pinned(c.dst)) {

@@ -156,6 +156,9 @@ private:
     TcWeights tcw_{};
     size_t tc_head_off_ = 0;
 
+    // planned geometry per call shape (mode, n, h, w, tile, band, bands)
+    std::map<std::array<int, 7>, Geometry> plan_cache_;
+    const Geometry& plan(const Call& c);
     // region tables per call geometry (mode, n, h, w, tile, group shape, first region, band, bands)
     using TableKey = std::array<int, 9>;
     std::map<TableKey, std::unique_ptr<DevBuf>> table_cache_;

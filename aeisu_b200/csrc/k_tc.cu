@@ -28,6 +28,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <map>
+#include <mutex>
 #include <utility>
 
 #include "common.h"
@@ -1060,10 +1063,17 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
     cta_teardown(tmem, 128);
 }
 
+// Per-call host work is part of a frame's latency: device properties and kernel attributes are
+// looked up or set once per device.
 int sm_count() {
-    int dev = 0, n = 0;
+    static std::atomic<int> cache[64];
+    int dev = 0;
     AEISU_CUDA(cudaGetDevice(&dev));
-    AEISU_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    int n = (dev >= 0 && dev < 64) ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (n == 0) {
+        AEISU_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+    }
     return n;
 }
 
@@ -1074,7 +1084,15 @@ unsigned grid_for(long long tiles, int per_sm, int sms) {
 
 template <typename K>
 void smem_attr(K kernel, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;   // (kernel, device) -> bytes set
+    int dev = 0;
+    AEISU_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    int& have = done[{reinterpret_cast<const void*>(kernel), dev}];
+    if (have >= bytes) return;
     AEISU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    have = bytes;
 }
 
 // Programmatic stream serialisation for small calls: a kernel's CTAs may then start while the

@@ -3,8 +3,10 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "common.h"
 
@@ -30,6 +32,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, int win) {
     require(win >= 1 && win <= 256 && nch >= 1 && nch <= 256, "tensor map box out of range");
     require((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base must be 16-byte aligned");
+    // A map depends only on its arguments, and calls reuse the same workspace: encode each once.
+    using Key = std::tuple<const void*, int, int, int, int, int>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, R, H, nch, W, win};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
     CUtensorMap map{};
     const cuuint64_t dims[5] = {16, cuuint64_t(W), cuuint64_t(nch), cuuint64_t(H), cuuint64_t(R)};
     const cuuint64_t strides[4] = {16, cuuint64_t(W) * 16, cuuint64_t(nch) * W * 16, cuuint64_t(H) * nch * W * 16};
@@ -39,6 +51,9 @@ CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, 
                                    box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail(AEISU_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, map);
     return map;
 }
 
