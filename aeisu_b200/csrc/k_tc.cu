@@ -481,29 +481,36 @@ struct Ring {
 // producer refills the ring slot of row y-1 with row y+3 once MMA(y) has completed.
 constexpr int kWsThreads = 160;
 
-template <bool FP8>
+// NG = groups per CTA.  With NG = 1 the two groups (independent 32->32 convolutions) run in
+// separate CTAs (even blockIdx: group 0, odd: group 1), each staging only its group's input
+// channels and weights: half the shared memory, so twice the CTAs per SM (the FP16 route).
+template <bool FP8, int NG>
 __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                         const uint8_t* __restrict__ wimg, EpiParams ep,
                                                         void* __restrict__ out, int band, int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
     constexpr int CPG = ICH / 2;              // chunks per group
-    constexpr int WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
+    constexpr int RCH = NG * CPG;             // chunks staged per row
+    constexpr int ACC = NG * 32;              // TMEM columns of one accumulator buffer
+    constexpr int WIN = kM + 2, LBO = WIN * 16, SLOT = RCH * LBO;
     constexpr int BG = 9 * CPG * 32 * 16;     // bytes of one group's weights
+    const int gb = NG == 2 ? 0 : int(blockIdx.x & 1);                     // first group of this CTA
+    const long long cta = NG == 2 ? blockIdx.x : blockIdx.x >> 1, stride = NG == 2 ? gridDim.x : gridDim.x >> 1;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;
-    float* s_scale = reinterpret_cast<float*>(sB + 2 * BG);
+    float* s_scale = reinterpret_cast<float*>(sB + NG * BG);
     float* s_bias = s_scale + 64;
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar[kRing + 4];   // ring slots, acc_full x2, acc_empty x2
     uint64_t* acc_full = s_bar + kRing;
     uint64_t* acc_empty = s_bar + kRing + 2;
-    copy_image(sB, wimg, 2 * BG);
+    copy_image(sB, wimg + gb * BG, NG * BG);
     if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     if (threadIdx.x == 0)
         for (int b = 0; b < 2; ++b) mbar_init(&acc_empty[b], 4);
     fence_async_smem();
-    cta_setup(&s_tmem, s_bar, kRing + 2, 128);
+    cta_setup(&s_tmem, s_bar, kRing + 2, 2 * ACC);
     const uint32_t tmem = s_tmem;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
     const int nstrip = (lw + kM - 1) / kM, nband = (lh + band - 1) / band;
@@ -521,12 +528,12 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
                 mbar_arrive_expect_tx(&s_bar[Ring::slot(row)], uint32_t(SLOT));
-                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, 0, row, sb.r, &s_bar[Ring::slot(row)]);
+                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, gb * CPG, row, sb.r, &s_bar[Ring::slot(row)]);
             }
             ring.pending |= 1u << Ring::slot(row);
         };
-        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
-            last_item(item, items);
+        for (long long item = cta; item < items && ok; item += stride) {
+            last_item(item, items, stride);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh);
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
@@ -540,7 +547,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                 fence_after_sync();
                 if (leader) {
 #pragma unroll
-                    for (int g = 0; g < 2; ++g) {
+                    for (int g = 0; g < NG; ++g) {
                         int step = 0;
 #pragma unroll
                         for (int ky = 0; ky < 3; ++ky) {
@@ -551,7 +558,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                                 for (int kk = 0; kk < CPG / 2; ++kk, ++step) {
                                     const uint64_t a = sdesc(row + (g * CPG + 2 * kk) * LBO + kx * 16, LBO, 128);
                                     const uint64_t bd = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * kk) * 32 * 16, 32 * 16, 128);
-                                    const uint32_t d = tmem + b * 64 + g * 32;
+                                    const uint32_t d = tmem + b * ACC + g * 32;
                                     if (FP8) mma_e4m3(d, a, bd, idesc, step > 0); else mma_f16(d, a, bd, idesc, step > 0);
                                 }
                         }
@@ -581,8 +588,8 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         // ---- epilogue warps ----
         uint32_t it = 0;
         bool ok = true;
-        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
-            last_item(item, items);
+        for (long long item = cta; item < items && ok; item += stride) {
+            last_item(item, items, stride);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh);
             const int x = sb.x0 + t;
             for (int y = sb.y0; y < sb.y1; ++y, ++it) {
@@ -591,33 +598,34 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                 if (!ok) break;
                 fence_after_sync();
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < NG; ++h) {
                     float v[32];
-                    tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 64 + h * 32, v);
-                    if (h == 1) {   // both halves read: hand the buffer back to the producer
+                    tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * ACC + h * 32, v);
+                    const int c0 = (gb + h) * 32;   // first output channel of this group
+                    if (h == NG - 1) {   // every column read: hand the buffer back to the producer
                         fence_before_sync();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
 #pragma unroll
                     for (int n = 0; n < 32; ++n)
-                        v[n] = leaky(fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
+                        v[n] = leaky(fmaf(v[n], s_scale[c0 + n], s_bias[c0 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
                     if (x < lw) {
                         if (FP8) {
                             uint4 q[2];
                             pack_e4m3x32(v, q);
-                            for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 2 + c, lw, x) = q[c];
+                            for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, (gb + h) * 2 + c, lw, x) = q[c];
                         } else {
                             uint4 q[4];
                             pack_f16x32(v, q);
-                            for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, h * 4 + c, lw, x) = q[c];
+                            for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, (gb + h) * 4 + c, lw, x) = q[c];
                         }
                     }
                 }
             }
         }
     }
-    cta_teardown(tmem, 128);
+    cta_teardown(tmem, 2 * ACC);
 }
 
 // refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core.
@@ -1162,20 +1170,23 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         else { smem_attr(k_tc_compress<false>, bytes); launch(pdl, k_tc_compress<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
     }
     {
-        const int ich = fp8 ? 4 : 8;
-        const int per_sm = fp8 ? 4 : 2;
-        const int bytes = 1024 + kRing * ich * (kM + 2) * 16 + 2 * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
+        // FP8: one CTA runs both groups (4 CTAs per SM); FP16: one group per CTA, the halved
+        // shared memory lets 4 CTAs share an SM instead of 2
+        const int ich = fp8 ? 4 : 8, ng = fp8 ? 2 : 1, rch = ng * ich / 2;
+        const int bytes = 1024 + kRing * rch * (kM + 2) * 16 + ng * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
+        const int slots = sms * 4 / (3 - ng);   // CTA slots for one group's work items
         const long long strips = (long long)rs.R * ((lw + kM - 1) / kM);
-        const int band = pick_band(strips, lh, sms * per_sm);
+        const int band = pick_band(strips, lh, slots);
         const long long items = strips * ((lh + band - 1) / band);
-        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM + 2);
-        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM + 2);
+        const unsigned grid = (3 - ng) * grid_for(items, slots / sms, sms);
+        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM + 2, rch);
+        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM + 2, rch);
         void* bufs[2] = {low_a, low_b};
         const CUtensorMap* maps[2] = {&map_a, &map_b};
-        if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
+        if (fp8) smem_attr(k_tc_core<true, 2>, bytes); else smem_attr(k_tc_core<false, 1>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) launch(pdl, k_tc_core<true>, grid_for(items, per_sm, sms), kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else launch(pdl, k_tc_core<false>, grid_for(items, per_sm, sms), kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            if (fp8) launch(pdl, k_tc_core<true, 2>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else launch(pdl, k_tc_core<false, 1>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);

@@ -79,10 +79,12 @@ __device__ __forceinline__ void cta_setup(uint32_t* tmem_slot, uint64_t* bars, i
     grid_dep_wait();
 }
 
-// Called by a CTA when it starts its last work item (see cta_setup).
-__device__ __forceinline__ void last_item(long long item, long long items) {
-    if (item + gridDim.x >= items) grid_dep_launch();
+// Called by a CTA when it starts its last work item (see cta_setup); `stride` is the step
+// between the work items of one CTA.
+__device__ __forceinline__ void last_item(long long item, long long items, long long stride) {
+    if (item + stride >= items) grid_dep_launch();
 }
+__device__ __forceinline__ void last_item(long long item, long long items) { last_item(item, items, gridDim.x); }
 
 __device__ __forceinline__ void cta_teardown(uint32_t tmem, uint32_t ncols) {
     fence_before_sync();

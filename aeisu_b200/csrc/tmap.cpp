@@ -29,14 +29,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, int win) {
-    require(win >= 1 && win <= 256 && nch >= 1 && nch <= 256, "tensor map box out of range");
+CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, int win, int box_ch) {
+    if (box_ch == 0) box_ch = nch;
+    require(win >= 1 && win <= 256 && nch >= 1 && nch <= 256 && box_ch >= 1 && box_ch <= nch,
+            "tensor map box out of range");
     require((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base must be 16-byte aligned");
     // A map depends only on its arguments, and calls reuse the same workspace: encode each once.
-    using Key = std::tuple<const void*, int, int, int, int, int>;
+    using Key = std::tuple<const void*, int, int, int, int, int, int>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{base, R, H, nch, W, win};
+    const Key key{base, R, H, nch, W, win, box_ch};
     {
         std::lock_guard<std::mutex> lock(mu);
         auto it = cache.find(key);
@@ -45,7 +47,7 @@ CUtensorMap make_row_window_map(const void* base, int R, int H, int nch, int W, 
     CUtensorMap map{};
     const cuuint64_t dims[5] = {16, cuuint64_t(W), cuuint64_t(nch), cuuint64_t(H), cuuint64_t(R)};
     const cuuint64_t strides[4] = {16, cuuint64_t(W) * 16, cuuint64_t(nch) * W * 16, cuuint64_t(H) * nch * W * 16};
-    const cuuint32_t box[5] = {16, cuuint32_t(win), cuuint32_t(nch), 1, 1};
+    const cuuint32_t box[5] = {16, cuuint32_t(win), cuuint32_t(box_ch), 1, 1};
     const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
     const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void*>(base), dims, strides,
                                    box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
