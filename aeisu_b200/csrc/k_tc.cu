@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
     uint8_t* sB = smem + 2 * 4 * kM * 16;                      // [4][32][16 B]
     float4 (*s_src)[kProjTW] = reinterpret_cast<float4 (*)[kProjTW]>(sB + 4 * 32 * 16);
     __shared__ float s_st[24];
-    __shared__ float s_bias[32];
+    __shared__ alignas(16) float s_bias[32];
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar[2];
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 32, v);
 #pragma unroll
-            for (int n = 0; n < 32; ++n) v[n] = leaky(v[n] + s_bias[n], slope);
+            epi_add_leaky(v, s_bias, slope);
             uint4 o[4];
             pack_f16x32(v, o);
             if (qx < pw && good) {
@@ -308,10 +308,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + h * 32, v);
 #pragma unroll
-            for (int n = 0; n < 32; ++n) {
-                const float a = fmaf(v[n], s_scale[h * 32 + n], s_bias[h * 32 + n]);
-                v[n] = leaky(a, ep.slope) * (FP8 ? ep.out_inv : 1.f);
-            }
+            epi_fma_leaky(v, s_scale + h * 32, s_bias + h * 32, ep.slope, FP8 ? ep.out_inv : 1.f);
             if (x < lw) {
                 if (FP8) {
                     uint4 o[2];
@@ -398,18 +395,22 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + p * 32, v);
             if (x < lw) {
                 const int oy = 2 * y + (p >> 1), ox = 2 * x + (p & 1);
-                const __half* skh = reinterpret_cast<const __half*>(sk[p]);
+                const __half2* skh = reinterpret_cast<const __half2*>(sk[p]);
+                epi_fma_leaky(v, s_scale + p * 32, s_bias + p * 32, ep.slope, FP8 ? ep.out_inv : 1.f);
+                if (FP8) {   // K8: requantise to e4m3 at 1/s7, dequantise
 #pragma unroll
-                for (int n = 0; n < 32; ++n) {
-                    const int col = p * 32 + n;
-                    float a = leaky(fmaf(v[n], s_scale[col], s_bias[col]), ep.slope);
-                    if (FP8) {
-                        // K8: requantise to e4m3 at 1/s7, dequantise, add the f16 skip
+                    for (int n = 0; n < 32; n += 4) {
                         float q[4];
-                        e4m3x4_to_f32(e4m3x4(a * ep.out_inv, 0.f, 0.f, 0.f), q);
-                        a = q[0] * ep.out_deq;
+                        e4m3x4_to_f32(e4m3x4(v[n], v[n + 1], v[n + 2], v[n + 3]), q);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) v[n + j] = q[j] * ep.out_deq;
                     }
-                    v[n] = a + __half2float(skh[n]);
+                }
+#pragma unroll
+                for (int n = 0; n < 32; n += 2) {   // + the f16 skip
+                    const float2 a = __fadd2_rn(make_float2(v[n], v[n + 1]), __half22float2(skh[n / 2]));
+                    v[n] = a.x;
+                    v[n + 1] = a.y;
                 }
                 uint4 o[4];
                 pack_f16x32(v, o);
@@ -607,9 +608,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
-#pragma unroll
-                    for (int n = 0; n < 32; ++n)
-                        v[n] = leaky(fmaf(v[n], s_scale[c0 + n], s_bias[c0 + n]), ep.slope) * (FP8 ? ep.out_inv : 1.f);
+                    epi_fma_leaky(v, s_scale + c0, s_bias + c0, ep.slope, FP8 ? ep.out_inv : 1.f);
                     if (x < lw) {
                         if (FP8) {
                             uint4 q[2];
@@ -630,15 +629,17 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
 
 // refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core.
 // The refine output (LeakyReLU, f16) goes to shared memory as the tail GEMM's A operand and
-// never reaches HBM.  Warp 4 (producer) issues, per row y: refine(y) into TMEM buffer b, then
-// tail(y-1) once the epilogue has written row y-1's operand, then the TMA refill of row y+3.
-// Warps 0-3 (epilogue) alternate: refine epilogue of row y, tail epilogue of row y-1, so the
-// tail MMA of a row runs while the next row's refine epilogue does.  Refine and tail
-// accumulators and the tail operand are double-buffered; every hand-over is an mbarrier.
+// never reaches HBM.  Warp 8 (producer) issues, per row y: refine(y) into TMEM buffer y&1,
+// then tail(y-1) once that row's operand is written, then the TMA refill of row y+3.  Two
+// epilogue warpgroups (warps 0-3 and 4-7) take alternate rows, each owning one TMEM buffer and
+// one tail operand: refine epilogue of its row, then its tail epilogue, while the other
+// warpgroup works on the neighbouring row.  Every hand-over is an mbarrier.
 // The tail epilogue writes clamped f16 coefficients in the head's layout
 // meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
-__global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+constexpr int kRefineThreads = 288;
+
+__global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                                const uint8_t* __restrict__ wref,
                                                                const uint8_t* __restrict__ wtail,
                                                                const float* __restrict__ rbias,
@@ -676,7 +677,7 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     constexpr uint32_t idesc = idesc_m128(64);
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ---- producer: the whole warp follows the control flow, lane 0 issues ----
         const bool leader = lane == 0;
         const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
@@ -758,77 +759,74 @@ __global__ void __launch_bounds__(kWsThreads) k_tc_refine_tail(const __grid_cons
             if (pend & (1u << i))
                 mbar_wait_bounded(i < 2 ? &ref_full[i] : &tail_full[i - 2], last[i] & 1, err, kErrTimeout, 200000000LL);
     } else {
-        // ---- epilogue warps: refine epilogue of row y, then tail epilogue of row y-1 ----
-        const uint32_t lrow = uint32_t(32 * warp) << 16;
+        // ---- epilogue: warpgroup wg takes the rows whose counter has parity wg ----
+        const int wg = warp >> 2, tq = t & 127;
+        const uint32_t lrow = uint32_t(32 * (warp & 3)) << 16;
+        uint8_t* a2 = sA2 + wg * A2;
         uint32_t it = 0;
         bool ok = true;
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph);
-            const int x = sb.x0 + t;
-            for (int y = sb.y0; y <= sb.y1 && ok; ++y) {
-                if (y < sb.y1) {
-                    const int b = it & 1;
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[b], (it >> 1) & 1, err, kErrTimeout));
-                    if (!ok) break;
-                    fence_after_sync();
-                    float vr[2][32];
-                    tmem_ld32x2(tmem + lrow + b * 128, tmem + lrow + b * 128 + 32, vr[0], vr[1]);
-                    fence_before_sync();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&ref_empty[b]);
-                    uint8_t* a2 = sA2 + b * A2;
+            const int x = sb.x0 + tq;
+            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
+                if (int(it & 1) != wg) continue;
+                const uint32_t k = it >> 1;
+                // refine epilogue -> tail operand of this row
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[wg], k & 1, err, kErrTimeout));
+                if (!ok) break;
+                fence_after_sync();
+                float vr[2][32];
+                tmem_ld32x2(tmem + lrow + wg * 128, tmem + lrow + wg * 128 + 32, vr[0], vr[1]);
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ref_empty[wg]);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < 2; ++h) {
+                    epi_add_leaky(vr[h], s_rb + h * 32, slope);
+                    uint4 q[4];
+                    pack_f16x32(vr[h], q);
 #pragma unroll
-                        for (int n = 0; n < 32; ++n) vr[h][n] = leaky(vr[h][n] + s_rb[h * 32 + n], slope);
-                        uint4 q[4];
-                        pack_f16x32(vr[h], q);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + t) * 16) = q[c];
-                    }
-                    fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&a2_full[b]);
-                    ++it;
+                    for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + tq) * 16) = q[c];
                 }
-                if (y > sb.y0) {   // tail epilogue of row y-1
-                    const uint32_t pit = it - 1 - (y < sb.y1 ? 1 : 0);
-                    const int pb = pit & 1, yt = y - 1;
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[pb], (pit >> 1) & 1, err, kErrTimeout));
-                    if (!ok) break;
-                    fence_after_sync();
-                    float vt[2][32];
-                    tmem_ld32x2(tmem + lrow + pb * 128 + 64, tmem + lrow + pb * 128 + 96, vt[0], vt[1]);
-                    fence_before_sync();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tail_empty[pb]);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a2_full[wg]);
+                // tail epilogue of this row
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[wg], k & 1, err, kErrTimeout));
+                if (!ok) break;
+                fence_after_sync();
+                float vt[2][32];
+                tmem_ld32x2(tmem + lrow + wg * 128 + 64, tmem + lrow + wg * 128 + 96, vt[0], vt[1]);
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tail_empty[wg]);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float (&v)[32] = vt[h];
-                        if (x < pw) {
+                for (int h = 0; h < 2; ++h) {
+                    float (&v)[32] = vt[h];
+                    if (x < pw) {
+                        epi_add(v, s_tb + h * 32);
+                        if (raw) {
+                            float* rp = raw + (((size_t)sb.r * ph + y) * pw + x) * 64 + h * 32;
 #pragma unroll
-                            for (int n = 0; n < 32; ++n) v[n] += s_tb[h * 32 + n];
-                            if (raw) {
-                                float* rp = raw + (((size_t)sb.r * ph + yt) * pw + x) * 64 + h * 32;
+                            for (int n = 0; n < 32; ++n) rp[n] = v[n];
+                        }
 #pragma unroll
-                                for (int n = 0; n < 32; ++n) rp[n] = v[n];
-                            }
+                        for (int n = 0; n < 32; ++n) {   // coefficient_clamp
+                            // v if |v| <= 2, else sign(v) * min(2 + 0.05 (|v| - 2), 2.5): for |v| <= 2
+                            // the soft term is >= |v| (also after rounding), so one min covers both
+                            // cases, and a NaN maps to sign * 2.5 as the reference's select does
+                            const float m = fabsf(v[n]);
+                            v[n] = copysignf(fminf(fminf(m, fmaf(0.05f, m - 2.f, 2.f)), 2.5f), v[n]);
+                        }
+                        uint4 q[4];
+                        pack_f16x32(v, q);
 #pragma unroll
-                            for (int n = 0; n < 32; ++n) {   // coefficient_clamp
-                                const float m = fabsf(v[n]);
-                                const float s = fminf(fmaf(0.05f, m - 2.f, 2.f), 2.5f);
-                                v[n] = m <= 2.f ? v[n] : copysignf(s, v[n]);
-                            }
-                            uint4 q[4];
-                            pack_f16x32(v, q);
+                        for (int pp = 0; pp < 2; ++pp) {
+                            const int parity = h * 2 + pp;
+                            const int Y = 2 * y + (parity >> 1), X = 2 * x + (parity & 1);
 #pragma unroll
-                            for (int pp = 0; pp < 2; ++pp) {
-                                const int parity = h * 2 + pp;
-                                const int Y = 2 * yt + (parity >> 1), X = 2 * x + (parity & 1);
-#pragma unroll
-                                for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
-                            }
+                            for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
                         }
                     }
                 }
@@ -1204,7 +1202,7 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const long long items = strips * ((ph + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
         smem_attr(k_tc_refine_tail, bytes);
-        launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kWsThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
+        launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kRefineThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;

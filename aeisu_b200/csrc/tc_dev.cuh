@@ -21,6 +21,45 @@ __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? l
 // max(v, s*v) equals (v > 0 ? v : s*v) for every input, signed zeros and NaN included.
 __device__ __forceinline__ float leaky(float v, float s) { return fmaxf(v, v * s); }
 
+// Epilogue arithmetic on 32 accumulator columns in packed f32x2 operations (each lane rounds
+// as the scalar operation would).  Per-channel vectors are read from shared memory as float2.
+//   v = leaky(v * scale + bias) * post
+__device__ __forceinline__ void epi_fma_leaky(float (&v)[32], const float* scale, const float* bias, float slope,
+                                              float post) {
+    const float2* s2 = reinterpret_cast<const float2*>(scale);
+    const float2* b2 = reinterpret_cast<const float2*>(bias);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float2 a = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2[i], b2[i]);
+        const float2 n = __fmul2_rn(a, make_float2(slope, slope));
+        a = make_float2(fmaxf(a.x, n.x), fmaxf(a.y, n.y));
+        a = __fmul2_rn(a, make_float2(post, post));
+        v[2 * i] = a.x;
+        v[2 * i + 1] = a.y;
+    }
+}
+//   v = leaky(v + bias)
+__device__ __forceinline__ void epi_add_leaky(float (&v)[32], const float* bias, float slope) {
+    const float2* b2 = reinterpret_cast<const float2*>(bias);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float2 a = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), b2[i]);
+        const float2 n = __fmul2_rn(a, make_float2(slope, slope));
+        v[2 * i] = fmaxf(a.x, n.x);
+        v[2 * i + 1] = fmaxf(a.y, n.y);
+    }
+}
+//   v = v + bias
+__device__ __forceinline__ void epi_add(float (&v)[32], const float* bias) {
+    const float2* b2 = reinterpret_cast<const float2*>(bias);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float2 a = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), b2[i]);
+        v[2 * i] = a.x;
+        v[2 * i + 1] = a.y;
+    }
+}
+
 // (a*w0 + b*w1) + c*w2 without contraction, as the reference's separate tensor ops.
 __device__ __forceinline__ float mix3(float a, float b, float c, float w0, float w1, float w2) {
     return __fadd_rn(__fadd_rn(__fmul_rn(a, w0), __fmul_rn(b, w1)), __fmul_rn(c, w2));
