@@ -436,7 +436,7 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
 // complete upscale call of its own; the device buffers hold the whole batch, so no chunk waits
 // for a buffer slot.
 void Engine::run_pipelined(const Call& c, cudaStream_t s) {
-    const int chunks = std::min(c.n, 8);
+    const int chunks = std::min(c.n, 16);
     const int per = (c.n + chunks - 1) / chunks;
     const size_t in_frame = size_t(3) * c.h * c.w, out_frame = size_t(12) * c.h * c.w;
     src_.ensure(in_frame * c.n, s);
