@@ -629,15 +629,26 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
 
 // refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core.
 // The refine output (LeakyReLU, f16) goes to shared memory as the tail GEMM's A operand and
-// never reaches HBM.  Warp 8 (producer) issues, per row y: refine(y) into TMEM buffer y&1,
-// then tail(y-1) once that row's operand is written, then the TMA refill of row y+3.  Two
-// epilogue warpgroups (warps 0-3 and 4-7) take alternate rows, each owning one TMEM buffer and
-// one tail operand: refine epilogue of its row, then its tail epilogue, while the other
-// warpgroup works on the neighbouring row.  Every hand-over is an mbarrier.
+// never reaches HBM.  Warp 8 (producer) issues refine(y) into TMEM buffer y&1 and refills the
+// TMA ring.  Two epilogue warpgroups (warps 0-3 and 4-7) take alternate rows, each owning one
+// TMEM buffer and one tail operand: refine epilogue of its row, then (after a barrier of its
+// own 128 threads) one of its threads issues the row's tail GEMM, then the tail epilogue.  The
+// producer never waits for a tail, so the refine GEMMs of successive rows follow each other
+// on the tensor core while the epilogues run.
 // The tail epilogue writes clamped f16 coefficients in the head's layout
 // meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
 constexpr int kRefineThreads = 288;
+
+// Barrier among the 128 threads of epilogue warpgroup wg (ids 1, 2); returns whether any of them
+// passed `v`, so an abort is taken by the whole warpgroup.
+__device__ __forceinline__ bool warpgroup_sync_or(int wg, bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, 128, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r) : "r"(uint32_t(v)), "r"(1 + wg) : "memory");
+    return r != 0;
+}
 
 __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                                const uint8_t* __restrict__ wref,
@@ -652,22 +663,20 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;   // refine weights
     uint8_t* sT = sB + BREF;             // tail weights
-    uint8_t* sA2 = sT + BTAIL;           // tail operands, one per buffer
+    uint8_t* sA2 = sT + BTAIL;           // tail operands, one per warpgroup
     float* s_rb = reinterpret_cast<float*>(sA2 + 2 * A2);
     float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
-    // ring slots, then per buffer b: ref_full, tail_full (count 1); ref_empty, a2_full, tail_empty (count 4)
-    __shared__ alignas(8) uint64_t s_bar[kRing + 10];
+    // ring slots, then per buffer b: ref_full, tail_full (count 1), ref_empty (count 4)
+    __shared__ alignas(8) uint64_t s_bar[kRing + 6];
     uint64_t* ref_full = s_bar + kRing;
     uint64_t* tail_full = s_bar + kRing + 2;
     uint64_t* ref_empty = s_bar + kRing + 4;
-    uint64_t* a2_full = s_bar + kRing + 6;
-    uint64_t* tail_empty = s_bar + kRing + 8;
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
     if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
     if (threadIdx.x == 0)
-        for (int i = kRing + 4; i < kRing + 10; ++i) mbar_init(&s_bar[i], 4);
+        for (int i = kRing + 4; i < kRing + 6; ++i) mbar_init(&s_bar[i], 4);
     fence_async_smem();
     cta_setup(&s_tmem, s_bar, kRing + 4, 256);
     const uint32_t tmem = s_tmem;
@@ -680,11 +689,11 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     if (warp == 8) {
         // ---- producer: the whole warp follows the control flow, lane 0 issues ----
         const bool leader = lane == 0;
-        const uint32_t b0 = smem_addr(sB), t0 = smem_addr(sT), a20 = smem_addr(sA2);
+        const uint32_t b0 = smem_addr(sB);
         Ring ring{smem, smem_addr(smem), SLOT, s_bar};
         uint32_t it = 0;             // rows whose refine was issued
-        uint32_t pend = 0;           // bits 0/1 refine, 2/3 tail: committed, not observed here
-        uint32_t last[4] = {0, 0, 0, 0};
+        uint32_t pend = 0;           // bits 0/1: refine committed into buffer b, not observed here
+        uint32_t last[2] = {0, 0};
         bool ok = true;
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
@@ -692,24 +701,6 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                 tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, 0, row, sb.r, &s_bar[Ring::slot(row)]);
             }
             ring.pending |= 1u << Ring::slot(row);
-        };
-        auto tail = [&](uint32_t row_it) {   // tail GEMM of the row with counter row_it
-            const int pb = row_it & 1;
-            const uint32_t pk = row_it >> 1;
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&a2_full[pb], pk & 1, err, kErrTimeout));
-            if (ok && pk > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_empty[pb], (pk - 1) & 1, err, kErrTimeout));
-            if (!ok) return;
-            fence_after_sync();
-            if (leader) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16(tmem + pb * 128 + 64, sdesc(a20 + pb * A2 + kk * 2 * kM * 16, kM * 16, 128),
-                            sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc, kk > 0);
-                commit(&tail_full[pb]);
-            }
-            __syncwarp();
-            pend |= 4u << pb;
-            last[2 + pb] = pk;
         };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             last_item(item, items);
@@ -740,10 +731,6 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                 __syncwarp();
                 pend |= 1u << b;
                 last[b] = k;
-                if (y > sb.y0) {   // tail of the previous row, queued behind refine(y)
-                    tail(it - 1);
-                    if (!ok) break;
-                }
                 if (y + 3 <= sb.y1) {   // refill the slot of row y-1 once refine(y) has read it
                     ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[b], k & 1, err, kErrTimeout));
                     if (!ok) break;
@@ -751,56 +738,71 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                     load(y + 3, sb);
                 }
             }
-            if (ok && sb.y1 > sb.y0) tail(it - 1);   // tail of the band's last row
         }
         // let copies and MMAs still in flight land before TMEM is released
         ring.drain(err);
-        for (int i = 0; i < 4; ++i)
-            if (pend & (1u << i))
-                mbar_wait_bounded(i < 2 ? &ref_full[i] : &tail_full[i - 2], last[i] & 1, err, kErrTimeout, 200000000LL);
+        for (int i = 0; i < 2; ++i)
+            if (pend & (1u << i)) mbar_wait_bounded(&ref_full[i], last[i] & 1, err, kErrTimeout, 200000000LL);
     } else {
         // ---- epilogue: warpgroup wg takes the rows whose counter has parity wg ----
+        // Loop exits are decided only by the warpgroup's barrier vote (`live`), never by one
+        // warp alone, so no warp can leave while the others wait at the warpgroup barrier.
         const int wg = warp >> 2, tq = t & 127;
         const uint32_t lrow = uint32_t(32 * (warp & 3)) << 16;
         uint8_t* a2 = sA2 + wg * A2;
-        uint32_t it = 0;
-        bool ok = true;
-        for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const uint32_t a2addr = smem_addr(a2), t0 = smem_addr(sT);
+        uint32_t it = 0, tail_phase = 0;
+        bool live = true, bad = false;   // bad: a wait of this warp expired (voted at the next barrier)
+        bool tail_pend = false;          // thread tq == 0 committed a tail not yet observed
+        for (long long item = blockIdx.x; item < items && live; item += gridDim.x) {
             last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph);
             const int x = sb.x0 + tq;
-            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
+            for (int y = sb.y0; y < sb.y1 && live; ++y, ++it) {
                 if (int(it & 1) != wg) continue;
                 const uint32_t k = it >> 1;
                 // refine epilogue -> tail operand of this row
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[wg], k & 1, err, kErrTimeout));
-                if (!ok) break;
-                fence_after_sync();
-                float vr[2][32];
-                tmem_ld32x2(tmem + lrow + wg * 128, tmem + lrow + wg * 128 + 32, vr[0], vr[1]);
-                fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ref_empty[wg]);
+                if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[wg], k & 1, err, kErrTimeout));
+                if (!bad) {
+                    fence_after_sync();
+                    float vr[2][32];
+                    tmem_ld32x2(tmem + lrow + wg * 128, tmem + lrow + wg * 128 + 32, vr[0], vr[1]);
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ref_empty[wg]);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    epi_add_leaky(vr[h], s_rb + h * 32, slope);
-                    uint4 q[4];
-                    pack_f16x32(vr[h], q);
+                    for (int h = 0; h < 2; ++h) {
+                        epi_add_leaky(vr[h], s_rb + h * 32, slope);
+                        uint4 q[4];
+                        pack_f16x32(vr[h], q);
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + tq) * 16) = q[c];
+                        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + tq) * 16) = q[c];
+                    }
+                    fence_async_smem();
                 }
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&a2_full[wg]);
+                // the whole operand is written (and every warp's previous tail read is done)
+                fence_before_sync();
+                if (warpgroup_sync_or(wg, bad)) {
+                    live = false;
+                    break;
+                }
+                if (tq == 0) {
+                    fence_after_sync();
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16(tmem + wg * 128 + 64, sdesc(a2addr + kk * 2 * kM * 16, kM * 16, 128),
+                                sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc, kk > 0);
+                    commit(&tail_full[wg]);
+                    tail_pend = true;
+                }
                 // tail epilogue of this row
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[wg], k & 1, err, kErrTimeout));
-                if (!ok) break;
+                bad = !__all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[wg], tail_phase, err, kErrTimeout));
+                if (bad) continue;
+                tail_phase ^= 1u;
+                tail_pend = false;
                 fence_after_sync();
                 float vt[2][32];
                 tmem_ld32x2(tmem + lrow + wg * 128 + 64, tmem + lrow + wg * 128 + 96, vt[0], vt[1]);
-                fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tail_empty[wg]);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float (&v)[32] = vt[h];
@@ -832,6 +834,8 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                 }
             }
         }
+        if (tq == 0 && tail_pend)   // abort path: the committed tail lands before TMEM is released
+            mbar_wait_bounded(&tail_full[wg], tail_phase, err, kErrTimeout, 200000000LL);
     }
     cta_teardown(tmem, 256);
 }
