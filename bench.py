@@ -49,7 +49,7 @@ CONTROLLER_FLOP_PER_PX = 2 * 11520
 HEAD_BYTES_PER_PX = 3 + 32 + 12
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of the
 # workload (profiles/k_tc_head_mixed720_traffic.md); reported as roofline.traffic
-RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.687e9)}
+RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.688e9)}
 
 
 def padded(h, w):
