@@ -432,6 +432,9 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
 // Every TMA issued is waited exactly once and every commit is waited exactly once, so the
 // mbarrier parities stay in step across work items.
 constexpr int kRing = 4;
+// Output pixels per strip of the 3x3 kernels: the 128-pixel input window holds the strip and
+// its one-pixel halo on either side; MMA rows 126 and 127 are computed and discarded.
+constexpr int kConvStrip = kM - 2;
 
 __device__ __forceinline__ uint8_t* align_smem(uint8_t* p) {
     const uint32_t a = smem_addr(p);
@@ -446,12 +449,6 @@ struct Ring {
     uint32_t phase = 0;   // bit s: parity of the next completion of slot s (issuing thread)
     uint32_t pending = 0; // bit s: a load into slot s has not been waited for
     __device__ static int slot(int row) { return (row + 4 * kRing) % kRing; }
-    __device__ void load(const CUtensorMap* map, int x0, int row, int r) {
-        const int s = slot(row);
-        mbar_arrive_expect_tx(&full[s], uint32_t(slot_bytes));
-        tma_load_5d(base + s * slot_bytes, map, 0, x0 - 1, 0, row, r, &full[s]);
-        pending |= 1u << s;
-    }
     __device__ bool wait(int row, int* err) {
         const int s = slot(row);
         const bool ok = mbar_wait_bounded(&full[s], (phase >> s) & 1u, err, kErrTimeout);
@@ -479,7 +476,9 @@ struct Ring {
 //   acc_full[b]  tcgen05.commit of row y's MMAs into TMEM buffer b  -> epilogue, producer
 //   acc_empty[b] one arrive per epilogue warp once it has read buffer b -> producer
 // so the epilogue never waits for MMA issue and there is no CTA-wide barrier per row.  The
-// producer refills the ring slot of row y-1 with row y+3 once MMA(y) has completed.
+// producer issues the taps of input rows y-1 and y before it waits for row y+1 to land, and
+// refills the slot of row y-1 with row y+3 as soon as the row y-1 taps have completed
+// (slot_free).
 constexpr int kWsThreads = 160;
 
 // NG = groups per CTA.  With NG = 1 the two groups (independent 32->32 convolutions) run in
@@ -493,7 +492,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     constexpr int CPG = ICH / 2;              // chunks per group
     constexpr int RCH = NG * CPG;             // chunks staged per row
     constexpr int ACC = NG * 32;              // TMEM columns of one accumulator buffer
-    constexpr int WIN = kM + 2, LBO = WIN * 16, SLOT = RCH * LBO;
+    constexpr int LBO = kM * 16, SLOT = RCH * LBO;   // a 128-pixel window per chunk
     constexpr int BG = 9 * CPG * 32 * 16;     // bytes of one group's weights
     const int gb = NG == 2 ? 0 : int(blockIdx.x & 1);                     // first group of this CTA
     const long long cta = NG == 2 ? blockIdx.x : blockIdx.x >> 1, stride = NG == 2 ? gridDim.x : gridDim.x >> 1;
@@ -503,18 +502,20 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     float* s_scale = reinterpret_cast<float*>(sB + NG * BG);
     float* s_bias = s_scale + 64;
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar[kRing + 4];   // ring slots, acc_full x2, acc_empty x2
+    // ring slots, acc_full x2, slot_free (count 1), acc_empty x2 (count 4)
+    __shared__ alignas(8) uint64_t s_bar[kRing + 5];
     uint64_t* acc_full = s_bar + kRing;
-    uint64_t* acc_empty = s_bar + kRing + 2;
+    uint64_t* slot_free = s_bar + kRing + 2;
+    uint64_t* acc_empty = s_bar + kRing + 3;
     copy_image(sB, wimg + gb * BG, NG * BG);
     if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     if (threadIdx.x == 0)
         for (int b = 0; b < 2; ++b) mbar_init(&acc_empty[b], 4);
     fence_async_smem();
-    cta_setup(&s_tmem, s_bar, kRing + 2, 2 * ACC);
+    cta_setup(&s_tmem, s_bar, kRing + 3, 2 * ACC);
     const uint32_t tmem = s_tmem;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
-    const int nstrip = (lw + kM - 1) / kM, nband = (lh + band - 1) / band;
+    const int nstrip = (lw + kConvStrip - 1) / kConvStrip, nband = (lh + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
 
@@ -524,78 +525,91 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         const uint32_t b0 = smem_addr(sB);
         constexpr uint32_t idesc = idesc_m128(32);
         Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-        uint32_t it = 0, pend = 0;   // rows issued; bit b: a commit into buffer b not yet observed here
+        uint32_t issued = 0, seen = 0;   // rows committed; rows [0, seen) observed complete here
         bool ok = true;
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
                 mbar_arrive_expect_tx(&s_bar[Ring::slot(row)], uint32_t(SLOT));
-                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, gb * CPG, row, sb.r, &s_bar[Ring::slot(row)]);
+                tma_load_4d(smem + Ring::slot(row) * SLOT, &tin, 2 * (sb.x0 - 1), gb * CPG, row, sb.r, &s_bar[Ring::slot(row)]);
             }
             ring.pending |= 1u << Ring::slot(row);
         };
+        // wait until the MMAs of row j (and so of every earlier row) have completed
+        auto done = [&](uint32_t j) {
+            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[j & 1], (j >> 1) & 1, err, kErrTimeout));
+            if (r) seen = j + 1;
+            return r;
+        };
         for (long long item = cta; item < items && ok; item += stride) {
             last_item(item, items, stride);
-            const StripBand sb = strip_band(item, nstrip, nband, band, lh);
+            const StripBand sb = strip_band(item, nstrip, nband, band, lh, kConvStrip);
+            // the previous item's last MMAs still read the ring: let them finish before refilling it
+            if (seen < issued && !(ok = done(issued - 1))) break;
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
-            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
-                const int b = it & 1;
-                const uint32_t k = it >> 1;
-                // buffer b free (its previous row drained) and input row y+1 landed
+            for (int y = sb.y0; y < sb.y1 && ok; ++y) {
+                const uint32_t j = issued;
+                const int b = j & 1;
+                const uint32_t k = j >> 1;
+                // buffer b free: its previous row drained
                 if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_empty[b], (k - 1) & 1, err, kErrTimeout));
-                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
                 if (!ok) break;
                 fence_after_sync();
+                // taps of input row y-1+ky; row y+1 (ky = 2) is waited for only after the
+                // first two rows' MMAs are queued
+                auto taps = [&](int ky) {
+                    const uint32_t row = ring.addr(y - 1 + ky);
+#pragma unroll
+                    for (int g = 0; g < NG; ++g)
+#pragma unroll
+                        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                            for (int kk = 0; kk < CPG / 2; ++kk) {
+                                const uint64_t a = sdesc(row + (g * CPG + 2 * kk) * LBO + kx * 16, LBO, 128);
+                                const uint64_t bd = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * kk) * 32 * 16, 32 * 16, 128);
+                                const uint32_t d = tmem + b * ACC + g * 32;
+                                const bool acc = ky > 0 || kx > 0 || kk > 0;
+                                if (FP8) mma_e4m3(d, a, bd, idesc, acc); else mma_f16(d, a, bd, idesc, acc);
+                            }
+                };
                 if (leader) {
-#pragma unroll
-                    for (int g = 0; g < NG; ++g) {
-                        int step = 0;
-#pragma unroll
-                        for (int ky = 0; ky < 3; ++ky) {
-                            const uint32_t row = ring.addr(y - 1 + ky);
-#pragma unroll
-                            for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                                for (int kk = 0; kk < CPG / 2; ++kk, ++step) {
-                                    const uint64_t a = sdesc(row + (g * CPG + 2 * kk) * LBO + kx * 16, LBO, 128);
-                                    const uint64_t bd = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * kk) * 32 * 16, 32 * 16, 128);
-                                    const uint32_t d = tmem + b * ACC + g * 32;
-                                    if (FP8) mma_e4m3(d, a, bd, idesc, step > 0); else mma_f16(d, a, bd, idesc, step > 0);
-                                }
-                        }
-                    }
-                    commit(&acc_full[b]);
+                    taps(0);
+                    commit(slot_free);   // row y-1's slot is read by nothing after these
+                    taps(1);
                 }
                 __syncwarp();
-                pend |= 1u << b;
-                // refill the slot of row y-1 with row y+3 once MMA(y) has read it
-                if (y + 3 <= sb.y1) {
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[b], k & 1, err, kErrTimeout));
-                    if (!ok) break;
-                    pend &= ~(1u << b);
-                    load(y + 3, sb);
+                ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
+                if (ok) {
+                    fence_after_sync();
+                    if (leader) taps(2);
                 }
+                // commit even on abort, so that the teardown's wait covers every issued MMA
+                if (leader) commit(&acc_full[b]);
+                __syncwarp();
+                ++issued;
+                // Row y+3 goes into the slot of row y-1, free once the ky = 0 MMAs completed (they
+                // were followed by the other taps, so the wait is normally over at once).
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, j & 1, err, kErrTimeout));
+                if (!ok) break;
+                if (y + 3 <= sb.y1) load(y + 3, sb);
             }
         }
-        // let copies and MMAs still in flight land before TMEM is released
+        // let copies and MMAs still in flight land before TMEM is released (MMAs complete in
+        // issue order, so the last commit covers them all)
         ring.drain(err);
-        for (int b = 0; b < 2; ++b)
-            if (pend & (1u << b)) {
-                // the last commit into buffer b: row it-1 or it-2
-                const uint32_t last = ((it - 1) & 1) == uint32_t(b) ? it - 1 : it - 2;
-                mbar_wait_bounded(&acc_full[b], (last >> 1) & 1, err, kErrTimeout, 200000000LL);
-            }
+        if (seen < issued)
+            mbar_wait_bounded(&acc_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
     } else {
         // ---- epilogue warps ----
         uint32_t it = 0;
         bool ok = true;
         for (long long item = cta; item < items && ok; item += stride) {
             last_item(item, items, stride);
-            const StripBand sb = strip_band(item, nstrip, nband, band, lh);
+            const StripBand sb = strip_band(item, nstrip, nband, band, lh, kConvStrip);
             const int x = sb.x0 + t;
             for (int y = sb.y0; y < sb.y1; ++y, ++it) {
                 const int b = it & 1;
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[b], (it >> 1) & 1, err, kErrTimeout));
+                ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], (it >> 1) & 1, err, kErrTimeout));
                 if (!ok) break;
                 fence_after_sync();
 #pragma unroll
@@ -609,7 +623,7 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
                     epi_fma_leaky(v, s_scale + c0, s_bias + c0, ep.slope, FP8 ? ep.out_inv : 1.f);
-                    if (x < lw) {
+                    if (t < kConvStrip && x < lw) {
                         if (FP8) {
                             uint4 q[2];
                             pack_e4m3x32(v, q);
@@ -640,6 +654,13 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
 constexpr int kRefineThreads = 288;
 
+// sign(a) xor sign(b) times min(|a|, |b|); with one NaN operand, the other's magnitude
+__device__ __forceinline__ float min_xorsign_abs(float a, float b) {
+    float r;
+    asm("min.xorsign.abs.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 // Barrier among the 128 threads of epilogue warpgroup wg (ids 1, 2); returns whether any of them
 // passed `v`, so an abort is taken by the whole warpgroup.
 __device__ __forceinline__ bool warpgroup_sync_or(int wg, bool v) {
@@ -657,7 +678,7 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                                                                const float* __restrict__ tbias, float slope,
                                                                void* __restrict__ meta, float* __restrict__ raw,
                                                                int band, int* err) {
-    constexpr int ICH = 4, WIN = kM + 2, LBO = WIN * 16, SLOT = ICH * LBO;
+    constexpr int ICH = 4, LBO = kM * 16, SLOT = ICH * LBO;   // a 128-pixel window per chunk
     constexpr int BREF = 36 * 64 * 16, BTAIL = 8 * 64 * 16, A2 = 8 * kM * 16;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
@@ -667,21 +688,23 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     float* s_rb = reinterpret_cast<float*>(sA2 + 2 * A2);
     float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
-    // ring slots, then per buffer b: ref_full, tail_full (count 1), ref_empty (count 4)
-    __shared__ alignas(8) uint64_t s_bar[kRing + 6];
+    // ring slots, then per buffer b: ref_full, tail_full (count 1); slot_free (count 1); then
+    // per buffer ref_empty (count 4)
+    __shared__ alignas(8) uint64_t s_bar[kRing + 7];
     uint64_t* ref_full = s_bar + kRing;
     uint64_t* tail_full = s_bar + kRing + 2;
-    uint64_t* ref_empty = s_bar + kRing + 4;
+    uint64_t* slot_free = s_bar + kRing + 4;
+    uint64_t* ref_empty = s_bar + kRing + 5;
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
     if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
     if (threadIdx.x == 0)
-        for (int i = kRing + 4; i < kRing + 6; ++i) mbar_init(&s_bar[i], 4);
+        for (int i = kRing + 5; i < kRing + 7; ++i) mbar_init(&s_bar[i], 4);
     fence_async_smem();
-    cta_setup(&s_tmem, s_bar, kRing + 4, 256);
+    cta_setup(&s_tmem, s_bar, kRing + 5, 256);
     const uint32_t tmem = s_tmem;
     const int ph = rs.rh / 2, pw = rs.rw / 2;
-    const int nstrip = (pw + kM - 1) / kM, nband = (ph + band - 1) / band;
+    const int nstrip = (pw + kConvStrip - 1) / kConvStrip, nband = (ph + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     constexpr uint32_t idesc = idesc_m128(64);
@@ -691,58 +714,71 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
         const bool leader = lane == 0;
         const uint32_t b0 = smem_addr(sB);
         Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-        uint32_t it = 0;             // rows whose refine was issued
-        uint32_t pend = 0;           // bits 0/1: refine committed into buffer b, not observed here
-        uint32_t last[2] = {0, 0};
+        uint32_t issued = 0, seen = 0;   // rows committed; rows [0, seen) observed complete here
         bool ok = true;
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
                 mbar_arrive_expect_tx(&s_bar[Ring::slot(row)], uint32_t(SLOT));
-                tma_load_5d(smem + Ring::slot(row) * SLOT, &tin, 0, sb.x0 - 1, 0, row, sb.r, &s_bar[Ring::slot(row)]);
+                tma_load_4d(smem + Ring::slot(row) * SLOT, &tin, 2 * (sb.x0 - 1), 0, row, sb.r, &s_bar[Ring::slot(row)]);
             }
             ring.pending |= 1u << Ring::slot(row);
         };
+        // wait until the refine MMAs of row j (and so of every earlier row) have completed
+        auto done = [&](uint32_t j) {
+            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[j & 1], (j >> 1) & 1, err, kErrTimeout));
+            if (r) seen = j + 1;
+            return r;
+        };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             last_item(item, items);
-            const StripBand sb = strip_band(item, nstrip, nband, band, ph);
+            const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
+            // the previous item's last MMAs still read the ring: let them finish before refilling it
+            if (seen < issued && !(ok = done(issued - 1))) break;
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
-            for (int y = sb.y0; y < sb.y1 && ok; ++y, ++it) {
-                const int b = it & 1;
-                const uint32_t k = it >> 1;
+            for (int y = sb.y0; y < sb.y1 && ok; ++y) {
+                const uint32_t j = issued;
+                const int b = j & 1;
+                const uint32_t k = j >> 1;
                 if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_empty[b], (k - 1) & 1, err, kErrTimeout));
-                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
                 if (!ok) break;
                 fence_after_sync();
+                auto taps = [&](int ky) {   // the 6 MMAs of input row y-1+ky
+                    const uint32_t row = ring.addr(y - 1 + ky);
+#pragma unroll
+                    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk)
+                            mma_f16(tmem + b * 128, sdesc(row + 2 * kk * LBO + kx * 16, LBO, 128),
+                                    sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * kk) * 64 * 16, 64 * 16, 128), idesc,
+                                    ky > 0 || kx > 0 || kk > 0);
+                };
                 if (leader) {
-                    int step = 0;
-#pragma unroll
-                    for (int ky = 0; ky < 3; ++ky) {
-                        const uint32_t row = ring.addr(y - 1 + ky);
-#pragma unroll
-                        for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                            for (int kk = 0; kk < 2; ++kk, ++step)
-                                mma_f16(tmem + b * 128, sdesc(row + 2 * kk * LBO + kx * 16, LBO, 128),
-                                        sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * kk) * 64 * 16, 64 * 16, 128), idesc, step > 0);
-                    }
-                    commit(&ref_full[b]);
+                    taps(0);
+                    commit(slot_free);   // row y-1's slot is read by nothing after these
+                    taps(1);
                 }
                 __syncwarp();
-                pend |= 1u << b;
-                last[b] = k;
-                if (y + 3 <= sb.y1) {   // refill the slot of row y-1 once refine(y) has read it
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[b], k & 1, err, kErrTimeout));
-                    if (!ok) break;
-                    pend &= ~(1u << b);
-                    load(y + 3, sb);
+                ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
+                if (ok) {
+                    fence_after_sync();
+                    if (leader) taps(2);
                 }
+                // commit even on abort, so that the teardown's wait covers every issued MMA
+                if (leader) commit(&ref_full[b]);
+                __syncwarp();
+                ++issued;
+                // row y+3 into the slot of row y-1 once its taps completed
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, j & 1, err, kErrTimeout));
+                if (!ok) break;
+                if (y + 3 <= sb.y1) load(y + 3, sb);
             }
         }
-        // let copies and MMAs still in flight land before TMEM is released
+        // let copies and MMAs still in flight land before TMEM is released (MMAs complete in
+        // issue order, so the last commit covers them all)
         ring.drain(err);
-        for (int i = 0; i < 2; ++i)
-            if (pend & (1u << i)) mbar_wait_bounded(&ref_full[i], last[i] & 1, err, kErrTimeout, 200000000LL);
+        if (seen < issued)
+            mbar_wait_bounded(&ref_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
     } else {
         // ---- epilogue: warpgroup wg takes the rows whose counter has parity wg ----
         // Loop exits are decided only by the warpgroup's barrier vote (`live`), never by one
@@ -756,13 +792,13 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
         bool tail_pend = false;          // thread tq == 0 committed a tail not yet observed
         for (long long item = blockIdx.x; item < items && live; item += gridDim.x) {
             last_item(item, items);
-            const StripBand sb = strip_band(item, nstrip, nband, band, ph);
+            const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
             const int x = sb.x0 + tq;
             for (int y = sb.y0; y < sb.y1 && live; ++y, ++it) {
                 if (int(it & 1) != wg) continue;
                 const uint32_t k = it >> 1;
                 // refine epilogue -> tail operand of this row
-                if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[wg], k & 1, err, kErrTimeout));
+                if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_idle(&ref_full[wg], k & 1, err, kErrTimeout));
                 if (!bad) {
                     fence_after_sync();
                     float vr[2][32];
@@ -796,7 +832,7 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                     tail_pend = true;
                 }
                 // tail epilogue of this row
-                bad = !__all_sync(0xffffffffu, mbar_wait_bounded(&tail_full[wg], tail_phase, err, kErrTimeout));
+                bad = !__all_sync(0xffffffffu, mbar_wait_idle(&tail_full[wg], tail_phase, err, kErrTimeout));
                 if (bad) continue;
                 tail_phase ^= 1u;
                 tail_pend = false;
@@ -806,7 +842,7 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float (&v)[32] = vt[h];
-                    if (x < pw) {
+                    if (tq < kConvStrip && x < pw) {
                         epi_add(v, s_tb + h * 32);
                         if (raw) {
                             float* rp = raw + (((size_t)sb.r * ph + y) * pw + x) * 64 + h * 32;
@@ -814,12 +850,16 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                             for (int n = 0; n < 32; ++n) rp[n] = v[n];
                         }
 #pragma unroll
-                        for (int n = 0; n < 32; ++n) {   // coefficient_clamp
+                        for (int n = 0; n < 32; n += 2) {   // coefficient_clamp
                             // v if |v| <= 2, else sign(v) * min(2 + 0.05 (|v| - 2), 2.5): for |v| <= 2
                             // the soft term is >= |v| (also after rounding), so one min covers both
-                            // cases, and a NaN maps to sign * 2.5 as the reference's select does
-                            const float m = fabsf(v[n]);
-                            v[n] = copysignf(fminf(fminf(m, fmaf(0.05f, m - 2.f, 2.f)), 2.5f), v[n]);
+                            // cases.  min.xorsign.abs(v, c) = sign(v) * min(|v|, c) for c > 0, and a
+                            // NaN v (soft term NaN) maps to sign * 2.5 as the reference's select does
+                            const float2 soft = __ffma2_rn(make_float2(0.05f, 0.05f),
+                                                           make_float2(fabsf(v[n]) - 2.f, fabsf(v[n + 1]) - 2.f),
+                                                           make_float2(2.f, 2.f));
+                            v[n] = min_xorsign_abs(v[n], fminf(soft.x, 2.5f));
+                            v[n + 1] = min_xorsign_abs(v[n + 1], fminf(soft.y, 2.5f));
                         }
                         uint4 q[4];
                         pack_f16x32(v, q);
@@ -1175,14 +1215,14 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         // FP8: one CTA runs both groups (4 CTAs per SM); FP16: one group per CTA, the halved
         // shared memory lets 4 CTAs share an SM instead of 2
         const int ich = fp8 ? 4 : 8, ng = fp8 ? 2 : 1, rch = ng * ich / 2;
-        const int bytes = 1024 + kRing * rch * (kM + 2) * 16 + ng * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
+        const int bytes = 1024 + kRing * rch * kM * 16 + ng * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
         const int slots = sms * 4 / (3 - ng);   // CTA slots for one group's work items
-        const long long strips = (long long)rs.R * ((lw + kM - 1) / kM);
+        const long long strips = (long long)rs.R * ((lw + kConvStrip - 1) / kConvStrip);
         const int band = pick_band(strips, lh, slots);
         const long long items = strips * ((lh + band - 1) / band);
         const unsigned grid = (3 - ng) * grid_for(items, slots / sms, sms);
-        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM + 2, rch);
-        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM + 2, rch);
+        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM, rch);
+        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM, rch);
         void* bufs[2] = {low_a, low_b};
         const CUtensorMap* maps[2] = {&map_a, &map_b};
         if (fp8) smem_attr(k_tc_core<true, 2>, bytes); else smem_attr(k_tc_core<false, 1>, bytes);
@@ -1200,11 +1240,11 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
     }
     mark(3);
     {
-        const int bytes = 1024 + kRing * 4 * (kM + 2) * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
-        const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
+        const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
+        const long long strips = (long long)rs.R * ((pw + kConvStrip - 1) / kConvStrip);
         const int band = pick_band(strips, ph, sms * 2);
         const long long items = strips * ((ph + band - 1) / band);
-        const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM + 2);
+        const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM);
         smem_attr(k_tc_refine_tail, bytes);
         launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kRefineThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
     }

@@ -165,6 +165,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may stay suspended for up to `hint_ns` (it resumes when the
+// phase completes): long waits then poll, and take issue slots from the other warps, less often.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait of an epilogue warp on a long pipeline stage (see mbar_wait_bounded).
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               long long limit_cycles = 4000000000LL) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait_hint(bar, parity, 100000u)) {
+        if (clock64() - t0 > limit_cycles) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Wait for phase `parity` of `bar` to complete, for at most ~`limit_cycles` SM clocks.
 // On expiry records `code` in *err (first error wins) and returns false; the caller then
 // stops issuing work and exits through its normal teardown.
@@ -211,6 +235,14 @@ __device__ __forceinline__ void tma_load_5d(void* smem, const void* tmap, int c0
         "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
         :: "r"(smem_addr(smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem, const void* tmap, int c0, int c1, int c2, int c3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_addr(smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
         : "memory");
 }
 

@@ -180,11 +180,12 @@ __device__ __forceinline__ uint4* cp_at(const void* base, int r, int H, int y, i
 struct StripBand {
     int r, x0, y0, y1;
 };
-__device__ __forceinline__ StripBand strip_band(long long item, int nstrip, int nband, int band, int H) {
+__device__ __forceinline__ StripBand strip_band(long long item, int nstrip, int nband, int band, int H,
+                                                int width = kM) {
     StripBand s;
     s.r = int(item / ((long long)nstrip * nband));
     const int b = int((item / nstrip) % nband);
-    s.x0 = int(item % nstrip) * kM;
+    s.x0 = int(item % nstrip) * width;
     s.y0 = b * band;
     s.y1 = min(s.y0 + band, H);
     return s;
