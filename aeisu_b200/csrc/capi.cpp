@@ -161,6 +161,15 @@ int aeisu_predict_coefficients(aeisu_t* handle, const float* src, int n, int h, 
     });
 }
 
+int aeisu_activation_stats(aeisu_t* handle, const uint8_t* src, int n, int h, int w, unsigned flags, float* peaks,
+                           float* means, void* stream) {
+    return guarded([&] {
+        check_io(n, h, w, flags);
+        engine_of(handle).activation_stats(src, flags == AEISU_IO_HOST, n, h, w, peaks, means,
+                                           static_cast<cudaStream_t>(stream));
+    });
+}
+
 int aeisu_synchronize(aeisu_t* handle, void* stream, double timeout_ms) {
     return guarded([&] { engine_of(handle).synchronize(static_cast<cudaStream_t>(stream), timeout_ms); });
 }

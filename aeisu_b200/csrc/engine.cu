@@ -407,9 +407,13 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
         } else {
             launch_f32_controller(src, rs, stencil_, f32_layers_, enc540_.as<float>(), low_a_.as<float>(),
                                   low_b_.as<float>(), dec540_.as<float>(), refined_.as<float>(), meta_.as<float>(), s,
-                                  &launches, mark);
+                                  &launches, mark,
+                                  c.mode == Mode::Calibrate ? reinterpret_cast<float*>(stats_.as<double>() + 448) : nullptr,
+                                  c.mode == Mode::Calibrate ? stats_.as<double>() : nullptr);
         }
-        if (predict) {
+        if (c.mode == Mode::Calibrate) {
+            // activation maxima only
+        } else if (predict) {
             // one region per frame, covering it: metadata NHWC [h/2, w/2, 64] per frame
             const size_t bytes = 4 * packed * 64;
             const char* meta = tcr ? raw_.as<char>() : meta_.as<char>();
@@ -493,10 +497,54 @@ const Geometry& Engine::plan(const Call& c) {
     auto it = plan_cache_.find(key);
     if (it != plan_cache_.end()) return it->second;
     Geometry g = c.bands > 0                ? plan_band(c.h, c.w, c.band, c.bands)
-                 : (c.mode == Mode::Upscale) ? plan_upscale(c.n, c.h, c.w, c.tile)
+                 : (c.mode == Mode::Upscale || c.mode == Mode::Calibrate) ? plan_upscale(c.n, c.h, c.w, c.tile)
                                              : plan_whole(c.n, c.h, c.w);
     if (plan_cache_.size() >= 256) plan_cache_.clear();
     return plan_cache_.emplace(key, std::move(g)).first->second;
+}
+
+// Calibration for the SPYR8 exporter: the FP32 controller on the padded frames, exactly as an
+// upscale with tile 0 runs it, with running maxima and channel sums.
+void Engine::activation_stats(const uint8_t* src, bool host, int n, int h, int w, float* peaks, float* means,
+                              cudaStream_t stream) {
+    DeviceGuard guard(device_);
+    require(src != nullptr && peaks != nullptr, "source and peaks must not be null");
+    if (precision_ != AEISU_PRECISION_FP32)
+        fail(AEISU_ERR_UNSUPPORTED, "activation statistics are measured on the FP32 route (open the folded checkpoint with precision fp32)");
+    Call c{Mode::Calibrate, src, 0, nullptr, 0, n, h, w, 0, host, stream};
+    const Geometry& g = plan(c);
+    cudaStream_t s = stream ? stream : stream_;
+    marks_.clear();
+    timings_pending_ = true;
+    AEISU_CUDA(cudaEventRecord(ev_[0], s));
+    const void* src_ptr = src;
+    if (host) {
+        const size_t bytes = size_t(n) * 3 * h * w;
+        src_.ensure(bytes, s);
+        AEISU_CUDA(cudaMemcpyAsync(src_.get(), src, bytes, cudaMemcpyHostToDevice, s));
+        src_ptr = src_.get();
+    }
+    constexpr size_t kStatBytes = 448 * sizeof(double) + 16 * sizeof(float);
+    stats_.ensure(kStatBytes, s);
+    AEISU_CUDA(cudaMemsetAsync(stats_.get(), 0, kStatBytes, s));
+    AEISU_CUDA(cudaMemsetAsync(flag_.get(), 0, 2 * sizeof(int), s));
+    record(0, s);
+    SrcDesc sd{src_ptr, 0, h, w, g.pad_y, g.pad_x};
+    DstDesc dd{nullptr, 0, 2 * g.out_h, 2 * g.out_w, g.pad_y, g.pad_x};
+    double packed = 0, low = 0;   // pixels at half and quarter resolution over all regions
+    for (const auto& grp : g.groups) {
+        run_group(c, g, grp, sd, dd, s);
+        packed += double(grp.regions.size()) * (grp.rh / 2) * (grp.rw / 2);
+        low += double(grp.regions.size()) * (grp.rh / 4) * (grp.rw / 4);
+    }
+    char* staged = static_cast<char*>(staging_.ensure(kStatBytes, s));
+    AEISU_CUDA(cudaMemcpyAsync(staged, stats_.get(), kStatBytes, cudaMemcpyDeviceToHost, s));
+    AEISU_CUDA(cudaEventRecord(ev_[6], s));
+    wait(s, timeout_ms_);
+    const double* sums = reinterpret_cast<const double*>(staged);
+    std::memcpy(peaks, staged + 448 * sizeof(double), 10 * sizeof(float));
+    if (means)
+        for (int i = 0; i < 448; ++i) means[i] = float(sums[i] / (i < 128 ? packed / 4 : low));
 }
 
 void Engine::run(const Call& c) {

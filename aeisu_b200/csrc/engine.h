@@ -76,7 +76,7 @@ Geometry plan_whole(int n, int h, int w);
 // whole-frame result (the controller's receptive field is smaller than the halo).
 Geometry plan_band(int h, int w, int band, int bands);
 
-enum class Mode { Upscale, Forward, Predict };
+enum class Mode { Upscale, Forward, Predict, Calibrate };
 
 struct Call {
     Mode mode;
@@ -97,6 +97,11 @@ public:
 
     void run(const Call& call);
     void synchronize(cudaStream_t s, double timeout_ms);
+    // FP32 route over n uint8 frames (tile 0, no reconstruction), returning (host) in peaks[10]
+    // the max |x| of each activation the mixed route quantises and, if means is not null, in
+    // means[448] the mean of every input channel of the FP8 layers; waits for completion.
+    void activation_stats(const uint8_t* src, bool host, int n, int h, int w, float* peaks, float* means,
+                          cudaStream_t stream);
 
     const std::string& report() const { return report_; }
     uint64_t device_bytes() const;
@@ -147,6 +152,7 @@ private:
     aeisu_timings timings_{};
 
     // resident weights
+    DevBuf stats_;               // calibration: channel sums (double[448]) then maxima (float[10])
     DevBuf w_f32_;               // all FP32 tensors, packed
     const float* stencil_ = nullptr;
     const float* base_ = nullptr;

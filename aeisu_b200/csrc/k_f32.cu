@@ -4,6 +4,8 @@
 // 473-492 (controller) and aeisu/reconstruction.py:15-83 (head) operation for operation.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.h"
 #include "kernels.h"
 
@@ -29,6 +31,15 @@ __device__ __forceinline__ float3 load_src(const SrcDesc& s, int f, int py, int 
 
 __device__ __forceinline__ float leaky(float v, float slope) { return v > 0.f ? v : v * slope; }
 
+// Running maximum of |activation| for calibration: `m` (>= 0, or NaN) of every active lane of
+// the warp into *peak.  Non-negative floats order like their bit patterns, and a NaN (above
+// +inf as bits) stays visible to the caller.
+__device__ __forceinline__ void peak_max(float* peak, float m) {
+    const unsigned mask = __activemask();
+    const unsigned v = __reduce_max_sync(mask, __float_as_uint(m));
+    if (int(threadIdx.x & 31) == __ffs(mask) - 1) atomicMax(reinterpret_cast<unsigned*>(peak), v);
+}
+
 // (a*w0 + b*w1) + c*w2 without contraction, as the reference's separate tensor ops.
 __device__ __forceinline__ float mix3(float a, float b, float c, float w0, float w1, float w2) {
     return __fadd_rn(__fadd_rn(__fmul_rn(a, w0), __fmul_rn(b, w1)), __fmul_rn(c, w2));
@@ -38,7 +49,8 @@ __device__ __forceinline__ float mix3(float a, float b, float c, float w0, float
 // unshuffle (channel c*4 + i*2 + j), project_540 1x1 32->32 + LeakyReLU (model.py:481).
 __global__ void __launch_bounds__(kThreads) k_analysis_project(SrcDesc src, RegionSet rs,
                                                                const float* __restrict__ stencil,
-                                                               F32Layer proj, float* __restrict__ out) {
+                                                               F32Layer proj, float* __restrict__ out,
+                                                               float* feat_peak) {
     __shared__ float s_w[32 * 32];
     __shared__ float s_b[32];
     __shared__ float s_st[24];
@@ -80,6 +92,11 @@ __global__ void __launch_bounds__(kThreads) k_analysis_project(SrcDesc src, Regi
             f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
                                      __fmul_rn(hmid, s_st[23]));
         }
+    if (feat_peak) {   // calibration: the unshuffled features, the input project_540 quantises
+        float m = 0.f;
+        for (int k = 0; k < 32; ++k) m = fmaxf(m, fabsf(f[k]));
+        peak_max(feat_peak, m);
+    }
     float* o = out + idx * 32;
     for (int c = 0; c < 32; ++c) {
         float acc = 0.f;
@@ -162,7 +179,8 @@ __global__ void __launch_bounds__(kThreads) k_conv3x3(int R, int H, int W, F32La
 // expand_270 1x1 64->128 + LeakyReLU, pixel_shuffle (channel c*4+i*2+j -> pixel (2y+i, 2x+j)),
 // + enc540 skip (model.py:488-489).  One thread per (low pixel, phase).
 __global__ void __launch_bounds__(kThreads) k_expand(RegionSet rs, F32Layer L, const float* __restrict__ low,
-                                                     const float* __restrict__ enc540, float* __restrict__ dec) {
+                                                     const float* __restrict__ enc540, float* __restrict__ dec,
+                                                     float* exp_peak) {
     __shared__ float s_w[128 * 64];
     for (int i = threadIdx.x; i < 128 * 64; i += blockDim.x) s_w[i] = L.w[i];
     __syncthreads();
@@ -182,7 +200,36 @@ __global__ void __launch_bounds__(kThreads) k_expand(RegionSet rs, F32Layer L, c
         for (int c = 0; c < 32; ++c) acc[c] = fmaf(s_w[(c * 4 + p) * 64 + k], v, acc[c]);
     }
     const size_t o = ((size_t(r) * ph + 2 * y + (p >> 1)) * pw + 2 * x + (p & 1)) * 32;
-    for (int c = 0; c < 32; ++c) dec[o + c] = enc540[o + c] + leaky(acc[c] + L.b[c * 4 + p], L.slope);
+    float m = 0.f;
+    for (int c = 0; c < 32; ++c) {
+        const float e = leaky(acc[c] + L.b[c * 4 + p], L.slope);
+        m = fmaxf(m, fabsf(e));
+        dec[o + c] = enc540[o + c] + e;
+    }
+    if (exp_peak) peak_max(exp_peak, m);   // calibration: expand_270's output before the skip add
+}
+
+// Calibration: per-channel sums of a float32 NHWC tensor [R][H][W][C] (C divides kThreads)
+// into sums; with `phases`, channel c of pixel (y, x) adds to sums[c*4 + (y&1)*2 + (x&1)], the
+// channel order of the pixel unshuffle that feeds the next layer, else to sums[c].
+__global__ void __launch_bounds__(kThreads) k_chansum(const float* __restrict__ x, long long npix, int H, int W,
+                                                      int C, bool phases, double* sums) {
+    const int c = threadIdx.x % C, row = threadIdx.x / C, rows = kThreads / C;
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    for (long long p = (long long)blockIdx.x * rows + row; p < npix; p += (long long)gridDim.x * rows) {
+        const float v = x[p * C + c];
+        const int k = phases ? int(((p / W) % H) & 1) * 2 + int((p % W) & 1) : 0;
+        acc[k] += double(v);
+    }
+    for (int k = 0; k < (phases ? 4 : 1); ++k) atomicAdd(&sums[phases ? c * 4 + k : c], acc[k]);
+}
+
+// Calibration: max |x| over n floats into *peak.
+__global__ void __launch_bounds__(kThreads) k_absmax(const float* __restrict__ x, long long n, float* peak) {
+    float m = 0.f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(x[i]));
+    peak_max(peak, m);
 }
 
 // 1x1 64->64 without activation (metadata_head, model.py:490).
@@ -289,27 +336,51 @@ void set_smem(const void* fn, int bytes) {
 
 void launch_f32_controller(const SrcDesc& src, const RegionSet& rs, const float* stencil, const F32Layer* L,
                            float* enc540, float* low_a, float* low_b, float* dec540, float* refined,
-                           float* meta, cudaStream_t s, int* launches, const StageMark& mark) {
+                           float* meta, cudaStream_t s, int* launches, const StageMark& mark, float* peaks,
+                           double* sums) {
     const long long packed = (long long)rs.R * (rs.rh / 2) * (rs.rw / 2);
     const long long low = (long long)rs.R * (rs.rh / 4) * (rs.rw / 4);
-    k_analysis_project<<<blocks_for(packed), kThreads, 0, s>>>(src, rs, stencil, L[0], enc540);
+    int extra = 0;
+    auto absmax = [&](const float* x, long long n, int k) {
+        if (!peaks) return;
+        k_absmax<<<unsigned(std::min<long long>(blocks_for(n), 4096)), kThreads, 0, s>>>(x, n, peaks + k);
+        ++extra;
+    };
+    // input-channel sums of the FP8 layers: compress (128, unshuffle order), bottleneck 0-3 and
+    // expand (64 each)
+    auto chansum = [&](const float* x, long long npix, int H, int W, int C, bool phases, int off) {
+        if (!sums) return;
+        k_chansum<<<unsigned(std::min<long long>((npix * C + kThreads - 1) / kThreads, 1024)), kThreads, 0, s>>>(
+            x, npix, H, W, C, phases, sums + off);
+        ++extra;
+    };
+    k_analysis_project<<<blocks_for(packed), kThreads, 0, s>>>(src, rs, stencil, L[0], enc540, peaks);
+    absmax(enc540, packed * 32, 1);
+    chansum(enc540, packed, rs.rh / 2, rs.rw / 2, 32, true, 0);
     mark(1);
     k_compress<<<blocks_for(low * 2), kThreads, 0, s>>>(rs, L[1], enc540, low_a);
+    absmax(low_a, low * 64, 2);
+    chansum(low_a, low, rs.rh / 4, rs.rw / 4, 64, false, 128);
     constexpr int core_smem = 64 * 32 * 9 * 4;
     set_smem((const void*)k_conv3x3<32, 32, 2>, core_smem);
     set_smem((const void*)k_conv3x3<32, 64, 1>, core_smem);
     float* bufs[2] = {low_a, low_b};
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 4; ++i) {
         k_conv3x3<32, 32, 2><<<blocks_for(low * 2), kThreads, core_smem, s>>>(
             rs.R, rs.rh / 4, rs.rw / 4, L[2 + i], true, bufs[i & 1], bufs[(i + 1) & 1]);
+        absmax(bufs[(i + 1) & 1], low * 64, 3 + i);
+        chansum(bufs[(i + 1) & 1], low, rs.rh / 4, rs.rw / 4, 64, false, 192 + 64 * i);
+    }
     mark(2);
-    k_expand<<<blocks_for(low * 4), kThreads, 0, s>>>(rs, L[6], low_a, enc540, dec540);
+    k_expand<<<blocks_for(low * 4), kThreads, 0, s>>>(rs, L[6], low_a, enc540, dec540, peaks ? peaks + 7 : nullptr);
+    absmax(dec540, packed * 32, 8);
     mark(3);
     k_conv3x3<32, 64, 1><<<blocks_for(packed * 2), kThreads, core_smem, s>>>(
         rs.R, rs.rh / 2, rs.rw / 2, L[7], true, dec540, refined);
+    absmax(refined, packed * 64, 9);
     k_tail<<<blocks_for(packed * 2), kThreads, 0, s>>>(packed, L[8], refined, meta);
     AEISU_CUDA(cudaGetLastError());
-    *launches += 10;
+    *launches += 10 + extra;
     mark(4);
 }
 

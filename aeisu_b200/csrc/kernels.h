@@ -44,11 +44,16 @@ struct StageMark {
     void operator()(int stage) const { if (fn) fn(ctx, stage); }
 };
 
-// FP32 parity route (k_f32.cu).  Activations are float32 NHWC.
+// FP32 parity route (k_f32.cu).  Activations are float32 NHWC.  Calibration outputs (device,
+// or null): peaks[10] accumulates the running max |x| of the ten activations the mixed route
+// quantises, in SPYR8 activation_scales order (unshuffled features, project_540, compress_270,
+// the four bottleneck outputs, expand_270 before the skip add, refine input, refine_540);
+// sums[448] the per-input-channel sums of the FP8 layers: compress_270 (128, unshuffle order
+// c*4 + phase), bottleneck 0-3 and expand_270 (64 each).
 void launch_f32_controller(const SrcDesc& src, const RegionSet& rs, const float* stencil,
                            const F32Layer* layers, float* enc540, float* low_a, float* low_b,
                            float* dec540, float* refined, float* meta, cudaStream_t s, int* launches,
-                           const StageMark& mark);
+                           const StageMark& mark, float* peaks = nullptr, double* sums = nullptr);
 // Epilogue parameters of a tensor-core convolution layer.
 struct EpiParams {
     const float* scale;   // per output channel: accumulator multiplier (FP8: s_in * w_scale)

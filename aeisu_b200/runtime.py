@@ -213,6 +213,22 @@ class Model:
         out = out.permute(0, 3, 1, 2) if a.device else out.transpose(0, 3, 1, 2)
         return self._wrap(a, out)
 
+    def activation_stats(self, frames):
+        """Calibration statistics of this FP32 model over uint8 frames [n,H,W,3] or [H,W,3]:
+        (peaks[10], means[448]) as aeisu_activation_stats defines them."""
+        a = _Array(frames, np.uint8, self.device_index)
+        x = a.keep
+        if x.ndim == 3:
+            x = x[None]
+        if x.ndim != 4 or x.shape[-1] != 3:
+            raise ValueError(f"Expected uint8 frames [n,H,W,3], got {tuple(x.shape)}")
+        peaks = np.zeros(10, np.float32)
+        means = np.zeros(448, np.float32)
+        _lib.check(_lib.lib().aeisu_activation_stats(
+            self._handle(), a.ptr, x.shape[0], x.shape[1], x.shape[2], _lib.IO_DEVICE if a.device else _lib.IO_HOST,
+            peaks.ctypes.data, means.ctypes.data, a.stream))
+        return peaks, means
+
     def __call__(self, source):
         """FoldedAEISU.forward: unclipped 2x RGB [B,3,2H,2W] of a padded batch."""
         a = _Array(source, np.float32, self.device_index)

@@ -143,6 +143,21 @@ int aeisu_forward_f32(aeisu_t* handle, const float* src, int n, int h, int w, fl
 int aeisu_predict_coefficients(aeisu_t* handle, const float* src, int n, int h, int w,
                                float* meta, unsigned flags, void* stream);
 
+/* Calibration for the SPYR8 exporter: runs the FP32 controller of a handle opened with
+ * AEISU_PRECISION_FP32 over n uint8 frames (h x w x 3, padded as aeisu_upscale_u8 with tile 0
+ * pads them) and writes (host memory):
+ *   peaks[10]  the largest |x| of the ten activations the mixed route quantises, in the order
+ *              of the SPYR8 activation_scales tensor: unshuffled analysis features,
+ *              project_540, compress_270, bottleneck 1-4, expand_270 before the skip add, the
+ *              refine input, refine_540;
+ *   means[448] (may be NULL) the mean of each input channel of the FP8 layers: compress_270
+ *              (128, in its unshuffled order c*4 + phase), bottleneck 1-4 and expand_270 (64
+ *              each), for the bias correction of their E4M3 weights.
+ * The SPYR8 layout is SrcPyrModel.cpp:37-85; the reference's calibrator itself is not shipped.
+ * Waits for completion.  AEISU_ERR_UNSUPPORTED for other precisions. */
+int aeisu_activation_stats(aeisu_t* handle, const uint8_t* src, int n, int h, int w, unsigned flags,
+                           float* peaks, float* means, void* stream);
+
 /* Wait for all work enqueued on the handle's stream (or `stream`) for at most
  * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
  * reconstruction since the last call produced a non-finite value. */

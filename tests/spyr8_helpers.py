@@ -19,10 +19,15 @@ def layer_weights(state):
     return out
 
 
-def activation_scales(state, frames):
-    """Per-layer absmax/448 of the FP32 activations the mixed route quantises."""
+def activation_stats(state, frames):
+    """CPU restatement of aeisu_activation_stats: per-layer max |x| of the FP32 activations the
+    mixed route quantises (activation_scales order) and the FP8 layers' input-channel means
+    (compress in unshuffle order c*4 + phase, bottleneck 0-3 and expand), over the padded
+    frames, pixels weighted equally."""
     st = O.FoldedModel(state).state
     peaks = np.zeros(10)
+    sums = np.zeros(448)
+    count = np.zeros(448)
     for frame in frames:
         src = O.u8_to_chw(frame)
         h, w = src.shape[1:]
@@ -35,18 +40,31 @@ def activation_scales(state, frames):
         enc = O.leaky(conv("project_540", O.pixel_unshuffle(feat)))
         low = O.leaky(conv("compress_270", O.pixel_unshuffle(enc)))
         vals = [O.pixel_unshuffle(feat), enc, low]
+        ins = [O.pixel_unshuffle(enc), low]
         a, b = low[:, :32], low[:, 32:]
         for i in range(1, 5):
             a = O.leaky(conv(f"bottleneck_270_a{i}", a))
             b = O.leaky(conv(f"bottleneck_270_b{i}", b))
             vals.append(np.concatenate([a, b], 1))
+            ins.append(vals[-1])
         exp = O.leaky(conv("expand_270", np.concatenate([a, b], 1)))
         dec_in = enc + O.pixel_shuffle(exp)
         dec = O.leaky(conv("refine_540", dec_in))
         vals += [exp, dec_in, dec]
         for k, v in enumerate(vals):
             peaks[k] = max(peaks[k], float(np.abs(v).max()))
-    return (np.maximum(peaks, 1e-6) / 448.0).astype(np.float32)
+        o = 0
+        for v in ins:   # compress input, bottleneck 0-3 inputs, expand input
+            c = v.shape[1]
+            sums[o:o + c] += v.sum(axis=(0, 2, 3), dtype=np.float64)
+            count[o:o + c] += v.shape[0] * v.shape[2] * v.shape[3]
+            o += c
+    return peaks.astype(np.float32), (sums / count).astype(np.float32)
+
+
+def activation_scales(state, frames):
+    """Per-layer absmax/448 of the FP32 activations the mixed route quantises."""
+    return (np.maximum(activation_stats(state, frames)[0], 1e-6) / 448.0).astype(np.float32)
 
 
 def build_artifact(state, frames, tensors_override=None):
