@@ -152,8 +152,9 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                         const __half2* h2 = reinterpret_cast<const __half2*>(&o[c]);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            q[8 * c + 2 * e] = __low2float(h2[e]) * inv_s1;
-                            q[8 * c + 2 * e + 1] = __high2float(h2[e]) * inv_s1;
+                            const float2 w = __fmul2_rn(__half22float2(h2[e]), f2(inv_s1));
+                            q[8 * c + 2 * e] = w.x;
+                            q[8 * c + 2 * e + 1] = w.y;
                         }
                     }
                     uint4 o8[2];
@@ -191,27 +192,33 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                     g[a][c] = v.w;
                     if (a >= 1 && a <= 2 && c >= 1 && c <= 2) rgb[a - 1][c - 1] = make_float3(v.x, v.y, v.z);
                 }
+            // the two LR pixels of row i (j = 0, 1) as the two lanes of packed f32x2 operations
             float f[32];
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < 2; ++i) {
+                const float2 R = make_float2(rgb[i][0].x, rgb[i][1].x), G = make_float2(rgb[i][0].y, rgb[i][1].y),
+                             B = make_float2(rgb[i][0].z, rgb[i][1].z);
+                auto gp = [&](int a, int c) { return make_float2(g[a][c], g[a][c + 1]); };   // columns c, c+1
+                const float2 ul = gp(i, 0), uc = gp(i, 1), ur = gp(i, 2);
+                const float2 cl = gp(i + 1, 0), cr = gp(i + 1, 2);
+                const float2 dl = gp(i + 2, 0), dc = gp(i + 2, 1), dr = gp(i + 2, 2);
+                const float2 hmid = sub2(cr, cl), vmid = sub2(dc, uc);
+                float2 v[8];
+                v[0] = mix3x2(R, G, B, s_st[0], s_st[1], s_st[2]);
+                v[1] = mix3x2(R, G, B, s_st[3], s_st[4], s_st[5]);
+                v[2] = mix3x2(R, G, B, s_st[6], s_st[7], s_st[8]);
+                v[3] = gp(i + 1, 1);
+                v[4] = mix3x2(sub2(ur, ul), hmid, sub2(dr, dl), s_st[12], s_st[13], s_st[14]);
+                v[5] = mix3x2(sub2(dl, ul), vmid, sub2(dr, ur), s_st[15], s_st[16], s_st[17]);
+                v[6] = mix3x2(sub2(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
+                v[7] = __fadd2_rn(sub2(__fmul2_rn(sub2(ur, dl), f2(s_st[21])), __fmul2_rn(vmid, f2(s_st[22]))),
+                                  __fmul2_rn(hmid, f2(s_st[23])));
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int p = i * 2 + j;
-                    const float3 c = rgb[i][j];
-                    f[0 * 4 + p] = mix3(c.x, c.y, c.z, s_st[0], s_st[1], s_st[2]);
-                    f[1 * 4 + p] = mix3(c.x, c.y, c.z, s_st[3], s_st[4], s_st[5]);
-                    f[2 * 4 + p] = mix3(c.x, c.y, c.z, s_st[6], s_st[7], s_st[8]);
-                    f[3 * 4 + p] = g[i + 1][j + 1];
-                    const float ul = g[i][j], uc = g[i][j + 1], ur = g[i][j + 2];
-                    const float cl = g[i + 1][j], cr = g[i + 1][j + 2];
-                    const float dl = g[i + 2][j], dc = g[i + 2][j + 1], dr = g[i + 2][j + 2];
-                    const float hmid = __fsub_rn(cr, cl), vmid = __fsub_rn(dc, uc);
-                    f[4 * 4 + p] = mix3(__fsub_rn(ur, ul), hmid, __fsub_rn(dr, dl), s_st[12], s_st[13], s_st[14]);
-                    f[5 * 4 + p] = mix3(__fsub_rn(dl, ul), vmid, __fsub_rn(dr, ur), s_st[15], s_st[16], s_st[17]);
-                    f[6 * 4 + p] = mix3(__fsub_rn(dr, ul), vmid, hmid, s_st[18], s_st[19], s_st[20]);
-                    f[7 * 4 + p] = __fadd_rn(__fsub_rn(__fmul_rn(__fsub_rn(ur, dl), s_st[21]), __fmul_rn(vmid, s_st[22])),
-                                             __fmul_rn(hmid, s_st[23]));
+                for (int k = 0; k < 8; ++k) {   // feature k of LR pixel p = 2i + j is channel 4k + p
+                    f[4 * k + 2 * i] = v[k].x;
+                    f[4 * k + 2 * i + 1] = v[k].y;
                 }
+            }
             uint4 fa[4];
             pack_f16x32(f, fa);
             uint8_t* a_b = sA + b * 4 * kM * 16;
@@ -1063,11 +1070,15 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
             // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
             // floats per channel plane
             if (x0 + t < xe) {
-                // one test for all twelve values: a non-finite term makes the sum non-finite
-                float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
-                all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
-                all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
-                if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
+                // One test for all twelve values: a non-finite term makes the sum non-finite.  Only
+                // float sources can make one: with uint8 sources every tap value lies in [0, 1]
+                // and every filter weight is finite (clamped coefficients times a finite bank).
+                if (src.kind != 0) {
+                    float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
+                    all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
+                    all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
+                    if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
+                }
                 const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {

@@ -65,6 +65,16 @@ __device__ __forceinline__ float mix3(float a, float b, float c, float w0, float
     return __fadd_rn(__fadd_rn(__fmul_rn(a, w0), __fmul_rn(b, w1)), __fmul_rn(c, w2));
 }
 
+// The same operations on two lanes at once: packed f32x2 arithmetic rounds each lane exactly
+// as the scalar instruction does, so results are bit-identical.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {   // a - b: a + (-1)*b, one rounding
+    return __ffma2_rn(b, f2(-1.f), a);
+}
+__device__ __forceinline__ float2 mix3x2(float2 a, float2 b, float2 c, float w0, float w1, float w2) {
+    return __fadd2_rn(__fadd2_rn(__fmul2_rn(a, f2(w0)), __fmul2_rn(b, f2(w1))), __fmul2_rn(c, f2(w2)));
+}
+
 // Source pixel at padded-grid coordinate (py, px) of frame f (replicate padding by clamping).
 // `lut` maps uint8 to value/255 (correctly rounded, as read_rgb's float division).
 __device__ __forceinline__ float3 load_src(const SrcDesc& s, int f, int py, int px, const float* lut) {
