@@ -180,3 +180,23 @@ def test_tensor_core_routes_report_and_launch_counts():
         assert "tcgen05" in model.report
     finally:
         model.close()
+
+
+@pytest.mark.parametrize("precision", ["fp16", "mixed"])
+@pytest.mark.parametrize("w", [220, 470])
+def test_strip_edges_match_the_restatement(precision, w):
+    """Widths whose padded grid leaves a 2- or 4-pixel last strip in the 3x3 kernels (126-pixel
+    strips): every output column must follow the CPU restatement, checked per column so that
+    one wrong column cannot hide in a frame-wide PSNR."""
+    data = staged("adaptive_fp8.bin").read_bytes()
+    restated = M.QuantizedModel(spyr8.read_spyr8(data), precision, headroom=2.0)
+    model = Model.from_spyr8_bytes(data, "cuda:0", precision)
+    try:
+        src = O.u8_to_chw(make_frame(1300 + w, 40, w))
+        ref = np.clip(O.upscale(restated, src, 0), 0, 1)
+        got = np.clip(model.upscale_f32(src, 0), 0, 1)
+        col_err = np.abs(got - ref).max(axis=(0, 1))
+        bound = 0.01 if precision == "fp16" else 0.06
+        assert col_err.max() <= bound, (int(col_err.argmax()), float(col_err.max()))
+    finally:
+        model.close()
