@@ -858,15 +858,20 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                         }
 #pragma unroll
                         for (int n = 0; n < 32; n += 2) {   // coefficient_clamp
-                            // v if |v| <= 2, else sign(v) * min(2 + 0.05 (|v| - 2), 2.5): for |v| <= 2
+                            // v if |v| <= 2, else sign(v) * min(2 + 0.05 (|v| - 2), 2.5).  For |v| <= 2
                             // the soft term is >= |v| (also after rounding), so one min covers both
-                            // cases.  min.xorsign.abs(v, c) = sign(v) * min(|v|, c) for c > 0, and a
-                            // NaN v (soft term NaN) maps to sign * 2.5 as the reference's select does
+                            // cases.  The soft term is monotone and reaches exactly 2.5 at |v| = 12
+                            // (fma(0.05f, 10, 2) rounds to 2.5f), so min(soft(|v|), 2.5) =
+                            // soft(min(|v|, 12)).  min.xorsign.abs(v, c) = sign(v) * min(|v|, c) for
+                            // c > 0; a NaN v gives min(NaN, 12) = 12, so sign * 2.5, as the
+                            // reference's select does
                             const float2 soft = __ffma2_rn(make_float2(0.05f, 0.05f),
-                                                           make_float2(fabsf(v[n]) - 2.f, fabsf(v[n + 1]) - 2.f),
+                                                           __fadd2_rn(make_float2(fminf(fabsf(v[n]), 12.f),
+                                                                                  fminf(fabsf(v[n + 1]), 12.f)),
+                                                                      make_float2(-2.f, -2.f)),
                                                            make_float2(2.f, 2.f));
-                            v[n] = min_xorsign_abs(v[n], fminf(soft.x, 2.5f));
-                            v[n + 1] = min_xorsign_abs(v[n + 1], fminf(soft.y, 2.5f));
+                            v[n] = min_xorsign_abs(v[n], soft.x);
+                            v[n + 1] = min_xorsign_abs(v[n + 1], soft.y);
                         }
                         uint4 q[4];
                         pack_f16x32(v, q);
