@@ -648,14 +648,19 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     cta_teardown(tmem, 2 * ACC);
 }
 
-// refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core.
+// refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core, two
+// output rows at a time.  Input rows y and y+1 feed both output rows y and y+1 with different
+// taps, so their MMAs have N = 128: B = [W_ky; W_ky+1] (the weights are stored ky-innermost,
+// so the two 64-row blocks are adjacent) writes output row y+1 to TMEM columns 0-63 and
+// output row y to 64-127 of the pair's buffer.  Rows y-1 and y+2 feed one output row each
+// (N = 64).  A pair takes 12 MMAs of N = 128 and 12 of N = 64 instead of 36 of N = 64, and the
+// A operand of the shared rows is read once.
 // The refine output (LeakyReLU, f16) goes to shared memory as the tail GEMM's A operand and
-// never reaches HBM.  Warp 8 (producer) issues refine(y) into TMEM buffer y&1 and refills the
-// TMA ring.  Two epilogue warpgroups (warps 0-3 and 4-7) take alternate rows, each owning one
-// TMEM buffer and one tail operand: refine epilogue of its row, then (after a barrier of its
-// own 128 threads) one of its threads issues the row's tail GEMM, then the tail epilogue.  The
-// producer never waits for a tail, so the refine GEMMs of successive rows follow each other
-// on the tensor core while the epilogues run.
+// never reaches HBM.  Warp 8 (producer) issues the pair's refine GEMMs into TMEM buffer
+// pair&1 and refills the TMA ring.  Epilogue warpgroup w (warps 4w..4w+3) takes output row
+// y + w of every pair: refine epilogue, then (after a barrier of its own 128 threads) one of
+// its threads issues the row's tail GEMM into the same 64 columns, then the tail epilogue;
+// the buffer returns to the producer when both warpgroups have read their tails.
 // The tail epilogue writes clamped f16 coefficients in the head's layout
 // meta[r][Y][2][X][8 f16]: LR pixel (Y, X) = (2y + i, 2x + j) takes channels
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
@@ -687,6 +692,7 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                                                                int band, int* err) {
     constexpr int ICH = 4, LBO = kM * 16, SLOT = ICH * LBO;   // a 128-pixel window per chunk
     constexpr int BREF = 36 * 64 * 16, BTAIL = 8 * 64 * 16, A2 = 8 * kM * 16;
+    constexpr int WBLK = 64 * 16, WLBO = 3 * WBLK;   // weights [kx][k4][ky][64 rows][16 B]
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;   // refine weights
@@ -696,17 +702,17 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
     // ring slots, then per buffer b: ref_full, tail_full (count 1); slot_free (count 1); then
-    // per buffer ref_empty (count 4)
+    // per buffer pair_empty (count 8: every epilogue warp)
     __shared__ alignas(8) uint64_t s_bar[kRing + 7];
     uint64_t* ref_full = s_bar + kRing;
     uint64_t* tail_full = s_bar + kRing + 2;
     uint64_t* slot_free = s_bar + kRing + 4;
-    uint64_t* ref_empty = s_bar + kRing + 5;
+    uint64_t* pair_empty = s_bar + kRing + 5;
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
     if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
     if (threadIdx.x == 0)
-        for (int i = kRing + 5; i < kRing + 7; ++i) mbar_init(&s_bar[i], 4);
+        for (int i = kRing + 5; i < kRing + 7; ++i) mbar_init(&s_bar[i], 8);
     fence_async_smem();
     cta_setup(&s_tmem, s_bar, kRing + 5, 256);
     const uint32_t tmem = s_tmem;
@@ -714,14 +720,14 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     const int nstrip = (pw + kConvStrip - 1) / kConvStrip, nband = (ph + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    constexpr uint32_t idesc = idesc_m128(64);
+    constexpr uint32_t idesc64 = idesc_m128(64), idesc128 = idesc_m128(128);
 
     if (warp == 8) {
         // ---- producer: the whole warp follows the control flow, lane 0 issues ----
         const bool leader = lane == 0;
         const uint32_t b0 = smem_addr(sB);
         Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-        uint32_t issued = 0, seen = 0;   // rows committed; rows [0, seen) observed complete here
+        uint32_t pairs = 0, seen = 0;   // pairs committed; pairs [0, seen) observed complete here
         bool ok = true;
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
@@ -730,89 +736,96 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
             }
             ring.pending |= 1u << Ring::slot(row);
         };
-        // wait until the refine MMAs of row j (and so of every earlier row) have completed
-        auto done = [&](uint32_t j) {
-            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[j & 1], (j >> 1) & 1, err, kErrTimeout));
-            if (r) seen = j + 1;
+        // wait until the refine MMAs of pair q (and so of every earlier pair) have completed
+        auto done = [&](uint32_t q) {
+            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_full[q & 1], (q >> 1) & 1, err, kErrTimeout));
+            if (r) seen = q + 1;
             return r;
+        };
+        // the 6 MMAs of input row `row` with the weights of tap row ky (and ky+1 when n128) into d
+        auto taps = [&](uint32_t d, int row, int ky, bool n128, bool first) {
+            const uint32_t a = ring.addr(row);
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk)
+                    mma_f16(d, sdesc(a + 2 * kk * LBO + kx * 16, LBO, 128),
+                            sdesc(b0 + ((kx * 4 + 2 * kk) * 3 + ky) * WBLK, WLBO, 128), n128 ? idesc128 : idesc64,
+                            !(first && kx == 0 && kk == 0));
         };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
             // the previous item's last MMAs still read the ring: let them finish before refilling it
-            if (seen < issued && !(ok = done(issued - 1))) break;
+            if (seen < pairs && !(ok = done(pairs - 1))) break;
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
-            for (int y = sb.y0; y < sb.y1 && ok; ++y) {
-                const uint32_t j = issued;
-                const int b = j & 1;
-                const uint32_t k = j >> 1;
-                if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&ref_empty[b], (k - 1) & 1, err, kErrTimeout));
+            for (int y = sb.y0; y < sb.y1 && ok; y += 2) {   // bands hold whole pairs
+                const uint32_t p = pairs;
+                const int b = p & 1;
+                const uint32_t k = p >> 1;
+                // buffer b free: both warpgroups read the tails of pair p-2
+                if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&pair_empty[b], (k - 1) & 1, err, kErrTimeout));
                 if (!ok) break;
                 fence_after_sync();
-                auto taps = [&](int ky) {   // the 6 MMAs of input row y-1+ky
-                    const uint32_t row = ring.addr(y - 1 + ky);
-#pragma unroll
-                    for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                        for (int kk = 0; kk < 2; ++kk)
-                            mma_f16(tmem + b * 128, sdesc(row + 2 * kk * LBO + kx * 16, LBO, 128),
-                                    sdesc(b0 + ((ky * 3 + kx) * 4 + 2 * kk) * 64 * 16, 64 * 16, 128), idesc,
-                                    ky > 0 || kx > 0 || kk > 0);
-                };
+                const uint32_t d = tmem + b * 128;
                 if (leader) {
-                    taps(0);
-                    commit(slot_free);   // row y-1's slot is read by nothing after these
-                    taps(1);
+                    taps(d, y, 0, true, true);        // [W0; W1] x row y: the first MMA initialises both rows
+                    taps(d + 64, y - 1, 0, false, false);   // W0 x row y-1 -> output row y
+                    commit(slot_free);                 // rows y-1 and y are read by nothing after these
                 }
                 __syncwarp();
                 ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
+                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 2, err));
                 if (ok) {
                     fence_after_sync();
-                    if (leader) taps(2);
+                    if (leader) {
+                        taps(d, y + 1, 1, true, false);   // [W1; W2] x row y+1
+                        taps(d, y + 2, 2, false, false);  // W2 x row y+2 -> output row y+1
+                    }
                 }
                 // commit even on abort, so that the teardown's wait covers every issued MMA
                 if (leader) commit(&ref_full[b]);
                 __syncwarp();
-                ++issued;
-                // row y+3 into the slot of row y-1 once its taps completed
-                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, j & 1, err, kErrTimeout));
+                ++pairs;
+                // rows y+3, y+4 into the slots of rows y-1, y once their MMAs completed (issued
+                // twelve MMAs ago, so the wait is normally over at once)
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, p & 1, err, kErrTimeout));
                 if (!ok) break;
                 if (y + 3 <= sb.y1) load(y + 3, sb);
+                if (y + 4 <= sb.y1) load(y + 4, sb);
             }
         }
         // let copies and MMAs still in flight land before TMEM is released (MMAs complete in
         // issue order, so the last commit covers them all)
         ring.drain(err);
-        if (seen < issued)
-            mbar_wait_bounded(&ref_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
+        if (seen < pairs)
+            mbar_wait_bounded(&ref_full[(pairs - 1) & 1], ((pairs - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
     } else {
-        // ---- epilogue: warpgroup wg takes the rows whose counter has parity wg ----
+        // ---- epilogue: warpgroup wg takes output row y + wg of every pair ----
         // Loop exits are decided only by the warpgroup's barrier vote (`live`), never by one
         // warp alone, so no warp can leave while the others wait at the warpgroup barrier.
         const int wg = warp >> 2, tq = t & 127;
         const uint32_t lrow = uint32_t(32 * (warp & 3)) << 16;
+        const uint32_t half = wg == 0 ? 64 : 0;   // TMEM columns of this warpgroup's row in a pair buffer
         uint8_t* a2 = sA2 + wg * A2;
         const uint32_t a2addr = smem_addr(a2), t0 = smem_addr(sT);
-        uint32_t it = 0, tail_phase = 0;
+        uint32_t p = 0, tail_phase = 0;
         bool live = true, bad = false;   // bad: a wait of this warp expired (voted at the next barrier)
         bool tail_pend = false;          // thread tq == 0 committed a tail not yet observed
         for (long long item = blockIdx.x; item < items && live; item += gridDim.x) {
             last_item(item, items);
             const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
             const int x = sb.x0 + tq;
-            for (int y = sb.y0; y < sb.y1 && live; ++y, ++it) {
-                if (int(it & 1) != wg) continue;
-                const uint32_t k = it >> 1;
+            for (int y0 = sb.y0; y0 < sb.y1 && live; y0 += 2, ++p) {
+                const int b = p & 1, y = y0 + wg;
+                const uint32_t col = tmem + lrow + b * 128 + half;
                 // refine epilogue -> tail operand of this row
-                if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_idle(&ref_full[wg], k & 1, err, kErrTimeout));
+                if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_idle(&ref_full[b], (p >> 1) & 1, err, kErrTimeout));
                 if (!bad) {
                     fence_after_sync();
                     float vr[2][32];
-                    tmem_ld32x2(tmem + lrow + wg * 128, tmem + lrow + wg * 128 + 32, vr[0], vr[1]);
-                    fence_before_sync();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&ref_empty[wg]);
+                    tmem_ld32x2(col, col + 32, vr[0], vr[1]);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         epi_add_leaky(vr[h], s_rb + h * 32, slope);
@@ -823,7 +836,8 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                     }
                     fence_async_smem();
                 }
-                // the whole operand is written (and every warp's previous tail read is done)
+                // the whole operand is written, every warp's refine columns are read (the tail
+                // overwrites them) and every warp's previous tail read is done
                 fence_before_sync();
                 if (warpgroup_sync_or(wg, bad)) {
                     live = false;
@@ -833,8 +847,8 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                     fence_after_sync();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_f16(tmem + wg * 128 + 64, sdesc(a2addr + kk * 2 * kM * 16, kM * 16, 128),
-                                sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc, kk > 0);
+                        mma_f16(tmem + b * 128 + half, sdesc(a2addr + kk * 2 * kM * 16, kM * 16, 128),
+                                sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc64, kk > 0);
                     commit(&tail_full[wg]);
                     tail_pend = true;
                 }
@@ -845,7 +859,10 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                 tail_pend = false;
                 fence_after_sync();
                 float vt[2][32];
-                tmem_ld32x2(tmem + lrow + wg * 128 + 64, tmem + lrow + wg * 128 + 96, vt[0], vt[1]);
+                tmem_ld32x2(col, col + 32, vt[0], vt[1]);
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pair_empty[b]);   // this warp's part of the buffer is read
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float (&v)[32] = vt[h];
@@ -1258,7 +1275,7 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
     {
         const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
         const long long strips = (long long)rs.R * ((pw + kConvStrip - 1) / kConvStrip);
-        const int band = pick_band(strips, ph, sms * 2);
+        const int band = (pick_band(strips, ph, sms * 2) + 1) & ~1;   // whole row pairs (ph is even)
         const long long items = strips * ((ph + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM);
         smem_attr(k_tc_refine_tail, bytes);

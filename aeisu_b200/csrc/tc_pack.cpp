@@ -99,11 +99,14 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         epilogue(P.expand, L, 128, s[6], s[7], torch_out);
         P.expand.out_deq = fp8 ? s[7] : 1.f;
     }
-    // refine_540: [64][9 taps x 32], f16 in both routes; metadata_head [64][64] f16
+    // refine_540: [64][9 taps x 32] f16 in both routes, chunks ordered [kx][k4][ky] (k4: 8 input
+    // channels) so that the blocks of tap rows ky and ky+1 are adjacent and one N = 128 operand
+    // covers both; metadata_head [64][64] f16
     {
         const LayerWeights& R = m.layers[kRefine];
-        P.refine = append_bytes(P.bytes, pack_operand(64, 288, 2, [&](int n, int kk) {
-            return R.w_fp16[(size_t(n) * 32 + kk % 32) * 9 + kk / 32];
+        P.refine = append_bytes(P.bytes, pack_operand(64, 288, 2, [&](int n, int kv) {
+            const int c = kv / 8, ky = c % 3, k4 = (c / 3) % 4, kx = c / 12;
+            return R.w_fp16[(size_t(n) * 32 + k4 * 8 + kv % 8) * 9 + ky * 3 + kx];
         }));
         P.refine_bias = append_floats(P.floats, R.bias);
         const LayerWeights& T = m.layers[kTail];
