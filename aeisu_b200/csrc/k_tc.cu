@@ -479,47 +479,47 @@ struct Ring {
 
 // Grouped (2 x 32->32) 3x3 bottleneck layer, warp-specialised: warp 4 is the producer (TMA
 // row loads and MMA issue, lane 0 issuing), warps 0-3 are the epilogue (warp w drains TMEM
-// lanes 32w..32w+31).  The two sides meet only on mbarriers:
-//   acc_full[b]  tcgen05.commit of row y's MMAs into TMEM buffer b  -> epilogue, producer
+// lanes 32w..32w+31).  The two groups (independent 32->32 convolutions) run in separate CTAs
+// (even blockIdx: group 0, odd: group 1), each staging only its group's input channels and
+// weights.  Output rows go in pairs, as in k_tc_refine_tail: input rows y and y+1 feed both
+// output rows of a pair, so their MMAs have N = 64 over the adjacent weight blocks of tap
+// rows ky and ky+1 (output row y+1 in TMEM columns 0-31 of the pair buffer, y in 32-63);
+// rows y-1 and y+2 feed one output row each (N = 32).  The two sides meet only on mbarriers:
+//   acc_full[b]  tcgen05.commit of a pair's MMAs into TMEM buffer b  -> epilogue, producer
 //   acc_empty[b] one arrive per epilogue warp once it has read buffer b -> producer
-// so the epilogue never waits for MMA issue and there is no CTA-wide barrier per row.  The
-// producer issues the taps of input rows y-1 and y before it waits for row y+1 to land, and
-// refills the slot of row y-1 with row y+3 as soon as the row y-1 taps have completed
+// The producer issues the taps of input rows y-1 and y before it waits for rows y+1 and y+2
+// to land, and refills their slots with rows y+3 and y+4 once those taps completed
 // (slot_free).
 constexpr int kWsThreads = 160;
 
-// NG = groups per CTA.  With NG = 1 the two groups (independent 32->32 convolutions) run in
-// separate CTAs (even blockIdx: group 0, odd: group 1), each staging only its group's input
-// channels and weights: half the shared memory, so twice the CTAs per SM (the FP16 route).
-template <bool FP8, int NG>
+template <bool FP8>
 __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                         const uint8_t* __restrict__ wimg, EpiParams ep,
                                                         void* __restrict__ out, int band, int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
-    constexpr int CPG = ICH / 2;              // chunks per group
-    constexpr int RCH = NG * CPG;             // chunks staged per row
-    constexpr int ACC = NG * 32;              // TMEM columns of one accumulator buffer
-    constexpr int LBO = kM * 16, SLOT = RCH * LBO;   // a 128-pixel window per chunk
-    constexpr int BG = 9 * CPG * 32 * 16;     // bytes of one group's weights
-    const int gb = NG == 2 ? 0 : int(blockIdx.x & 1);                     // first group of this CTA
-    const long long cta = NG == 2 ? blockIdx.x : blockIdx.x >> 1, stride = NG == 2 ? gridDim.x : gridDim.x >> 1;
+    constexpr int CPG = ICH / 2;              // chunks per group (staged per row)
+    constexpr int LBO = kM * 16, SLOT = CPG * LBO;   // a 128-pixel window per chunk
+    constexpr int WBLK = 32 * 16, WLBO = 3 * WBLK;  // weights [kx][chunk][ky][32 rows][16 B]
+    constexpr int BG = 9 * CPG * WBLK;        // bytes of one group's weights
+    const int gb = int(blockIdx.x & 1);      // this CTA's group
+    const long long cta = blockIdx.x >> 1, stride = gridDim.x >> 1;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;
-    float* s_scale = reinterpret_cast<float*>(sB + NG * BG);
-    float* s_bias = s_scale + 64;
+    float* s_scale = reinterpret_cast<float*>(sB + BG);
+    float* s_bias = s_scale + 32;
     __shared__ uint32_t s_tmem;
     // ring slots, acc_full x2, slot_free (count 1), acc_empty x2 (count 4)
     __shared__ alignas(8) uint64_t s_bar[kRing + 5];
     uint64_t* acc_full = s_bar + kRing;
     uint64_t* slot_free = s_bar + kRing + 2;
     uint64_t* acc_empty = s_bar + kRing + 3;
-    copy_image(sB, wimg + gb * BG, NG * BG);
-    if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
+    copy_image(sB, wimg + gb * BG, BG);
+    if (threadIdx.x < 32) { s_scale[threadIdx.x] = ep.scale[gb * 32 + threadIdx.x]; s_bias[threadIdx.x] = ep.bias[gb * 32 + threadIdx.x]; }
     if (threadIdx.x == 0)
         for (int b = 0; b < 2; ++b) mbar_init(&acc_empty[b], 4);
     fence_async_smem();
-    cta_setup(&s_tmem, s_bar, kRing + 3, 2 * ACC);
+    cta_setup(&s_tmem, s_bar, kRing + 3, 128);
     const uint32_t tmem = s_tmem;
     const int lh = rs.rh / 4, lw = rs.rw / 4;
     const int nstrip = (lw + kConvStrip - 1) / kConvStrip, nband = (lh + band - 1) / band;
@@ -530,9 +530,9 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
         // ---- producer: the whole warp follows the control flow, lane 0 issues ----
         const bool leader = lane == 0;
         const uint32_t b0 = smem_addr(sB);
-        constexpr uint32_t idesc = idesc_m128(32);
+        constexpr uint32_t idesc32 = idesc_m128(32), idesc64 = idesc_m128(64);
         Ring ring{smem, smem_addr(smem), SLOT, s_bar};
-        uint32_t issued = 0, seen = 0;   // rows committed; rows [0, seen) observed complete here
+        uint32_t pairs = 0, seen = 0;   // pairs committed; pairs [0, seen) observed complete here
         bool ok = true;
         auto load = [&](int row, const StripBand& sb) {
             if (leader) {
@@ -541,111 +541,113 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
             }
             ring.pending |= 1u << Ring::slot(row);
         };
-        // wait until the MMAs of row j (and so of every earlier row) have completed
-        auto done = [&](uint32_t j) {
-            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[j & 1], (j >> 1) & 1, err, kErrTimeout));
-            if (r) seen = j + 1;
+        // wait until the MMAs of pair q (and so of every earlier pair) have completed
+        auto done = [&](uint32_t q) {
+            const bool r = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[q & 1], (q >> 1) & 1, err, kErrTimeout));
+            if (r) seen = q + 1;
             return r;
+        };
+        // the MMAs of input row `row` with the weights of tap row ky (and ky+1 when n64) into d
+        auto taps = [&](uint32_t d, int row, int ky, bool n64, bool first) {
+            const uint32_t a = ring.addr(row);
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int kk = 0; kk < CPG / 2; ++kk) {
+                    const uint64_t ad = sdesc(a + 2 * kk * LBO + kx * 16, LBO, 128);
+                    const uint64_t bd = sdesc(b0 + ((kx * CPG + 2 * kk) * 3 + ky) * WBLK, WLBO, 128);
+                    const bool acc = !(first && kx == 0 && kk == 0);
+                    if (FP8) mma_e4m3(d, ad, bd, n64 ? idesc64 : idesc32, acc);
+                    else mma_f16(d, ad, bd, n64 ? idesc64 : idesc32, acc);
+                }
         };
         for (long long item = cta; item < items && ok; item += stride) {
             last_item(item, items, stride);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh, kConvStrip);
             // the previous item's last MMAs still read the ring: let them finish before refilling it
-            if (seen < issued && !(ok = done(issued - 1))) break;
+            if (seen < pairs && !(ok = done(pairs - 1))) break;
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
             for (int row = sb.y0 - 1; row <= sb.y0 && ok; ++row) ok = __all_sync(0xffffffffu, ring.wait(row, err));
-            for (int y = sb.y0; y < sb.y1 && ok; ++y) {
-                const uint32_t j = issued;
-                const int b = j & 1;
-                const uint32_t k = j >> 1;
-                // buffer b free: its previous row drained
+            for (int y = sb.y0; y < sb.y1 && ok; y += 2) {   // bands hold whole pairs
+                const uint32_t p = pairs;
+                const int b = p & 1;
+                const uint32_t k = p >> 1;
+                // buffer b free: its previous pair drained
                 if (k > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_empty[b], (k - 1) & 1, err, kErrTimeout));
                 if (!ok) break;
                 fence_after_sync();
-                // taps of input row y-1+ky; row y+1 (ky = 2) is waited for only after the
-                // first two rows' MMAs are queued
-                auto taps = [&](int ky) {
-                    const uint32_t row = ring.addr(y - 1 + ky);
-#pragma unroll
-                    for (int g = 0; g < NG; ++g)
-#pragma unroll
-                        for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                            for (int kk = 0; kk < CPG / 2; ++kk) {
-                                const uint64_t a = sdesc(row + (g * CPG + 2 * kk) * LBO + kx * 16, LBO, 128);
-                                const uint64_t bd = sdesc(b0 + g * BG + ((ky * 3 + kx) * CPG + 2 * kk) * 32 * 16, 32 * 16, 128);
-                                const uint32_t d = tmem + b * ACC + g * 32;
-                                const bool acc = ky > 0 || kx > 0 || kk > 0;
-                                if (FP8) mma_e4m3(d, a, bd, idesc, acc); else mma_f16(d, a, bd, idesc, acc);
-                            }
-                };
+                const uint32_t d = tmem + b * 64;
                 if (leader) {
-                    taps(0);
-                    commit(slot_free);   // row y-1's slot is read by nothing after these
-                    taps(1);
+                    taps(d, y, 0, true, true);              // [W0; W1] x row y: the first MMA initialises both rows
+                    taps(d + 32, y - 1, 0, false, false);   // W0 x row y-1 -> output row y
+                    commit(slot_free);                       // rows y-1 and y are read by nothing after these
                 }
                 __syncwarp();
                 ok = __all_sync(0xffffffffu, ring.wait(y + 1, err));
+                if (ok) ok = __all_sync(0xffffffffu, ring.wait(y + 2, err));
                 if (ok) {
                     fence_after_sync();
-                    if (leader) taps(2);
+                    if (leader) {
+                        taps(d, y + 1, 1, true, false);    // [W1; W2] x row y+1
+                        taps(d, y + 2, 2, false, false);   // W2 x row y+2 -> output row y+1
+                    }
                 }
                 // commit even on abort, so that the teardown's wait covers every issued MMA
                 if (leader) commit(&acc_full[b]);
                 __syncwarp();
-                ++issued;
-                // Row y+3 goes into the slot of row y-1, free once the ky = 0 MMAs completed (they
-                // were followed by the other taps, so the wait is normally over at once).
-                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, j & 1, err, kErrTimeout));
+                ++pairs;
+                // rows y+3, y+4 into the slots of rows y-1, y once their MMAs completed (issued
+                // before the second half of the pair, so the wait is normally over at once)
+                if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(slot_free, p & 1, err, kErrTimeout));
                 if (!ok) break;
                 if (y + 3 <= sb.y1) load(y + 3, sb);
+                if (y + 4 <= sb.y1) load(y + 4, sb);
             }
         }
         // let copies and MMAs still in flight land before TMEM is released (MMAs complete in
         // issue order, so the last commit covers them all)
         ring.drain(err);
-        if (seen < issued)
-            mbar_wait_bounded(&acc_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
+        if (seen < pairs)
+            mbar_wait_bounded(&acc_full[(pairs - 1) & 1], ((pairs - 1) >> 1) & 1, err, kErrTimeout, 200000000LL);
     } else {
-        // ---- epilogue warps ----
-        uint32_t it = 0;
+        // ---- epilogue warps: both rows of a pair ----
+        uint32_t p = 0;
         bool ok = true;
         for (long long item = cta; item < items && ok; item += stride) {
             last_item(item, items, stride);
             const StripBand sb = strip_band(item, nstrip, nband, band, lh, kConvStrip);
             const int x = sb.x0 + t;
-            for (int y = sb.y0; y < sb.y1; ++y, ++it) {
-                const int b = it & 1;
-                ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], (it >> 1) & 1, err, kErrTimeout));
+            for (int y0 = sb.y0; y0 < sb.y1; y0 += 2, ++p) {
+                const int b = p & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], (p >> 1) & 1, err, kErrTimeout));
                 if (!ok) break;
                 fence_after_sync();
 #pragma unroll
-                for (int h = 0; h < NG; ++h) {
+                for (int r = 0; r < 2; ++r) {   // output row y0 + r: TMEM columns 32 (r = 0) or 0 (r = 1)
                     float v[32];
-                    tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * ACC + h * 32, v);
-                    const int c0 = (gb + h) * 32;   // first output channel of this group
-                    if (h == NG - 1) {   // every column read: hand the buffer back to the producer
+                    tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 64 + (1 - r) * 32, v);
+                    if (r == 1) {   // every column read: hand the buffer back to the producer
                         fence_before_sync();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
-                    epi_fma_leaky(v, s_scale + c0, s_bias + c0, ep.slope, FP8 ? ep.out_inv : 1.f);
+                    epi_fma_leaky(v, s_scale, s_bias, ep.slope, FP8 ? ep.out_inv : 1.f);
                     if (t < kConvStrip && x < lw) {
                         if (FP8) {
                             uint4 q[2];
                             pack_e4m3x32(v, q);
-                            for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y, ICH, (gb + h) * 2 + c, lw, x) = q[c];
+                            for (int c = 0; c < 2; ++c) *cp_at(out, sb.r, lh, y0 + r, ICH, gb * 2 + c, lw, x) = q[c];
                         } else {
                             uint4 q[4];
                             pack_f16x32(v, q);
-                            for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y, ICH, (gb + h) * 4 + c, lw, x) = q[c];
+                            for (int c = 0; c < 4; ++c) *cp_at(out, sb.r, lh, y0 + r, ICH, gb * 4 + c, lw, x) = q[c];
                         }
                     }
                 }
             }
         }
     }
-    cta_teardown(tmem, 2 * ACC);
+    cta_teardown(tmem, 128);
 }
 
 // refine_540 (3x3 32->64) + metadata_head (1x1 64->64), warp-specialised like k_tc_core, two
@@ -1245,23 +1247,22 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         else { smem_attr(k_tc_compress<false>, bytes); launch(pdl, k_tc_compress<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
     }
     {
-        // FP8: one CTA runs both groups (4 CTAs per SM); FP16: one group per CTA, the halved
-        // shared memory lets 4 CTAs share an SM instead of 2
-        const int ich = fp8 ? 4 : 8, ng = fp8 ? 2 : 1, rch = ng * ich / 2;
-        const int bytes = 1024 + kRing * rch * kM * 16 + ng * 9 * (ich / 2) * 32 * 16 + 2 * 64 * 4;
-        const int slots = sms * 4 / (3 - ng);   // CTA slots for one group's work items
+        // one group per CTA (two CTAs per work item), four CTAs per SM; bands hold whole row pairs
+        const int ich = fp8 ? 4 : 8, cpg = ich / 2;
+        const int bytes = 1024 + kRing * cpg * kM * 16 + 9 * cpg * 32 * 16 + 2 * 32 * 4;
+        const int slots = sms * 2;   // work items in flight: two CTAs each
         const long long strips = (long long)rs.R * ((lw + kConvStrip - 1) / kConvStrip);
-        const int band = pick_band(strips, lh, slots);
+        const int band = (pick_band(strips, lh, slots) + 1) & ~1;   // lh is a multiple of 8
         const long long items = strips * ((lh + band - 1) / band);
-        const unsigned grid = (3 - ng) * grid_for(items, slots / sms, sms);
-        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM, rch);
-        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM, rch);
+        const unsigned grid = 2 * grid_for(items, 2, sms);
+        const CUtensorMap map_a = make_row_window_map(low_a, rs.R, lh, ich, lw, kM, cpg);
+        const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM, cpg);
         void* bufs[2] = {low_a, low_b};
         const CUtensorMap* maps[2] = {&map_a, &map_b};
-        if (fp8) smem_attr(k_tc_core<true, 2>, bytes); else smem_attr(k_tc_core<false, 1>, bytes);
+        if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
         for (int i = 0; i < 4; ++i) {
-            if (fp8) launch(pdl, k_tc_core<true, 2>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else launch(pdl, k_tc_core<false, 1>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            if (fp8) launch(pdl, k_tc_core<true>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            else launch(pdl, k_tc_core<false>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
         }
     }
     mark(2);

@@ -75,14 +75,16 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         }));
         epilogue(P.compress, L, 64, s[1], s[2], [](int i) { return i; });
     }
-    // bottleneck i: two groups of [32 out][9 taps x 32 in], K order tap*32 + c
+    // bottleneck i: two groups of [32 out][9 taps x 32 in], chunks ordered [kx][chunk][ky] so
+    // that the blocks of tap rows ky and ky+1 are adjacent and one N = 64 operand covers both
     for (int i = 0; i < 4; ++i) {
         const LayerWeights& L = m.layers[kCore0 + i];
         std::vector<uint8_t> img;
+        const int epc = 16 / es, cpg = 32 / epc;   // elements per 16-byte chunk, chunks per tap
         for (int g = 0; g < 2; ++g) {
-            auto part = pack_operand(32, 288, es, [&](int n, int kk) {
-                const int tap = kk / 32, c = kk % 32;
-                return elem(L, (size_t(g * 32 + n) * 32 + c) * 9 + tap);
+            auto part = pack_operand(32, 288, es, [&](int n, int kv) {
+                const int c = kv / epc, ky = c % 3, kc = (c / 3) % cpg, kx = c / (3 * cpg);
+                return elem(L, (size_t(g * 32 + n) * 32 + kc * epc + kv % epc) * 9 + ky * 3 + kx);
             });
             img.insert(img.end(), part.begin(), part.end());
         }
