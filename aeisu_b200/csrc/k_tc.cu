@@ -964,9 +964,13 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
     const long long items = (long long)rs.R * nstrip * nband;
     const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB);
     constexpr uint32_t idesc = idesc_m128(128);
-    const bool two = t + kThreads < kHeadTW;   // this thread stages a second window column
+    // Work beside the apply is spread over the warps, so that no warp arrives late at the row
+    // barrier: the last warp stages the four extra window columns, warp 1 issues the MMAs.
+    constexpr int kExtra = kHeadTW - kThreads;   // window columns beyond one per thread (4)
+    const bool two = t >= kThreads - kExtra;    // this thread stages a second window column
+    const int issuer = 32;
     bool ok = true;
-    bool pend = false;   // thread 0: an MMA round was committed and not yet waited for
+    bool pend = false;   // issuing thread: an MMA round was committed and not yet waited for
     auto issue = [&](int b) {   // MMA round of the row whose coefficients sit in sA[b]
         fence_after_sync();
         const uint64_t a = sdesc(smem_addr(sA[b]), kM * 16, 128);
@@ -991,7 +995,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
         int sx[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
-            sx[j] = clampi(reg.z + clampi(x0 - 2 + t + j * kThreads, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+            sx[j] = clampi(reg.z + clampi(x0 - 2 + t + j * kExtra, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
         auto src_raw = [&](int row, int j) -> uint3 {
             const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
             if (src.kind == 0) {
@@ -1005,7 +1009,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
         auto slot = [&](int row) { return (row - y0 + 2) & (kHeadRing - 1); };
         auto put = [&](int row, int j, uint3 raw) {   // value of column col: first of pair col, second of col-1
             const float3 v = finish_src(src, raw, s_lut);
-            const int col = t + j * kThreads;
+            const int col = t + j * kExtra;
             float2(&ps)[3][kHeadTW] = s_pair[slot(row)];
             ps[0][col].x = v.x; ps[1][col].x = v.y; ps[2][col].x = v.z;
             if (col > 0) { ps[0][col - 1].y = v.x; ps[1][col - 1].y = v.y; ps[2][col - 1].y = v.z; }
@@ -1030,7 +1034,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
         fence_async_smem();
         fence_before_sync();
         __syncthreads();
-        if (t == 0) issue(0);
+        if (t == issuer) issue(0);
         for (int y = y0; y < y1; ++y) {
             const int b = (y - y0) & 1;
             // prefetch: next row's coefficients (async) and source row y+3 (registers)
@@ -1138,12 +1142,12 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                 ok = false;
                 break;
             }
-            if (t == 0 && next) issue(b ^ 1);
+            if (t == issuer && next) issue(b ^ 1);
         }
     }
     if (!ok) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
         cp_async_wait_all();
-        if (t == 0 && pend) mbar_wait_bounded(&s_bar, phase, err, kErrTimeout, 200000000LL);
+        if (t == issuer && pend) mbar_wait_bounded(&s_bar, phase, err, kErrTimeout, 200000000LL);
     }
     cta_teardown(tmem, 128);
 }
