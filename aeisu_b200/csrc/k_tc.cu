@@ -85,6 +85,13 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
     const int t = threadIdx.x, warp = t >> 5;
     const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
     constexpr int PER = (kProjTW + kThreads - 1) / kThreads;   // staged columns per thread (3)
+    // Column j of this thread: t and t + 128, and the last two threads also stage the two
+    // columns beyond 256; warp 1 issues the MMAs.  The extra work sits in different warps
+    // from the first, so no warp arrives late at the row barrier carrying both.
+    constexpr int kLast = kProjTW - (PER - 1) * kThreads;     // columns of the last pass (2)
+    auto col_of = [&](int j) { return j < PER - 1 ? t + j * kThreads : t - (kThreads - kLast) + (PER - 1) * kThreads; };
+    auto stages = [&](int j) { return j < PER - 1 || t >= kThreads - kLast; };
+    const int issuer = 32;
     bool ok = true;
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
         last_item(item, items);
@@ -96,7 +103,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
         int sx[PER];
 #pragma unroll
         for (int j = 0; j < PER; ++j)
-            sx[j] = clampi(reg.z + clampi(2 * sb.x0 - 1 + t + j * kThreads, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+            sx[j] = clampi(reg.z + clampi(2 * sb.x0 - 1 + col_of(j), 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
         auto raw_at = [&](int row, int j) -> uint3 {
             const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
             if (src.kind == 0) {
@@ -109,21 +116,21 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
         };
         auto put = [&](int row, int j, uint3 raw) {
             const float3 v = finish_src(src, raw, s_lut);
-            s_src[slot(row)][t + j * kThreads] = make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
+            s_src[slot(row)][col_of(j)] = make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
         };
         auto fetch2 = [&](int row, uint3 (&pre)[2][PER]) {   // raw loads of rows row, row+1
 #pragma unroll
             for (int k = 0; k < 2; ++k)
 #pragma unroll
                 for (int j = 0; j < PER; ++j)
-                    if (t + j * kThreads < kProjTW) pre[k][j] = raw_at(row + k, j);
+                    if (stages(j)) pre[k][j] = raw_at(row + k, j);
         };
         auto put2 = [&](int row, const uint3 (&pre)[2][PER]) {
 #pragma unroll
             for (int k = 0; k < 2; ++k)
 #pragma unroll
                 for (int j = 0; j < PER; ++j)
-                    if (t + j * kThreads < kProjTW) put(row + k, j, pre[k][j]);
+                    if (stages(j)) put(row + k, j, pre[k][j]);
         };
         // epilogue of packed row qy from TMEM buffer b: enc540 and the compress input
         auto epilogue = [&](int qy, int b) {
@@ -172,7 +179,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
         for (int row = base_row; row <= 2 * sb.y0 + 2; ++row)
 #pragma unroll
             for (int j = 0; j < PER; ++j)
-                if (t + j * kThreads < kProjTW) put(row, j, raw_at(row, j));
+                if (stages(j)) put(row, j, raw_at(row, j));
         uint3 pre_cur[2][PER];
         if (sb.y0 + 1 < sb.y1) fetch2(2 * sb.y0 + 3, pre_cur);
         __syncthreads();
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             fence_async_smem();
             fence_before_sync();
             if (__syncthreads_or(!ok)) { ok = false; break; }   // also spreads an epilogue failure
-            if (t == 0) {
+            if (t == issuer) {
                 fence_after_sync();
                 constexpr uint32_t idesc = idesc_m128(32);
 #pragma unroll
@@ -248,7 +255,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
         if (ok && sb.y1 > sb.y0 && !epilogue(sb.y1 - 1, (sb.y1 - 1 - sb.y0) & 1)) ok = false;
         if (__syncthreads_or(!ok)) ok = false;
     }
-    if (!ok && t == 0)   // abort path: let committed MMAs land before TMEM is freed
+    if (!ok && t == issuer)   // abort path: let committed MMAs land before TMEM is freed
         for (int b = 0; b < 2; ++b)
             if (pend & (1u << b)) mbar_wait_bounded(&s_bar[b], (phase >> b) & 1u, err, kErrTimeout, 200000000LL);
     cta_teardown(tmem, 64);
