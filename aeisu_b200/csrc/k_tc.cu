@@ -901,13 +901,11 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                         }
                         uint4 q[4];
                         pack_f16x32(v, q);
+                        // LR pixels (2y + h, 2x) and (2y + h, 2x + 1) are adjacent in each chunk
+                        // plane: chunk c of both in one 32-byte store (2x is even, rw a multiple of 32)
 #pragma unroll
-                        for (int pp = 0; pp < 2; ++pp) {
-                            const int parity = h * 2 + pp;
-                            const int Y = 2 * y + (parity >> 1), X = 2 * x + (parity & 1);
-#pragma unroll
-                            for (int c = 0; c < 2; ++c) *cp_at(meta, sb.r, rs.rh, Y, 2, c, rs.rw, X) = q[pp * 2 + c];
-                        }
+                        for (int c = 0; c < 2; ++c)
+                            st_global_2x16(cp_at(meta, sb.r, rs.rh, 2 * y + h, 2, c, rs.rw, 2 * x), q[c], q[2 + c]);
                     }
                 }
             }
