@@ -1129,9 +1129,10 @@ __global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs,
                         const uint2 q45 = u8_code_bits2(out[2 * i + 1][1], out[2 * i + 1][2]);
                         uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
                                                                   ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
-                        o[0] = uint16_t(__byte_perm(q01.x, q01.y, 0x0040));
-                        o[1] = uint16_t(__byte_perm(q23.x, q23.y, 0x0040));
-                        o[2] = uint16_t(__byte_perm(q45.x, q45.y, 0x0040));
+                        // streaming stores: the frame is read back only by the host copy
+                        __stcs(reinterpret_cast<unsigned short*>(o), (unsigned short)__byte_perm(q01.x, q01.y, 0x0040));
+                        __stcs(reinterpret_cast<unsigned short*>(o + 1), (unsigned short)__byte_perm(q23.x, q23.y, 0x0040));
+                        __stcs(reinterpret_cast<unsigned short*>(o + 2), (unsigned short)__byte_perm(q45.x, q45.y, 0x0040));
                     }
                 }
             }

@@ -187,9 +187,10 @@ __device__ __forceinline__ uint4* cp_at(const void* base, int r, int H, int y, i
 }
 
 // Two 16-byte chunks to consecutive chunk positions with one 32-byte store (p 32-byte aligned):
-// a warp storing pixel pairs then writes whole sectors instead of every other half.
+// a warp storing pixel pairs then writes whole sectors instead of every other half.  Streaming
+// (.cs): the data is read back once, by the next kernel, after far more than L2 has passed.
 __device__ __forceinline__ void st_global_2x16(uint4* p, const uint4& a, const uint4& b) {
-    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+    asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
                  :: "l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
                  : "memory");
 }
