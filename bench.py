@@ -73,17 +73,53 @@ def gen_frames(seed, count, h, w, degradation):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of the benchmarked GPU, sampled during the
+    timed region: NVML every ~10 ms (the timed region can be under 100 ms), else nvidia-smi."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clock-event reason bits (nvml.h: SwPowerCap 0x4, HwSlowdown 0x8, SwThermal 0x20, HwThermal 0x40)
+    BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, device_index):
+    def __init__(self, device_index, period=0.01):
         self.device_index = device_index
+        self.period = period
         self.proc = None
-        self.lines = []
+        self.thread = None
+        self.stop = threading.Event()
+        self.lines = []     # nvidia-smi csv lines
+        self.samples = []   # NVML (sm_mhz, max_mhz, reason bits)
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:   # the CUDA device's own NVML handle (CUDA and NVML indices can differ)
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.device_index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+
+    def _poll(self, nvml, handle):
+        while not self.stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+                bits = nvml.nvmlDeviceGetCurrentClocksThrottleReasons(handle)
+                self.samples.append((float(sm), float(mx), int(bits)))
+            except Exception:
+                return
+            self.stop.wait(self.period)
 
     def __enter__(self):
+        try:
+            nvml, handle = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, args=(nvml, handle), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -100,16 +136,22 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        elif self.thread:
+            self.thread.join(timeout=2)
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for s_mhz, m_mhz, bits in self.samples:
+            sm.append(s_mhz)
+            mx.append(m_mhz)
+            reasons.update(n for n in self.NAMES if bits & self.BITS[n])
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 8:
@@ -119,13 +161,13 @@ class ClockSampler:
                 mx.append(float(parts[1]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[4:8]):
+            for name, val in zip(self.NAMES, parts[4:8]):
                 if val.lower() == "active":
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 def measured_peaks():
