@@ -59,6 +59,7 @@ _SIGNATURES = {
     "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
     "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "aeisu_set_timeout": (C.c_int, [C.c_void_p, C.c_double]),
+    "aeisu_set_workspace_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
     "aeisu_report": (C.c_char_p, [C.c_void_p]),
     "aeisu_device_bytes": (C.c_uint64, [C.c_void_p]),
     "aeisu_kernel_launches": (C.c_uint64, [C.c_void_p]),

@@ -110,6 +110,7 @@ public:
     const aeisu_timings& timings();
     void set_detailed(bool on) { detailed_ = on; }
     void set_timeout(double ms) { timeout_ms_ = ms; }
+    void set_workspace_cap(size_t bytes) { workspace_cap_ = bytes; }
     int precision() const { return precision_; }
     int device() const { return device_; }
 

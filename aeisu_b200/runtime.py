@@ -180,6 +180,10 @@ class Model:
     def set_timeout(self, ms: float):
         _lib.check(_lib.lib().aeisu_set_timeout(self._handle(), float(ms)))
 
+    def set_workspace_limit(self, nbytes: int):
+        """Bound the intermediate-tensor bytes of one call; larger batches run in passes."""
+        _lib.check(_lib.lib().aeisu_set_workspace_limit(self._handle(), int(nbytes)))
+
     def synchronize(self, stream=None, timeout_ms=60000.0):
         _lib.check(_lib.lib().aeisu_synchronize(self._handle(), stream, float(timeout_ms)))
 

@@ -181,6 +181,11 @@ int aeisu_set_detailed_timing(aeisu_t* handle, int enabled);
 /* Bound, in milliseconds, on every host wait for GPU completion (default 60000). */
 int aeisu_set_timeout(aeisu_t* handle, double timeout_ms);
 
+/* Bound on the intermediate-tensor bytes one call allocates (default 6 GiB).  A batch of
+ * regions (frames or tiles) that needs more is run in several passes of as many regions as
+ * fit, at least one; the results are the same.  For hosts with a device memory budget. */
+int aeisu_set_workspace_limit(aeisu_t* handle, uint64_t bytes);
+
 /* Startup report (device, artifact hash, precision, kernel route), like
  * CudaRuntime::StartupReport (SrcPyrCudaRuntime.cu:3739-3783).  Valid until close. */
 const char* aeisu_report(aeisu_t* handle);

@@ -200,3 +200,18 @@ def test_strip_edges_match_the_restatement(precision, w):
         assert col_err.max() <= bound, (int(col_err.argmax()), float(col_err.max()))
     finally:
         model.close()
+
+
+@pytest.mark.parametrize("precision,tile", [("mixed", 0), ("fp16", 64), ("fp32", 0)])
+def test_workspace_limit_runs_the_batch_in_passes(precision, tile):
+    """A workspace limit smaller than one region forces one region per pass (the region
+    tables, workspace and launches of every pass); the frames must come out unchanged."""
+    model = load_model(staged("adaptive_fp8.bin" if precision != "fp32" else "aeisu_area.pt"), "cuda:0", precision)
+    try:
+        frames = make_frames(1400, 5, 80, 112)
+        whole = model.upscale_u8(frames, tile)
+        model.set_workspace_limit(1)
+        np.testing.assert_array_equal(model.upscale_u8(frames, tile), whole)
+        model.set_workspace_limit(6 << 30)
+    finally:
+        model.close()
