@@ -55,6 +55,8 @@ _SIGNATURES = {
                                              C.c_uint, C.c_void_p]),
     "aeisu_activation_stats": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint, C.c_void_p,
                                          C.c_void_p, C.c_void_p]),
+    "aeisu_distortion": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint, C.c_int,
+                                   C.c_void_p, C.c_void_p]),
     "aeisu_synchronize": (C.c_int, [C.c_void_p, C.c_void_p, C.c_double]),
     "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
     "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),

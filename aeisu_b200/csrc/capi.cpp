@@ -9,6 +9,7 @@
 
 #include "common.h"
 #include "engine.h"
+#include "kernels.h"
 #include "model.h"
 #include "noalloc.h"
 
@@ -167,6 +168,15 @@ int aeisu_activation_stats(aeisu_t* handle, const uint8_t* src, int n, int h, in
         check_io(n, h, w, flags);
         engine_of(handle).activation_stats(src, flags == AEISU_IO_HOST, n, h, w, peaks, means,
                                            static_cast<cudaStream_t>(stream));
+    });
+}
+
+int aeisu_distortion(const float* prediction, const float* target, int n, int h, int w, int crop, unsigned flags,
+                     int device, double* out, void* stream) {
+    return guarded([&] {
+        aeisu::require(flags == AEISU_IO_HOST || flags == AEISU_IO_DEVICE, "unknown I/O flags");
+        aeisu::distortion(prediction, target, n, h, w, crop, flags == AEISU_IO_HOST, device, out,
+                          static_cast<cudaStream_t>(stream));
     });
 }
 

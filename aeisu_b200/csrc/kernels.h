@@ -97,4 +97,10 @@ void launch_f32_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst
                      const float* meta, const float* base, const float* basis, int* nonfinite,
                      cudaStream_t s, int* launches);
 
+// Encoded-Y MSE / PSNR / SSIM of n image pairs (aeisu/metrics.py:17-39), k_metrics.cu.
+// out[3f .. 3f+2] = y_mse, y_psnr, y_ssim of frame f; waits for completion.
+void distortion(const float* pred, const float* tgt, int n, int h, int w, int crop, bool host_io, int device,
+                double* out, cudaStream_t stream);
+int metric_launches_per_call(int crop);
+
 }  // namespace aeisu

@@ -233,6 +233,51 @@ def measure_latency(dev, runs, distinct=16):
     return res
 
 
+def measure_metrics(dev, out_u8, pairs, cpu_pairs=1):
+    """Evaluation metrics (aeisu_distortion: encoded-Y MSE/PSNR + 11x11 Gaussian SSIM in FP64) on
+    `pairs` float32 CHW pairs of the step's output size, device resident: CUDA events around
+    batched calls on the launching stream; beside it the FP64 numpy port on `cpu_pairs` pair(s)."""
+    import torch
+    from aeisu_b200 import metrics
+    from oracle import metrics_np as M
+    m = min(pairs, out_u8.shape[0])
+    target = out_u8[:m].permute(0, 3, 1, 2).float().div(255).contiguous()
+    gen = torch.Generator(device=dev).manual_seed(7)
+    pred = (target + 0.01 * torch.randn(target.shape, generator=gen, device=dev)).contiguous()
+    _, _, H, W = target.shape
+    stream = torch.cuda.Stream(dev)
+    runs = 10
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            metrics.distortion_batch(pred, target)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(runs):
+            scores = metrics.distortion_batch(pred, target)
+        end.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / runs
+    px = m * H * W
+    hbm = measured_peaks()[0]
+    nbytes = 2 * 3 * 4 * px
+    p0, t0 = pred[0].cpu().numpy(), target[0].cpu().numpy()
+    c0 = time.perf_counter()
+    for _ in range(cpu_pairs):
+        ref = M.distortion(p0, t0)
+    cpu_s = (time.perf_counter() - c0) / cpu_pairs
+    return {"value": px / (ms / 1e3) / 1e6, "unit": "pixel pairs Mpix/s", "ms_per_call": ms, "pairs_per_call": m,
+            "frame": f"{W}x{H}", "dtype": "f32 in, f64 arithmetic",
+            "hbm": {"achieved": nbytes / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "frac": nbytes / (ms / 1e3) / 1e9 / hbm},
+            "fp64_flop_per_px": 284,
+            "check_vs_port": {"y_ssim_abs_diff": abs(scores[0]["y_ssim"] - ref["y_ssim"]),
+                              "y_mse_abs_diff": abs(scores[0]["y_mse"] - ref["y_mse"])},
+            "cpu_port": {"value": H * W / cpu_s / 1e6, "unit": "pixel pairs Mpix/s", "cores": 1,
+                         "kind": "port", "sample": f"{cpu_pairs} pair(s) {W}x{H}, numpy FP64"},
+            "config": "the step's upscaled frames as targets, +N(0, 0.01) as predictions, crop 2, "
+                      f"{runs} batched calls after 3 warm-up calls, inputs in HBM"}
+
+
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
     """Time the reference algorithm's CPU implementation (the oracle port, FP32, all host
     threads) on a bounded sample of the workload's frames."""
@@ -294,6 +339,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--latency-runs", type=int, default=1000,
                     help="1080p->4K single-frame latency runs (0 disables)")
+    ap.add_argument("--metric-pairs", type=int, default=8,
+                    help="image pairs per call of the evaluation-metrics measurement (0 disables)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -380,6 +427,8 @@ def main():
     stage_ms = {k: v / args.steps for k, v in stage_sum.items() if k.endswith("_ms")}
 
     latency = measure_latency(dev, args.latency_runs) if (rank == 0 and args.latency_runs > 0) else None
+    metric_line = (measure_metrics(dev, out, args.metric_pairs)
+                   if (rank == 0 and args.metric_pairs > 0 and not band) else None)
 
     # end-to-end through the public API with pinned host buffers
     host_src = torch.from_numpy(frames).pin_memory()
@@ -442,6 +491,7 @@ def main():
                     "steps": e2e_steps},
             "gpu_launches": int(launches),
             "latency_1080p": latency,
+            "evaluation_metrics": metric_line,
             "clocks": clocks.summary(),
             "report": model.report,
         }

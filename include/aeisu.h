@@ -158,6 +158,20 @@ int aeisu_predict_coefficients(aeisu_t* handle, const float* src, int n, int h, 
 int aeisu_activation_stats(aeisu_t* handle, const uint8_t* src, int n, int h, int w, unsigned flags,
                            float* peaks, float* means, void* stream);
 
+/* Evaluation metrics, no model needed: distortion() of aeisu/metrics.py:17-39 (called per image
+ * pair by evaluate.py:41) on n pairs of float32 CHW images (3 x h x w each: the prediction as
+ * upscale returns it, the target as read_rgb gives it), computed in FP64 on GPU `device`:
+ * prediction clamped to [0, 1], both cropped by `crop` pixels per side, BT.601 encoded luma,
+ * out[3i + 0] = y_mse, out[3i + 1] = y_psnr (+inf when the MSE is 0), out[3i + 2] = y_ssim
+ * (mean over the valid 11x11 Gaussian windows, sigma 1.5).  Results agree with the reference
+ * to FP64 rounding (separable window sums; the reference's own tolerance for these figures is
+ * 2e-10).  flags: AEISU_IO_HOST or AEISU_IO_DEVICE for both images; `out` is host memory and
+ * the call waits.  AEISU_ERR_INVALID_ARG when min(h, w) < 11 + 2 crop or crop < 0;
+ * AEISU_ERR_NONFINITE when any value of either image is not finite (that pair's outputs are
+ * NaN, the others are still written). */
+int aeisu_distortion(const float* prediction, const float* target, int n, int h, int w, int crop,
+                     unsigned flags, int device, double* out, void* stream);
+
 /* Wait for all work enqueued on the handle's stream (or `stream`) for at most
  * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
  * reconstruction since the last call produced a non-finite value. */
