@@ -180,6 +180,21 @@ int aeisu_distortion(const float* prediction, const float* target, int n, int h,
     });
 }
 
+uint64_t aeisu_png_bound(int h, int w) {
+    uint64_t r = 0;
+    const int st = guarded([&] { r = aeisu::png_bound(h, w); });
+    return st == AEISU_OK ? r : 0;
+}
+
+int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned flags, int device, uint8_t* out,
+                     uint64_t capacity, uint64_t* sizes, void* stream) {
+    return guarded([&] {
+        aeisu::require(flags == AEISU_IO_HOST || flags == AEISU_IO_DEVICE, "unknown I/O flags");
+        aeisu::png_encode(frames, kind, n, h, w, flags == AEISU_IO_HOST, device, out, capacity, sizes,
+                          static_cast<cudaStream_t>(stream));
+    });
+}
+
 int aeisu_synchronize(aeisu_t* handle, void* stream, double timeout_ms) {
     return guarded([&] { engine_of(handle).synchronize(static_cast<cudaStream_t>(stream), timeout_ms); });
 }

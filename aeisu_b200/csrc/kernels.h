@@ -103,4 +103,10 @@ void distortion(const float* pred, const float* tgt, int n, int h, int w, int cr
                 double* out, cudaStream_t stream);
 int metric_launches_per_call(int crop);
 
+// PNG files of n frames (k_png.cu): kind 0 uint8 HWC, kind 1 float32 CHW quantised as save_rgb.
+uint64_t png_bound(int h, int w);
+void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, int device, uint8_t* out,
+                uint64_t capacity, uint64_t* sizes, cudaStream_t stream);
+int png_launches_per_call();
+
 }  // namespace aeisu

@@ -278,6 +278,40 @@ def measure_metrics(dev, out_u8, pairs, cpu_pairs=1):
                       f"{runs} batched calls after 3 warm-up calls, inputs in HBM"}
 
 
+def measure_png(out_u8, frames):
+    """PNG egress (aeisu_png_encode): `frames` of the step's uint8 output, device resident, encoded
+    per call into host memory (the D2H copy of the files is inside the timed region); beside it
+    the reference's save_rgb encoder (PIL, zlib level 6) on one frame of the same output."""
+    import io
+    import torch
+    from PIL import Image
+    from aeisu_b200 import codec
+    m = min(frames, out_u8.shape[0])
+    x = out_u8[:m].contiguous()
+    for _ in range(2):
+        files = codec.encode_png(x)
+    torch.cuda.synchronize(x.device)
+    runs = 5
+    t0 = time.perf_counter()
+    for _ in range(runs):
+        files = codec.encode_png(x)
+    dt = (time.perf_counter() - t0) / runs
+    _, H, W, _ = x.shape
+    ours = sum(len(f) for f in files) / m
+    frame = x[0].cpu().numpy()
+    c0 = time.perf_counter()
+    buf = io.BytesIO()
+    Image.fromarray(frame).save(buf, format="PNG")
+    pil_s = time.perf_counter() - c0
+    return {"value": m * H * W / dt / 1e6, "unit": "Mpix/s encoded", "ms_per_call": dt * 1e3, "frames_per_call": m,
+            "frame": f"{W}x{H}", "bytes_per_frame": ours, "raw_bytes_per_frame": H * W * 3,
+            "pil_bytes_per_frame": len(buf.getvalue()),
+            "cpu_reference": {"value": H * W / pil_s / 1e6, "unit": "Mpix/s encoded", "cores": 1,
+                              "kind": "reference", "sample": f"PIL PNG save of 1 frame {W}x{H} (save_rgb's encoder)"},
+            "config": "the step's uint8 output frames in HBM, files returned to host memory; wall clock over "
+                      f"{runs} calls after 2 warm-up calls"}
+
+
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
     """Time the reference algorithm's CPU implementation (the oracle port, FP32, all host
     threads) on a bounded sample of the workload's frames."""
@@ -339,6 +373,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--latency-runs", type=int, default=1000,
                     help="1080p->4K single-frame latency runs (0 disables)")
+    ap.add_argument("--png-frames", type=int, default=8,
+                    help="frames per call of the PNG egress measurement (0 disables)")
     ap.add_argument("--metric-pairs", type=int, default=8,
                     help="image pairs per call of the evaluation-metrics measurement (0 disables)")
     args = ap.parse_args()
@@ -429,6 +465,7 @@ def main():
     latency = measure_latency(dev, args.latency_runs) if (rank == 0 and args.latency_runs > 0) else None
     metric_line = (measure_metrics(dev, out, args.metric_pairs)
                    if (rank == 0 and args.metric_pairs > 0 and not band) else None)
+    png_line = measure_png(out, args.png_frames) if (rank == 0 and args.png_frames > 0 and not band) else None
 
     # end-to-end through the public API with pinned host buffers
     host_src = torch.from_numpy(frames).pin_memory()
@@ -492,6 +529,7 @@ def main():
             "gpu_launches": int(launches),
             "latency_1080p": latency,
             "evaluation_metrics": metric_line,
+            "png_egress": png_line,
             "clocks": clocks.summary(),
             "report": model.report,
         }

@@ -16,6 +16,8 @@
  *   aeisu.runtime.load_model               aeisu/runtime.py:45-56
  *   aeisu.runtime.upscale                  aeisu/runtime.py:70-103
  *   FoldedAEISU.forward / predict_coefficients   aeisu/model.py:494-551
+ *   aeisu.metrics.distortion               aeisu/metrics.py:17-39 (evaluate.py:41)
+ *   aeisu.runtime.save_rgb (PNG egress)    aeisu/runtime.py:23-27 (infer.py, evaluate.py:48)
  * The Python binding that mirrors aeisu.runtime over this ABI is aeisu_b200/runtime.py.
  */
 #ifndef AEISU_B200_H
@@ -171,6 +173,26 @@ int aeisu_activation_stats(aeisu_t* handle, const uint8_t* src, int n, int h, in
  * NaN, the others are still written). */
 int aeisu_distortion(const float* prediction, const float* target, int n, int h, int w, int crop,
                      unsigned flags, int device, double* out, void* stream);
+
+/* PNG egress on the GPU: the files save_rgb writes (aeisu/runtime.py:23-27), for n frames at
+ * once.  kind AEISU_PNG_U8: frames are uint8 h x w x 3 (HWC, as aeisu_upscale_u8 writes them);
+ * kind AEISU_PNG_F32: frames are float32 3 x h x w (CHW, as aeisu_upscale_f32 writes them),
+ * quantised as save_rgb does (clamp to [0, 1], floor(x * 255 + 0.5)).  The files are 8-bit RGB,
+ * non-interlaced, adaptively filtered per row; their pixels decode to exactly save_rgb's, the
+ * compressed stream is the encoder's own (literal-only dynamic Huffman blocks, not zlib's
+ * LZ77), so the file bytes and sizes differ from PIL's.  flags: where the frames are,
+ * AEISU_IO_HOST or AEISU_IO_DEVICE (on GPU `device`); `out` may be host or device memory.
+ * The n files are written back to back into `out` (capacity bytes;
+ * n * aeisu_png_bound(h, w) always suffices) and sizes[i]
+ * (host) receives each file's length; AEISU_ERR_INVALID_ARG if they do not fit (sizes[] is
+ * filled first).  Widths above 32768 are rejected.  The call waits for completion. */
+#define AEISU_PNG_U8  0
+#define AEISU_PNG_F32 1
+int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned flags, int device,
+                     uint8_t* out, uint64_t capacity, uint64_t* sizes, void* stream);
+
+/* Largest PNG file aeisu_png_encode can produce for one h x w frame (0 for an empty size). */
+uint64_t aeisu_png_bound(int h, int w);
 
 /* Wait for all work enqueued on the handle's stream (or `stream`) for at most
  * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
