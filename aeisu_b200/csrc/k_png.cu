@@ -1,20 +1,23 @@
 // PNG encoding on the GPU: the file save_rgb writes (aeisu/runtime.py:23-27: clamp,
 // floor(x * 255 + 0.5), 8-bit RGB PNG through PIL), produced from frames already in HBM.
-// The decoded pixels are the reference's; the compressed bytes differ (PIL runs zlib's LZ77 at
-// level 6, this encoder codes literals only).
+// The decoded pixels are the reference's; the compressed bytes differ (PIL runs zlib at level 6
+// with hash chains and lazy matching, this encoder one candidate per position and a greedy
+// parse).
 //
 // Pipeline per call (all frames of the batch at once):
 //   k_png_filter   one CTA per image row: the row and the row above are staged in shared
 //                  memory, the five PNG filters (None, Sub, Up, Average, Paeth) are scored by
 //                  the sum of |residual| as signed bytes (the usual adaptive choice) and the
 //                  filter byte + filtered row are written to the frame's zlib input stream.
-//   k_png_deflate  one CTA per 60 KiB segment of that stream: per-warp histograms, the
-//                  segment's literal Huffman code (deflate.cuh, one thread), a block scan of
-//                  the per-thread bit counts, then every thread packs its bytes' codes into a
-//                  shared-memory bit buffer.  A segment is one dynamic block; all but the last
-//                  end with an empty stored block so that the next starts on a byte boundary.
-//                  A segment whose code would not be smaller than the raw bytes is stored.
-//                  Adler-32 partial sums of the segment come out of the histogram pass.
+//   k_png_deflate  one CTA per 60 KiB segment of that stream: LZ77 match candidates from a
+//                  shared-memory hash table, a greedy parse per thread, the segment's Huffman
+//                  codes (deflate.cuh, one thread; a literal-only code is built beside it by
+//                  another thread and the smaller block wins), a block scan of the per-thread
+//                  bit counts, then every thread packs its tokens into a shared-memory bit
+//                  buffer.  A segment is one dynamic block; all but the last end with an empty
+//                  stored block so that the next starts on a byte boundary.  A segment whose
+//                  code would not be smaller than the raw bytes is stored.  Adler-32 partial
+//                  sums of the segment come out of the hashing pass.
 //   k_png_layout   one CTA per frame: segment offsets (scan), Adler-32, the PNG framing.
 //   k_png_gather   copies every segment to its place in the file.
 //   k_png_crc      CRC-32 of the IDAT chunk: 256 bytes per thread (table), combined across
@@ -44,6 +47,9 @@ constexpr int kSlot = kSeg + 64;            // bytes reserved per coded segment
 constexpr int kFiltThreads = 256;
 constexpr int kDefThreads = 512;
 constexpr int kDefWarps = kDefThreads / 32;
+constexpr int kChunk = kSeg / kDefThreads;    // bytes parsed per thread (120)
+constexpr int kHashBits = 13;
+constexpr int kDefSmem = kSlot + 2 * kSeg;    // bit buffer (hash table before it) + candidates
 constexpr int kCrcChunk = 256;              // bytes per thread
 constexpr int kCrcThreads = 512;
 constexpr long long kCrcSpan = (long long)kCrcChunk * kCrcThreads;
@@ -199,55 +205,124 @@ struct BitOut {
     }
 };
 
-__global__ void __launch_bounds__(kDefThreads) k_png_deflate(PngGeom g, const uint8_t* __restrict__ filt,
-                                                             uint8_t* __restrict__ slots, uint32_t* seg_bytes,
-                                                             unsigned long long* seg_s1, unsigned long long* seg_s2) {
-    extern __shared__ uint32_t obuf[];   // kSlot bytes
+// One CTA per segment.  Phase A finds, for every position, the nearest earlier position with
+// the same four bytes (a hash table of last positions in shared memory, filled in rounds of
+// kDefThreads positions: a position sees the positions of earlier rounds, reaching back over
+// the previous 32 KiB of the frame's stream, so matches may cross into the previous segment).
+// Pass 1: each thread parses its 120 bytes greedily (longest of the hash candidate, distance 1
+// and the row above, at least 4 bytes, cut at the thread's end), keeps its tokens in global
+// scratch and counts symbols.  Thread 0 builds the codes of that parse, thread 32 the codes of
+// a literal-only block of the same bytes; the smaller wins (or stored bytes, if smaller still).
+// Pass 2 sums each thread's bits for the scan; pass 3 packs them.
+__device__ __forceinline__ uint32_t hash4(const uint8_t* p) {
+    const uint32_t v = uint32_t(p[0]) | uint32_t(p[1]) << 8 | uint32_t(p[2]) << 16 | uint32_t(p[3]) << 24;
+    return (v * 2654435761u) >> (32 - kHashBits);
+}
+
+__global__ void __launch_bounds__(kDefThreads, 1) k_png_deflate(PngGeom g, const uint8_t* __restrict__ filt,
+                                                                uint8_t* __restrict__ slots, uint32_t* __restrict__ tokens,
+                                                                uint32_t* seg_bytes, unsigned long long* seg_s1,
+                                                                unsigned long long* seg_s2) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    uint32_t* obuf = reinterpret_cast<uint32_t*>(dsm);             // kSlot bytes; the hash table before
+    int* table = reinterpret_cast<int*>(dsm);                       // (1 << kHashBits) ints
+    uint16_t* dist16 = reinterpret_cast<uint16_t*>(dsm + kSlot);    // kSeg: hash candidate distance
     __shared__ uint32_t hist[kDefWarps][defl::kLit];
-    __shared__ uint32_t freq[defl::kLit];
-    __shared__ uint32_t wt[2 * defl::kLit];
-    __shared__ uint16_t par[2 * defl::kLit], sorted[defl::kLit];
-    __shared__ defl::Header hd;
+    __shared__ uint32_t dhist[kDefWarps][defl::kDist];
+    __shared__ uint32_t freq[2][defl::kLit];   // [0] parse, [1] literal only
+    __shared__ uint32_t dfreq[2][defl::kDist];
+    __shared__ uint32_t wt[2][2 * defl::kLit];
+    __shared__ uint16_t par[2][2 * defl::kLit], sorted[2][defl::kLit];
+    __shared__ defl::Header hd[2];
     __shared__ unsigned long long s_red[2][kDefWarps];
     __shared__ unsigned long long s_scan[kDefWarps];
-    __shared__ unsigned long long s_body;
+    __shared__ unsigned long long s_body[2];
+    __shared__ int s_m[2];
     const int seg = blockIdx.x, f = blockIdx.y, t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const long long off = (long long)seg * kSeg;
-    const int len = int(std::min<long long>(kSeg, g.U - off));
+    const long long fbase = (long long)seg * kSeg;
+    const int len = int(std::min<long long>(kSeg, g.U - fbase));
     const bool final = seg == g.nseg - 1;
-    const uint8_t* in = filt + size_t(f) * g.ustride + off;
+    const uint8_t* frame = filt + size_t(f) * g.ustride;
+    const uint8_t* in = frame + fbase;
     uint8_t* slot = slots + (size_t(f) * g.nseg + seg) * kSlot;
+    uint32_t* tok = tokens + (size_t(f) * g.nseg + seg) * kSeg;   // [kChunk][kDefThreads]
     for (int i = t; i < kDefWarps * defl::kLit; i += kDefThreads) (&hist[0][0])[i] = 0;
-    for (int i = t; i < kSlot / 4; i += kDefThreads) obuf[i] = 0;
-    if (t == 0) s_body = 0;
+    for (int i = t; i < kDefWarps * defl::kDist; i += kDefThreads) (&dhist[0][0])[i] = 0;
+    for (int i = t; i < (1 << kHashBits); i += kDefThreads) table[i] = -1;
+    if (t < 2) s_body[t] = 0;
     __syncthreads();
-    // histogram and the Adler-32 sums of the segment: s1 = sum b, s2 = sum (len - j) b_j
+    // phase A: hash candidates, and the Adler-32 sums s1 = sum b, s2 = sum (len - j) b_j
     unsigned long long s1 = 0, s2 = 0;
-    for (int i = 4 * t; i < len; i += 4 * kDefThreads) {
-        uint32_t v;
-        if (i + 4 <= len) {
-            v = *reinterpret_cast<const uint32_t*>(in + i);
-        } else {
-            v = 0;
-            for (int k = 0; i + k < len; ++k) v |= uint32_t(in[i + k]) << (8 * k);
-        }
-        for (int k = 0; k < 4 && i + k < len; ++k) {
-            const uint32_t b = (v >> (8 * k)) & 0xFF;
-            atomicAdd(&hist[warp][b], 1u);
+    const long long ws = fbase > defl::kWindow ? fbase - defl::kWindow : 0;
+    for (long long r0 = ws; r0 < fbase + len; r0 += kDefThreads) {
+        const long long p = r0 + t;
+        const bool inseg = p >= fbase && p < fbase + len;
+        const bool hashed = p < fbase + len && p + 4 <= g.U;
+        uint32_t h = 0;
+        if (hashed) h = hash4(frame + p);
+        if (inseg) {
+            int d = 0;
+            if (hashed) {
+                const int c = table[h];
+                if (c >= 0 && p - c <= defl::kWindow) d = int(p - c);
+            }
+            dist16[p - fbase] = uint16_t(d);   // 32768 fits; 0 = no candidate
+            const uint32_t b = frame[p];
             s1 += b;
-            s2 += (unsigned long long)(len - i - k) * b;
+            s2 += (unsigned long long)(fbase + len - p) * b;
         }
+        __syncthreads();
+        if (hashed) atomicMax(&table[h], int(p));
+        __syncthreads();
     }
     for (int o = 16; o > 0; o >>= 1) {
         s1 += __shfl_down_sync(0xffffffffu, s1, o);
         s2 += __shfl_down_sync(0xffffffffu, s2, o);
     }
     if (lane == 0) s_red[0][warp] = s1, s_red[1][warp] = s2;
+    // pass 1: greedy parse of this thread's bytes
+    const int i0 = std::min(len, t * kChunk), i1 = std::min(len, i0 + kChunk);
+    int ntok = 0;
+    for (int i = i0; i < i1;) {
+        const long long p = fbase + i;
+        const int lim = min(int(defl::kMaxMatch), i1 - i);
+        int best = 0, bd = 0;
+        const int cand[3] = {int(dist16[i]), 1, int(g.row)};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int d = cand[k];
+            if (d <= 0 || d > defl::kWindow || p < d || lim < defl::kMinMatch) continue;
+            const uint8_t* a = frame + p;
+            const uint8_t* b = a - d;
+            int L = 0;
+            while (L < lim && a[L] == b[L]) ++L;
+            if (L > best) best = L, bd = d;
+        }
+        uint32_t tk;
+        if (best >= defl::kMinMatch) {
+            tk = defl::match_token(best, bd);
+            int ne, ev;
+            atomicAdd(&hist[warp][defl::length_symbol(best, ne, ev)], 1u);
+            atomicAdd(&dhist[warp][defl::distance_symbol(bd, ne, ev)], 1u);
+            i += best;
+        } else {
+            tk = in[i];
+            atomicAdd(&hist[warp][tk], 1u);
+            ++i;
+        }
+        tok[size_t(ntok++) * kDefThreads + t] = tk;
+    }
     __syncthreads();
-    if (t < defl::kLit) {
+    if (t < defl::kLit) {   // parse frequencies; literal-only frequencies = byte counts
         uint32_t c = t == 256 ? 1u : 0u;
         for (int w = 0; w < kDefWarps; ++w) c += hist[w][t];
-        freq[t] = c;
+        freq[0][t] = c;
+    }
+    if (t < defl::kDist) {
+        uint32_t c = 0;
+        for (int w = 0; w < kDefWarps; ++w) c += dhist[w][t];
+        dfreq[0][t] = c;
+        dfreq[1][t] = 0;
     }
     if (t == 0) {
         unsigned long long a = 0, b = 0;
@@ -255,33 +330,62 @@ __global__ void __launch_bounds__(kDefThreads) k_png_deflate(PngGeom g, const ui
         seg_s1[size_t(f) * g.nseg + seg] = a;
         seg_s2[size_t(f) * g.nseg + seg] = b;
     }
+    // byte histogram for the literal-only alternative (reuses the per-warp tables)
     __syncthreads();
-    // used symbols in ascending (frequency, symbol) order, by rank
-    const bool used = t < defl::kLit && freq[t] > 0;
-    const int m = __syncthreads_count(used);
-    if (used) {
-        const uint32_t ft = freq[t];
-        int rank = 0;
-        for (int j = 0; j < defl::kLit; ++j) {
-            const uint32_t fj = freq[j];
-            rank += fj > 0 && (fj < ft || (fj == ft && j < t));
-        }
-        sorted[rank] = uint16_t(t);
-    }
+    for (int i = t; i < kDefWarps * defl::kLit; i += kDefThreads) (&hist[0][0])[i] = 0;
     __syncthreads();
-    if (t == 0) defl::build_header(freq, m, hd, defl::HuffScratch{wt, par, sorted});
+    for (int i = i0; i < i1; ++i) atomicAdd(&hist[warp][in[i]], 1u);
     __syncthreads();
-    // body size: the original counts (freq may have been flattened) times the code lengths
     if (t < defl::kLit) {
         uint32_t c = t == 256 ? 1u : 0u;
         for (int w = 0; w < kDefWarps; ++w) c += hist[w][t];
-        atomicAdd(&s_body, (unsigned long long)c * hd.lit_len[t]);
+        freq[1][t] = c;
     }
     __syncthreads();
-    const unsigned long long huff_bits = hd.bits + s_body;
-    const unsigned long long huff_bytes = final ? (huff_bits + 7) / 8 : (huff_bits + 3 + 7) / 8 + 4;
-    const bool stored = huff_bytes >= 5ull + len;
-    if (stored) {
+    // used symbols of both alphabets in ascending (frequency, symbol) order, by rank
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        const bool used = t < defl::kLit && freq[a][t] > 0;
+        const int m = __syncthreads_count(used);
+        if (t == 0) s_m[a] = m;
+        if (used) {
+            const uint32_t ft = freq[a][t];
+            int rank = 0;
+            for (int j = 0; j < defl::kLit; ++j) {
+                const uint32_t fj = freq[a][j];
+                rank += fj > 0 && (fj < ft || (fj == ft && j < t));
+            }
+            sorted[a][rank] = uint16_t(t);
+        }
+    }
+    __syncthreads();
+    if (t == 0 || t == 32) {   // the two codes are built by threads of different warps at once
+        const int a = t ? 1 : 0;
+        defl::build_header(freq[a], s_m[a], dfreq[a], hd[a], defl::HuffScratch{wt[a], par[a], sorted[a]});
+    }
+    __syncthreads();
+    // body sizes of both alternatives (exact: the parse's tokens, the literal bytes)
+    unsigned long long mine[2] = {0, 0};
+    for (int k = 0; k < ntok; ++k) mine[0] += defl::token_bits(hd[0], tok[size_t(k) * kDefThreads + t]);
+    for (int i = i0; i < i1; ++i) mine[1] += hd[1].lit_len[in[i]];
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        unsigned long long v = mine[a];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (lane == 0) atomicAdd(&s_body[a], v);
+    }
+    // the hash table is dead: the region becomes the output bit buffer
+    for (int i = t; i < kSlot / 4; i += kDefThreads) obuf[i] = 0;
+    __syncthreads();
+    unsigned long long bytes[2];
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        const unsigned long long bits = hd[a].bits + s_body[a] + hd[a].lit_len[256];
+        bytes[a] = final ? (bits + 7) / 8 : (bits + 3 + 7) / 8 + 4;
+    }
+    const int mode = bytes[1] < bytes[0] ? 1 : 0;
+    const unsigned long long huff_bytes = bytes[mode];
+    if (huff_bytes >= 5ull + len) {   // stored
         if (t == 0) {
             slot[0] = final ? 1 : 0;   // BFINAL, BTYPE = 00, padding
             slot[1] = uint8_t(len), slot[2] = uint8_t(len >> 8);
@@ -291,12 +395,8 @@ __global__ void __launch_bounds__(kDefThreads) k_png_deflate(PngGeom g, const ui
         for (int i = t; i < len; i += kDefThreads) slot[5 + i] = in[i];
         return;
     }
-    // bits of every thread's contiguous share of the segment, then their exclusive scan
-    const int share = (len + kDefThreads - 1) / kDefThreads;
-    const int i0 = std::min(len, t * share), i1 = std::min(len, i0 + share);
-    unsigned long long mine = 0;
-    for (int i = i0; i < i1; ++i) mine += hd.lit_len[in[i]];
-    unsigned long long incl = mine;
+    const defl::Header& H = hd[mode];
+    unsigned long long incl = mine[mode];
     for (int o = 1; o < 32; o <<= 1) {
         const unsigned long long v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
@@ -304,26 +404,27 @@ __global__ void __launch_bounds__(kDefThreads) k_png_deflate(PngGeom g, const ui
     if (lane == 31) s_scan[warp] = incl;
     if (t == 0) {
         BitOut bo{obuf, 0};
-        defl::write_header(hd, final, [&](uint32_t v, int b) { bo.put(v, b); });
+        defl::write_header(H, final, [&](uint32_t v, int b) { bo.put(v, b); });
         bo.finish();
     }
     __syncthreads();
     unsigned long long before = 0;
     for (int w = 0; w < warp; ++w) before += s_scan[w];
-    BitOut bo{obuf, (unsigned long long)hd.bits + before + incl - mine};
-    for (int i = i0; i < i1; ++i) {
-        const int b = in[i];
-        bo.put(hd.lit_code[b], hd.lit_len[b]);
+    BitOut bo{obuf, (unsigned long long)H.bits + before + incl - mine[mode]};
+    if (mode == 0) {
+        for (int k = 0; k < ntok; ++k)
+            defl::put_token(H, tok[size_t(k) * kDefThreads + t], [&](uint32_t v, int b) { bo.put(v, b); });
+    } else {
+        for (int i = i0; i < i1; ++i) bo.put(H.lit_code[in[i]], H.lit_len[in[i]]);
     }
     bo.finish();
     if (t == kDefThreads - 1) {   // end of block, then byte alignment
         BitOut e{obuf, bo.pos};
-        e.put(hd.lit_code[256], hd.lit_len[256]);
+        e.put(H.lit_code[256], H.lit_len[256]);
         if (!final) e.put(0u, 3);   // empty stored block: BFINAL 0, BTYPE 00, then LEN/NLEN
         e.finish();
         if (!final) {
-            const unsigned long long byte = (e.pos + 7) / 8;
-            BitOut z{obuf, byte * 8};
+            BitOut z{obuf, (e.pos + 7) / 8 * 8};
             z.put(0u, 16);
             z.put(0xFFFFu, 16);
             z.finish();
@@ -585,9 +686,9 @@ void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, in
     const size_t segs = size_t(n) * g.nseg;
     const size_t b_in = host_io ? align256(in_bytes) : 0, b_filt = align256(size_t(n) * g.ustride),
                  b_slots = align256(segs * kSlot), b_files = align256(size_t(n) * g.fstride),
-                 b_seg = align256(segs * 4), b_off = align256(segs * 8), b_s = align256(segs * 8),
+                 b_tok = align256(segs * size_t(kSeg) * 4), b_seg = align256(segs * 4), b_off = align256(segs * 8), b_s = align256(segs * 8),
                  b_fb = align256(size_t(n) * 8), b_crc = align256(size_t(n) * g.crc_blocks * 4);
-    const size_t need = b_in + b_filt + b_slots + b_files + b_seg + b_off + 2 * b_s + b_fb + b_crc;
+    const size_t need = b_in + b_filt + b_slots + b_tok + b_files + b_seg + b_off + 2 * b_s + b_fb + b_crc;
     if (sc.bytes < need) {
         if (sc.p) {
             AEISU_CUDA(cudaStreamSynchronize(stream));
@@ -608,6 +709,7 @@ void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, in
     }
     uint8_t* filt = take(b_filt);
     uint8_t* slots = take(b_slots);
+    uint32_t* tokens = reinterpret_cast<uint32_t*>(take(b_tok));
     uint8_t* files = take(b_files);
     uint32_t* seg_bytes = reinterpret_cast<uint32_t*>(take(b_seg));
     auto* seg_off = reinterpret_cast<unsigned long long*>(take(b_off));
@@ -621,8 +723,9 @@ void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, in
         AEISU_CUDA(cudaFuncSetAttribute(k_png_filter, cudaFuncAttributeMaxDynamicSharedMemorySize, filt_smem));
     k_png_filter<<<dim3(h, n), kFiltThreads, filt_smem, stream>>>(dsrc, kind, g, filt);
     AEISU_CUDA(cudaGetLastError());
-    AEISU_CUDA(cudaFuncSetAttribute(k_png_deflate, cudaFuncAttributeMaxDynamicSharedMemorySize, kSlot));
-    k_png_deflate<<<dim3(g.nseg, n), kDefThreads, kSlot, stream>>>(g, filt, slots, seg_bytes, seg_s1, seg_s2);
+    AEISU_CUDA(cudaFuncSetAttribute(k_png_deflate, cudaFuncAttributeMaxDynamicSharedMemorySize, kDefSmem));
+    k_png_deflate<<<dim3(g.nseg, n), kDefThreads, kDefSmem, stream>>>(g, filt, slots, tokens, seg_bytes, seg_s1,
+                                                                     seg_s2);
     AEISU_CUDA(cudaGetLastError());
     k_png_layout<<<n, 256, 0, stream>>>(g, png_head(h, w), seg_bytes, seg_s1, seg_s2, seg_off, files, file_bytes);
     AEISU_CUDA(cudaGetLastError());

@@ -111,7 +111,7 @@ def test_compressed_size_bounds():
     assert len(ours) <= 1.02 * huff_only + 64, (len(ours), huff_only)
     buf = io.BytesIO()
     Image.fromarray(frame).save(buf, format="PNG")
-    assert len(ours) < 2.6 * len(buf.getvalue()), (len(ours), len(buf.getvalue()))
+    assert len(ours) < 1.8 * len(buf.getvalue()), (len(ours), len(buf.getvalue()))
 
 
 def test_upscaled_output_encodes_to_the_saved_pixels():
