@@ -60,6 +60,11 @@ _SIGNATURES = {
     "aeisu_png_encode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint, C.c_int,
                                    C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
     "aeisu_png_bound": (C.c_uint64, [C.c_int, C.c_int]),
+    "aeisu_reconstruct_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "aeisu_reconstruct_backward_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                                 C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "aeisu_synchronize": (C.c_int, [C.c_void_p, C.c_void_p, C.c_double]),
     "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
     "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),

@@ -5,7 +5,7 @@ C ABI's ``aeisu_png_encode`` from frames already on the device (or copied there)
 ``upscale_u8`` returns) or float32 CHW images (``[3, H, W]`` or ``[n, 3, H, W]``, what ``upscale``
 returns; quantised as ``save_rgb`` does: clamp to [0, 1], floor(x * 255 + 0.5)) and returns the
 PNG file bytes (one ``bytes`` object per frame for a batch).  The decoded pixels are exactly
-``save_rgb``'s; the compressed stream is this encoder's own (literal-only Huffman blocks), so the
+``save_rgb``'s; the compressed stream is this encoder's own (dynamic Huffman blocks with greedy LZ77 matches), so the
 files are byte-for-byte different from PIL's and typically somewhat larger.  ``save_png`` writes
 one file.  There is no CPU fallback.
 """

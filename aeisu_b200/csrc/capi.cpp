@@ -195,6 +195,25 @@ int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned
     });
 }
 
+int aeisu_reconstruct_f32(const float* source, const float* metadata, const float* base, const float* basis, int n,
+                          int h, int w, int trim, int device, float* out, void* stream) {
+    return guarded([&] {
+        aeisu::reconstruct_f32(source, metadata, base, basis, n, h, w, trim, device, out,
+                               static_cast<cudaStream_t>(stream));
+    });
+}
+
+int aeisu_reconstruct_backward_f32(const float* source, const float* metadata, const float* basis,
+                                   const float* grad_out, int n, int h, int w, int trim, int gradient_stride,
+                                   int phase, int device, float* grad_metadata, float* grad_base,
+                                   float* grad_basis, void* stream) {
+    return guarded([&] {
+        aeisu::reconstruct_backward_f32(source, metadata, basis, grad_out, n, h, w, trim, gradient_stride, phase,
+                                        device, grad_metadata, grad_base, grad_basis,
+                                        static_cast<cudaStream_t>(stream));
+    });
+}
+
 int aeisu_synchronize(aeisu_t* handle, void* stream, double timeout_ms) {
     return guarded([&] { engine_of(handle).synchronize(static_cast<cudaStream_t>(stream), timeout_ms); });
 }

@@ -109,4 +109,13 @@ void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, in
                 uint64_t capacity, uint64_t* sizes, cudaStream_t stream);
 int png_launches_per_call();
 
+// reconstruct() of aeisu/reconstruction.py:29-83 on caller-given metadata, base and basis, FP32,
+// and its backward (k_recon.cu).  Device pointers; both only enqueue on `stream`.
+void reconstruct_f32(const float* src, const float* meta, const float* base, const float* basis, int n, int h,
+                     int w, int trim, int device, float* out, cudaStream_t stream);
+void reconstruct_backward_f32(const float* src, const float* meta, const float* basis, const float* grad, int n,
+                              int h, int w, int trim, int stride, int phase, int device, float* gmeta,
+                              float* gbase, float* gbasis, cudaStream_t stream);
+int recon_launches(bool backward, int trim, int stride);
+
 }  // namespace aeisu

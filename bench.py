@@ -312,6 +312,67 @@ def measure_png(out_u8, frames):
                       f"{runs} calls after 2 warm-up calls"}
 
 
+def measure_train(dev, batch, sm_mhz=None):
+    """Training reconstruction (aeisu_reconstruct_f32 + aeisu_reconstruct_backward_f32 through the
+    autograd drop-in aeisu_b200.reconstruction.reconstruct) at the reference recipe's shape
+    (configs/area.json: batch 32, 512x512 HR patches, source_pad 16 -> 288x288 sources, trim 32,
+    basis_grad_stride 16): CUDA events around forward + backward on the launching stream, inputs
+    in HBM (larger than L2).  Beside it the FP32 numpy port on one 288x288 sample."""
+    import torch
+    from aeisu_b200.reconstruction import reconstruct
+    from oracle import reconstruct_np as R
+    h = w = 288
+    trim, stride = 32, 16
+    ch, cw = h - trim, w - trim
+    g = torch.Generator(device=dev).manual_seed(3)
+    src = torch.rand((batch, 3, h, w), device=dev, generator=g)
+    meta = (torch.randn((batch, 64, h // 2, w // 2), device=dev, generator=g) * 2).requires_grad_()
+    base = (torch.randn((25, 4), device=dev, generator=g) * 0.05).requires_grad_()
+    basis = (torch.randn((25, 16, 4), device=dev, generator=g) * 0.05).requires_grad_()
+    grad = torch.randn((batch, 3, 2 * ch, 2 * cw), device=dev, generator=g)
+    stream = torch.cuda.Stream(dev)
+    runs = 10
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * runs)]
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride).backward(grad)
+        for r in range(runs):
+            ev[3 * r].record(stream)
+            out = reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride)
+            ev[3 * r + 1].record(stream)
+            out.backward(grad)
+            ev[3 * r + 2].record(stream)
+    torch.cuda.synchronize(dev)
+    fwd = sum(ev[3 * r].elapsed_time(ev[3 * r + 1]) for r in range(runs)) / runs
+    bwd = sum(ev[3 * r + 1].elapsed_time(ev[3 * r + 2]) for r in range(runs)) / runs
+    px = batch * ch * cw
+    sel = batch * ((ch + stride - 1) // stride) * ((cw + stride - 1) // stride)
+    # FP32 FLOPs: filter assembly 2 x 1,600 + apply 2 x 300 per core pixel forward; filter
+    # gradient 2 x 300 + coefficient gradient 2 x 1,600 backward; 2 x 1,700 per sampled pixel
+    f_fwd, f_bwd = 3800.0 * px, 3800.0 * px + 3400.0 * sel
+    mhz = sm_mhz or 1965.0
+    peak = 148 * 128 * 2 * mhz * 1e6 / 1e12   # FP32 FMA pipe: 128 lanes per SM per clock
+    c0 = time.perf_counter()
+    s0 = src[:1].cpu().numpy()
+    m0 = meta[:1].detach().cpu().numpy()
+    b0, k0 = base.detach().cpu().numpy(), basis.detach().cpu().numpy()
+    R.reconstruct(s0, m0, b0, k0, trim)
+    R.reconstruct_backward(s0, m0, b0, k0, grad[:1].cpu().numpy(), trim, stride, 0)
+    cpu_s = time.perf_counter() - c0
+    total = fwd + bwd
+    return {"value": 4 * px / (total / 1e3) / 1e6, "unit": "output Mpix/s (forward + backward)",
+            "ms_per_step": total, "forward_ms": fwd, "backward_ms": bwd,
+            "fp32": {"bound": "fp32 pipe", "forward_tflops": f_fwd / (fwd / 1e3) / 1e12,
+                     "backward_tflops": f_bwd / (bwd / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "forward_frac": f_fwd / (fwd / 1e3) / 1e12 / peak,
+                     "backward_frac": f_bwd / (bwd / 1e3) / 1e12 / peak,
+                     "peak_kind": f"nominal FP32 FMA rate at {mhz:.0f} MHz (148 SMs x 128 lanes)"},
+            "cpu_port": {"value": 4 * ch * cw / cpu_s / 1e6, "unit": "output Mpix/s (forward + backward)",
+                         "cores": 1, "kind": "port", "sample": f"1 source {w}x{h}, trim {trim}, stride {stride}, numpy FP32"},
+            "config": f"batch {batch} x 3x{h}x{w} float32 sources, trim {trim} -> {2 * cw}x{2 * ch} outputs, "
+                      f"gradient_stride {stride}, phase 0; {runs} steps after 3 warm-up steps"}
+
+
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
     """Time the reference algorithm's CPU implementation (the oracle port, FP32, all host
     threads) on a bounded sample of the workload's frames."""
@@ -377,6 +438,8 @@ def main():
                     help="frames per call of the PNG egress measurement (0 disables)")
     ap.add_argument("--metric-pairs", type=int, default=8,
                     help="image pairs per call of the evaluation-metrics measurement (0 disables)")
+    ap.add_argument("--train-batch", type=int, default=32,
+                    help="sources per step of the training-reconstruction measurement (0 disables)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -466,6 +529,8 @@ def main():
     metric_line = (measure_metrics(dev, out, args.metric_pairs)
                    if (rank == 0 and args.metric_pairs > 0 and not band) else None)
     png_line = measure_png(out, args.png_frames) if (rank == 0 and args.png_frames > 0 and not band) else None
+    train_line = (measure_train(dev, args.train_batch, clocks.summary().get("sm_mhz"))
+                  if (rank == 0 and args.train_batch > 0 and not band) else None)
 
     # end-to-end through the public API with pinned host buffers
     host_src = torch.from_numpy(frames).pin_memory()
@@ -530,6 +595,7 @@ def main():
             "latency_1080p": latency,
             "evaluation_metrics": metric_line,
             "png_egress": png_line,
+            "reconstruct_train": train_line,
             "clocks": clocks.summary(),
             "report": model.report,
         }

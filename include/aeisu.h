@@ -18,6 +18,8 @@
  *   FoldedAEISU.forward / predict_coefficients   aeisu/model.py:494-551
  *   aeisu.metrics.distortion               aeisu/metrics.py:17-39 (evaluate.py:41)
  *   aeisu.runtime.save_rgb (PNG egress)    aeisu/runtime.py:23-27 (infer.py, evaluate.py:48)
+ *   aeisu.reconstruction.reconstruct (forward and its autograd backward)
+ *                                          aeisu/reconstruction.py:29-83 (train.py:99-103)
  * The Python binding that mirrors aeisu.runtime over this ABI is aeisu_b200/runtime.py.
  */
 #ifndef AEISU_B200_H
@@ -179,8 +181,9 @@ int aeisu_distortion(const float* prediction, const float* target, int n, int h,
  * kind AEISU_PNG_F32: frames are float32 3 x h x w (CHW, as aeisu_upscale_f32 writes them),
  * quantised as save_rgb does (clamp to [0, 1], floor(x * 255 + 0.5)).  The files are 8-bit RGB,
  * non-interlaced, adaptively filtered per row; their pixels decode to exactly save_rgb's, the
- * compressed stream is the encoder's own (literal-only dynamic Huffman blocks, not zlib's
- * LZ77), so the file bytes and sizes differ from PIL's.  flags: where the frames are,
+ * compressed stream is the encoder's own (one dynamic Huffman block per 60 KiB segment, with
+ * greedy single-candidate LZ77 matches, not zlib's chained lazy matching), so the file bytes
+ * and sizes differ from PIL's.  flags: where the frames are,
  * AEISU_IO_HOST or AEISU_IO_DEVICE (on GPU `device`); `out` may be host or device memory.
  * The n files are written back to back into `out` (capacity bytes;
  * n * aeisu_png_bound(h, w) always suffices) and sizes[i]
@@ -193,6 +196,34 @@ int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned
 
 /* Largest PNG file aeisu_png_encode can produce for one h x w frame (0 for an empty size). */
 uint64_t aeisu_png_bound(int h, int w);
+
+/* reconstruct() of aeisu/reconstruction.py:29-83 as a standalone FP32 operator (the function
+ * train.py:99-103 differentiates), no model handle needed.  All pointers are device memory on
+ * GPU `device`, contiguous float32: source [n][3][h][w], metadata [n][64][h/2][w/2] (channel
+ * parity * 16 + k, unclamped), base [25][4] (tap, phase), basis [25][16][4] (tap, component,
+ * phase: project_basis's output).  trim as the reference's: 0, or an even HR border >= 4, so
+ * the core is (h - trim) x (w - trim) LR pixels, read with replicate padding at trim 0 and the
+ * real border otherwise.  out [n][3][2ch][2cw] (ch = h - trim, cw = w - trim) receives the
+ * unclipped 2x core.  Enqueues on `stream` (NULL: the legacy default stream)
+ * and returns.  AEISU_ERR_INVALID_ARG with the reference's messages for a bad trim, stride or
+ * phase, an empty core, odd h or w. */
+int aeisu_reconstruct_f32(const float* source, const float* metadata, const float* base, const float* basis,
+                          int n, int h, int w, int trim, int device, float* out, void* stream);
+
+/* Backward of aeisu_reconstruct_f32 with the reference's sampled global-filter gradients
+ * (reconstruction.py:56-78): given grad_out [n][3][2ch][2cw], writes grad_metadata (same
+ * layout as metadata; dense, through the coefficient clamp; zero outside the core) and, when
+ * gradient_stride > 0, grad_base [25][4] and grad_basis [25][16][4]: over every core pixel at
+ * stride 1, otherwise over the pixels with y % s == phase' / s and x % s == phase' % s (core
+ * coordinates, phase' = phase mod s^2), each weighted s^2.  gradient_stride 0 leaves
+ * grad_base and grad_basis untouched (they may be NULL): the reference gives them no
+ * gradient.  Gradients with respect to the source are not computed.  The filter-gradient
+ * sums are deterministic for a given GPU.  Takes a small stream-ordered workspace
+ * (cudaMallocAsync, 6.8 KB per SM-resident CTA) and enqueues on `stream`. */
+int aeisu_reconstruct_backward_f32(const float* source, const float* metadata, const float* basis,
+                                   const float* grad_out, int n, int h, int w, int trim, int gradient_stride,
+                                   int phase, int device, float* grad_metadata, float* grad_base,
+                                   float* grad_basis, void* stream);
 
 /* Wait for all work enqueued on the handle's stream (or `stream`) for at most
  * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
