@@ -17,14 +17,17 @@
 //                     shared-memory slot list in thread order; after each tile the CTA adds
 //                     their outer products into per-thread accumulators of the 17 x 100
 //                     base/basis gradient.  Each CTA writes its partial once.
-//   k_recon_reduce    sums the partials of all CTAs in CTA order (deterministic for a given
+//                     With trim > 0 it first zeroes the metadata gradients of the pixels
+//                     outside the core, which the reference's crop gives no gradient.
+//   k_recon_reduce    sums the partials of all CTAs in a fixed order (deterministic for a given
 //                     grid), writing grad_base [25][4] and grad_basis [25][16][4].
-//   k_recon_zero      with trim > 0: zero metadata gradients of pixels outside the core, which
-//                     the reference's crop gives no gradient.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.h"
 #include "kernels.h"
@@ -160,6 +163,23 @@ __global__ void __launch_bounds__(kRThreads) k_recon_fwd(ReconJob j) {
     }
 }
 
+// trim > 0: metadata gradients of pixels outside the core are zero (the reference's crop gives
+// them none).  A grid-stride pass over the metadata positions of the border, one thread per
+// (frame, parity, position), before the CTA's tiles.
+__device__ __forceinline__ void zero_border(const ReconJob& j) {
+    const int hh = j.h >> 1, ww = j.w >> 1;
+    const long long total = (long long)j.n * 4 * hh * ww;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int xx = int(i % ww), yy = int((i / ww) % hh), parity = int((i / ((long long)ww * hh)) % 4);
+        const int b = int(i / (4LL * ww * hh));
+        const int Y = 2 * yy + (parity >> 1), X = 2 * xx + (parity & 1);
+        if (Y >= j.off && Y < j.off + j.ch && X >= j.off && X < j.off + j.cw) continue;
+        float* g = j.gmeta + ((size_t(b) * 64 + parity * 16) * hh + yy) * ww + xx;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) g[size_t(k) * hh * ww] = 0.f;
+    }
+}
+
 __global__ void __launch_bounds__(kRThreads, 2) k_recon_bwd(ReconJob j) {
     __shared__ __align__(16) float s_bank[kBank - kBase];   // basis only
     __shared__ float s_win[3][kRWinY][kRWinX];
@@ -168,6 +188,7 @@ __global__ void __launch_bounds__(kRThreads, 2) k_recon_bwd(ReconJob j) {
     float* s_gw = s_dyn;                                   // [slots][100]
     float* s_mc = s_dyn + size_t(j.slots) * kSlotW;        // [slots][20]
     for (int i = threadIdx.x; i < kBank - kBase; i += kRThreads) s_bank[i] = __ldg(j.basis + i);
+    if (j.off > 0) zero_border(j);
     const int tx = threadIdx.x % kRTX, ty = threadIdx.x / kRTX;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t kplane = size_t(j.h >> 1) * (j.w >> 1);
@@ -267,28 +288,28 @@ __global__ void __launch_bounds__(kRThreads, 2) k_recon_bwd(ReconJob j) {
     }
 }
 
-// grad_base[t][p] = sum of k-row 16; grad_basis[t][k][p] = k-row k, at column t * 4 + p.
-__global__ void k_recon_reduce(const float* __restrict__ partial, int nblk, float* gbase, float* gbasis) {
-    const int o = blockIdx.x * blockDim.x + threadIdx.x;
-    if (o >= kGrad) return;
+// grad_base[t][p] = sum of k-row 16; grad_basis[t][k][p] = k-row k, at column t * 4 + p.  One
+// block per 32 outputs: lane l owns output 32 * block + l, warp w sums the partials of CTAs
+// w, w + 8, ... in order (coalesced 128-byte rows), then the eight warp sums are added in warp
+// order: the same order on every call.
+constexpr int kRedWarps = 8;
+__global__ void __launch_bounds__(32 * kRedWarps) k_recon_reduce(const float* __restrict__ partial, int nblk,
+                                                                 float* gbase, float* gbasis) {
+    __shared__ float s_part[kRedWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int o = blockIdx.x * 32 + lane;
     float sum = 0.f;
-    for (int c = 0; c < nblk; ++c) sum = __fadd_rn(sum, partial[size_t(c) * kGrad + o]);
+    if (o < kGrad)
+        for (int c = warp; c < nblk; c += kRedWarps) sum = __fadd_rn(sum, __ldg(partial + size_t(c) * kGrad + o));
+    s_part[warp][lane] = sum;
+    __syncthreads();
+    if (warp != 0 || o >= kGrad) return;
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRedWarps; ++w) total = __fadd_rn(total, s_part[w][lane]);
     const int k = o / 100, tpv = o % 100, t = tpv >> 2, p = tpv & 3;
-    if (k == 16) gbase[tpv] = sum;
-    else gbasis[(t * 16 + k) * 4 + p] = sum;
-}
-
-__global__ void k_recon_zero(ReconJob j) {
-    const int hh = j.h >> 1, ww = j.w >> 1;
-    const long long total = (long long)j.n * 4 * hh * ww;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const int xx = int(i % ww), yy = int((i / ww) % hh), parity = int((i / ((long long)ww * hh)) % 4);
-        const int b = int(i / (4LL * ww * hh));
-        const int Y = 2 * yy + (parity >> 1), X = 2 * xx + (parity & 1);
-        if (Y >= j.off && Y < j.off + j.ch && X >= j.off && X < j.off + j.cw) continue;
-        float* g = j.gmeta + ((size_t(b) * 64 + parity * 16) * hh + yy) * ww + xx;
-        for (int k = 0; k < 16; ++k) g[size_t(k) * hh * ww] = 0.f;
-    }
+    if (k == 16) gbase[tpv] = total;
+    else gbasis[(t * 16 + k) * 4 + p] = total;
 }
 
 struct DeviceGuard {
@@ -329,17 +350,54 @@ ReconJob plan_recon(int n, int h, int w, int trim, int stride, int phase) {
     return j;
 }
 
-int sms_of(int device) {
-    int sms = 148;
-    AEISU_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-    return sms;
+// Per-call host work is part of a training step's latency: SM counts, occupancy-derived grids
+// and the workspace pool are set up once per device (and per shared-memory size).
+struct DeviceState {
+    int sms = 0;
+    long long fwd_ctas = 0;                 // resident k_recon_fwd CTAs
+    std::map<size_t, long long> bwd_ctas;   // resident k_recon_bwd CTAs per dynamic smem size
+    cudaMemPool_t pool = nullptr;           // backward partials; keeps its memory between calls
+};
+
+std::mutex g_state_mu;
+std::map<int, DeviceState> g_state;
+
+// The largest dynamic shared memory the backward takes: every pixel of a tile selected.
+constexpr size_t kMaxDyn = size_t(kRThreads) * (kSlotW + kSlotC) * sizeof(float);
+
+DeviceState& state_of(int device) {
+    std::lock_guard<std::mutex> lock(g_state_mu);
+    DeviceState& d = g_state[device];
+    if (d.sms == 0) {
+        int sms = 0, per_sm = 0;
+        AEISU_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        AEISU_CUDA(cudaFuncSetAttribute(k_recon_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDyn)));
+        AEISU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_recon_fwd, kRThreads, 0));
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        AEISU_CUDA(cudaMemPoolCreate(&d.pool, &props));
+        uint64_t keep = UINT64_MAX;
+        AEISU_CUDA(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        d.fwd_ctas = (long long)std::max(per_sm, 1) * sms;
+        d.sms = sms;
+    }
+    return d;
+}
+
+long long bwd_ctas(DeviceState& d, size_t dyn) {
+    std::lock_guard<std::mutex> lock(g_state_mu);
+    auto it = d.bwd_ctas.find(dyn);
+    if (it != d.bwd_ctas.end()) return it->second;
+    int per_sm = 0;
+    AEISU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_recon_bwd, kRThreads, dyn));
+    const long long n = (long long)std::max(per_sm, 1) * d.sms;
+    d.bwd_ctas.emplace(dyn, n);
+    return n;
 }
 
 }  // namespace
-
-int recon_launches(bool backward, int trim, int stride) {
-    return backward ? 1 + (stride > 0 ? 1 : 0) + (trim > 0 ? 1 : 0) : 1;
-}
 
 void reconstruct_f32(const float* src, const float* meta, const float* base, const float* basis, int n, int h,
                      int w, int trim, int device, float* out, cudaStream_t stream) {
@@ -351,9 +409,7 @@ void reconstruct_f32(const float* src, const float* meta, const float* base, con
     j.base = base;
     j.basis = basis;
     j.out = out;
-    int per_sm = 0;
-    AEISU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_recon_fwd, kRThreads, 0));
-    const long long grid = std::min<long long>(j.tiles, (long long)std::max(per_sm, 1) * sms_of(device));
+    const long long grid = std::min<long long>(j.tiles, state_of(device).fwd_ctas);
     k_recon_fwd<<<unsigned(grid), kRThreads, 0, stream>>>(j);
     AEISU_CUDA(cudaGetLastError());
 }
@@ -371,24 +427,17 @@ void reconstruct_backward_f32(const float* src, const float* meta, const float* 
     j.grad = grad;
     j.gmeta = gmeta;
     const size_t dyn = size_t(j.slots) * (kSlotW + kSlotC) * sizeof(float);
-    if (dyn > 48 * 1024) AEISU_CUDA(cudaFuncSetAttribute(k_recon_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
-    int per_sm = 0;
-    AEISU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_recon_bwd, kRThreads, dyn));
-    const long long grid = std::min<long long>(j.tiles, (long long)std::max(per_sm, 1) * sms_of(device));
+    DeviceState& ds = state_of(device);
+    const long long grid = std::min<long long>(j.tiles, bwd_ctas(ds, dyn));
     void* ws = nullptr;
     if (stride > 0) {
-        AEISU_CUDA(cudaMallocAsync(&ws, size_t(grid) * kGrad * sizeof(float), stream));
+        AEISU_CUDA(cudaMallocFromPoolAsync(&ws, size_t(grid) * kGrad * sizeof(float), ds.pool, stream));
         j.partial = static_cast<float*>(ws);
-    }
-    if (j.off > 0) {
-        const long long total = (long long)n * 4 * (h / 2) * (w / 2);
-        const long long blocks = std::min<long long>((total + 255) / 256, 4LL * sms_of(device));
-        k_recon_zero<<<unsigned(blocks), 256, 0, stream>>>(j);
     }
     k_recon_bwd<<<unsigned(grid), kRThreads, dyn, stream>>>(j);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess && stride > 0) {
-        k_recon_reduce<<<(kGrad + 255) / 256, 256, 0, stream>>>(j.partial, int(grid), gbase, gbasis);
+        k_recon_reduce<<<(kGrad + 31) / 32, 32 * kRedWarps, 0, stream>>>(j.partial, int(grid), gbase, gbasis);
         e = cudaGetLastError();
     }
     if (ws) cudaFreeAsync(ws, stream);

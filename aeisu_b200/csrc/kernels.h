@@ -116,6 +116,5 @@ void reconstruct_f32(const float* src, const float* meta, const float* base, con
 void reconstruct_backward_f32(const float* src, const float* meta, const float* basis, const float* grad, int n,
                               int h, int w, int trim, int stride, int phase, int device, float* gmeta,
                               float* gbase, float* gbasis, cudaStream_t stream);
-int recon_launches(bool backward, int trim, int stride);
 
 }  // namespace aeisu

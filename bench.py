@@ -330,18 +330,24 @@ def measure_train(dev, batch, sm_mhz=None):
     base = (torch.randn((25, 4), device=dev, generator=g) * 0.05).requires_grad_()
     basis = (torch.randn((25, 16, 4), device=dev, generator=g) * 0.05).requires_grad_()
     grad = torch.randn((batch, 3, 2 * ch, 2 * cw), device=dev, generator=g)
-    stream = torch.cuda.Stream(dev)
-    runs = 10
+    stream = torch.cuda.current_stream(dev)   # where a training loop runs its steps
+    runs, warm = 10, 5
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * runs)]
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride).backward(grad)
-        for r in range(runs):
-            ev[3 * r].record(stream)
-            out = reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride)
-            ev[3 * r + 1].record(stream)
-            out.backward(grad)
-            ev[3 * r + 2].record(stream)
+
+    def zero_grad():   # optimizer.zero_grad(set_to_none=True), train.py:98
+        meta.grad = base.grad = basis.grad = None
+
+    for _ in range(warm):
+        zero_grad()
+        reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride).backward(grad)
+    torch.cuda.synchronize(dev)
+    for r in range(runs):
+        zero_grad()
+        ev[3 * r].record(stream)
+        out = reconstruct(src, meta, base, basis, trim=trim, gradient_stride=stride)
+        ev[3 * r + 1].record(stream)
+        out.backward(grad)
+        ev[3 * r + 2].record(stream)
     torch.cuda.synchronize(dev)
     fwd = sum(ev[3 * r].elapsed_time(ev[3 * r + 1]) for r in range(runs)) / runs
     bwd = sum(ev[3 * r + 1].elapsed_time(ev[3 * r + 2]) for r in range(runs)) / runs
@@ -370,7 +376,8 @@ def measure_train(dev, batch, sm_mhz=None):
             "cpu_port": {"value": 4 * ch * cw / cpu_s / 1e6, "unit": "output Mpix/s (forward + backward)",
                          "cores": 1, "kind": "port", "sample": f"1 source {w}x{h}, trim {trim}, stride {stride}, numpy FP32"},
             "config": f"batch {batch} x 3x{h}x{w} float32 sources, trim {trim} -> {2 * cw}x{2 * ch} outputs, "
-                      f"gradient_stride {stride}, phase 0; {runs} steps after 3 warm-up steps"}
+                      f"gradient_stride {stride}, phase 0; {runs} steps after {warm} warm-up steps, grads set to "
+                      "None before each step, CUDA events on the current stream"}
 
 
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):

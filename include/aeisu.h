@@ -218,8 +218,8 @@ int aeisu_reconstruct_f32(const float* source, const float* metadata, const floa
  * coordinates, phase' = phase mod s^2), each weighted s^2.  gradient_stride 0 leaves
  * grad_base and grad_basis untouched (they may be NULL): the reference gives them no
  * gradient.  Gradients with respect to the source are not computed.  The filter-gradient
- * sums are deterministic for a given GPU.  Takes a small stream-ordered workspace
- * (cudaMallocAsync, 6.8 KB per SM-resident CTA) and enqueues on `stream`. */
+ * sums are deterministic for a given GPU.  Takes a small stream-ordered workspace (6.8 KB per
+ * SM-resident CTA) from a memory pool the library keeps per device, and enqueues on `stream`. */
 int aeisu_reconstruct_backward_f32(const float* source, const float* metadata, const float* basis,
                                    const float* grad_out, int n, int h, int w, int trim, int gradient_stride,
                                    int phase, int device, float* grad_metadata, float* grad_base,
