@@ -5,10 +5,11 @@
 //
 //   k_recon_fwd       one thread per core LR pixel, persistent CTAs over 4 x 64 pixel tiles.
 //                     The 5x5 RGB window of the tile sits in shared memory, the 1,700-float bank
-//                     (base [25][4], basis [25][16][4]) too; per tap the four phase weights are
-//                     base + sum_k c_k basis[tap][k] (the reference's einsum then base add), then
-//                     applied to the three channels.  Phase pairs run as packed f32x2 FMAs.
-//   k_recon_bwd       same tiles.  Per pixel and tap, the filter gradient
+//                     (base [25][4], basis [25][16][4]) in constant memory.  Per tap the four
+//                     phase weights are base + sum_k c_k basis[tap][k] (the reference's einsum
+//                     then base add), applied to the three channels (phase pairs as packed
+//                     f32x2 FMAs).
+//   k_recon_bwd       same tiles, the basis in shared memory.  Per pixel and tap, the filter gradient
 //                     gw[p] = sum_c grad[c][p] src[c][tap]; the coefficient gradient
 //                     gc[k] = sum_{tap,p} gw[p] basis[tap][k][p], through the clamp's derivative
 //                     (1 where |v| <= 2, 0.05 on the soft ramp up to 2.5 inclusive, else 0) into
@@ -61,6 +62,15 @@ struct ReconJob {
     int slots;             // slot capacity per tile (0 when stride == 0)
 };
 
+// The forward's bank is the same for every thread, so it sits in constant memory, where an FFMA
+// reads it as a direct operand: no load instruction and no shared-memory wavefront per FMA (a
+// broadcast 16-byte shared load costs two wavefronts; with the bank in shared memory they bound
+// the forward).  Each call copies its base/basis here on its own stream, after the previous
+// forward has finished with them (see reconstruct_f32).  The backward keeps its basis in shared
+// memory: streamed from constant memory it measured slower (0.46 against 0.37 ms per training
+// step), its constant operands missing the per-SM constant cache.
+__constant__ float c_fwd_bank[kBank];   // base [25][4], then basis [25][16][4]
+
 __device__ __forceinline__ float clamp_coef(float v) {
     // reconstruction.py:15-17 with the reference's own operations and comparisons
     const float mag = fabsf(v);
@@ -105,10 +115,7 @@ __device__ __forceinline__ size_t meta_at(const ReconJob& j, int b, int y, int x
 }
 
 __global__ void __launch_bounds__(kRThreads) k_recon_fwd(ReconJob j) {
-    __shared__ __align__(16) float s_bank[kBank];
     __shared__ float s_win[3][kRWinY][kRWinX];
-    for (int i = threadIdx.x; i < kBase; i += kRThreads) s_bank[i] = __ldg(j.base + i);
-    for (int i = threadIdx.x; i < kBank - kBase; i += kRThreads) s_bank[kBase + i] = __ldg(j.basis + i);
     const int tx = threadIdx.x % kRTX, ty = threadIdx.x / kRTX;
     const size_t kplane = size_t(j.h >> 1) * (j.w >> 1);
     const int OH = 2 * j.ch, OW = 2 * j.cw;
@@ -120,45 +127,36 @@ __global__ void __launch_bounds__(kRThreads) k_recon_fwd(ReconJob j) {
         __syncthreads();
         const int y = y0 + ty, x = x0 + tx;
         if (y >= j.ch || x >= j.cw) continue;
-        float2 cc[16];
+        float c[16];
         const float* mp = j.meta + meta_at(j, b, y, x);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const float c = clamp_coef(__ldg(mp + k * kplane));
-            cc[k] = make_float2(c, c);
-        }
+        for (int k = 0; k < 16; ++k) c[k] = clamp_coef(__ldg(mp + k * kplane));
         float2 o01[3], o23[3];   // phases (0, 1) and (2, 3) per channel
 #pragma unroll
-        for (int c = 0; c < 3; ++c) o01[c] = o23[c] = make_float2(0.f, 0.f);
-#pragma unroll 1
-        for (int ky = 0; ky < 5; ++ky) {
+        for (int ch = 0; ch < 3; ++ch) o01[ch] = o23[ch] = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int kx = 0; kx < 5; ++kx) {
-                const int t = ky * 5 + kx;
-                const float4* bk = reinterpret_cast<const float4*>(s_bank + kBase + t * 64);
-                float2 w01 = make_float2(0.f, 0.f), w23 = w01;
+        for (int t = 0; t < 25; ++t) {   // every bank index is a compile-time constant
+            const int ky = t / 5, kx = t % 5;
+            float w[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    const float4 v = bk[k];
-                    w01 = __ffma2_rn(cc[k], make_float2(v.x, v.y), w01);
-                    w23 = __ffma2_rn(cc[k], make_float2(v.z, v.w), w23);
-                }
-                const float4 bs = reinterpret_cast<const float4*>(s_bank)[t];
-                w01 = __fadd2_rn(make_float2(bs.x, bs.y), w01);
-                w23 = __fadd2_rn(make_float2(bs.z, bs.w), w23);
+            for (int k = 0; k < 16; ++k)
 #pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    const float s = s_win[c][ty + ky][tx + kx];
-                    o01[c] = __ffma2_rn(make_float2(s, s), w01, o01[c]);
-                    o23[c] = __ffma2_rn(make_float2(s, s), w23, o23[c]);
-                }
+                for (int p = 0; p < 4; ++p) w[p] = fmaf(c[k], c_fwd_bank[kBase + (t * 16 + k) * 4 + p], w[p]);
+            // the reference's einsum, then the base add (reconstruction.py:70)
+            const float2 a = make_float2(__fadd_rn(c_fwd_bank[t * 4 + 0], w[0]), __fadd_rn(c_fwd_bank[t * 4 + 1], w[1]));
+            const float2 d = make_float2(__fadd_rn(c_fwd_bank[t * 4 + 2], w[2]), __fadd_rn(c_fwd_bank[t * 4 + 3], w[3]));
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                const float sv = s_win[ch][ty + ky][tx + kx];
+                o01[ch] = __ffma2_rn(make_float2(sv, sv), a, o01[ch]);
+                o23[ch] = __ffma2_rn(make_float2(sv, sv), d, o23[ch]);
             }
         }
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            float* op = j.out + ((size_t(b) * 3 + c) * OH + 2 * y) * OW + 2 * x;
-            *reinterpret_cast<float2*>(op) = o01[c];        // HR row 2y: phases 0, 1
-            *reinterpret_cast<float2*>(op + OW) = o23[c];   // HR row 2y + 1: phases 2, 3
+        for (int ch = 0; ch < 3; ++ch) {
+            float* op = j.out + ((size_t(b) * 3 + ch) * OH + 2 * y) * OW + 2 * x;
+            *reinterpret_cast<float2*>(op) = o01[ch];        // HR row 2y: phases 0, 1
+            *reinterpret_cast<float2*>(op + OW) = o23[ch];   // HR row 2y + 1: phases 2, 3
         }
     }
 }
@@ -357,6 +355,10 @@ struct DeviceState {
     long long fwd_ctas = 0;                 // resident k_recon_fwd CTAs
     std::map<size_t, long long> bwd_ctas;   // resident k_recon_bwd CTAs per dynamic smem size
     cudaMemPool_t pool = nullptr;           // backward partials; keeps its memory between calls
+    // One constant bank per device: a forward's copy waits (on its own stream) for the previous
+    // forward's kernel to be done with it, and forwards are enqueued one at a time.
+    std::mutex bank_mu;
+    cudaEvent_t fwd_done = nullptr;
 };
 
 std::mutex g_state_mu;
@@ -380,6 +382,7 @@ DeviceState& state_of(int device) {
         AEISU_CUDA(cudaMemPoolCreate(&d.pool, &props));
         uint64_t keep = UINT64_MAX;
         AEISU_CUDA(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        AEISU_CUDA(cudaEventCreateWithFlags(&d.fwd_done, cudaEventDisableTiming));
         d.fwd_ctas = (long long)std::max(per_sm, 1) * sms;
         d.sms = sms;
     }
@@ -409,9 +412,16 @@ void reconstruct_f32(const float* src, const float* meta, const float* base, con
     j.base = base;
     j.basis = basis;
     j.out = out;
-    const long long grid = std::min<long long>(j.tiles, state_of(device).fwd_ctas);
+    DeviceState& ds = state_of(device);
+    const long long grid = std::min<long long>(j.tiles, ds.fwd_ctas);
+    std::lock_guard<std::mutex> lock(ds.bank_mu);
+    AEISU_CUDA(cudaStreamWaitEvent(stream, ds.fwd_done, 0));   // the previous forward has read the bank
+    AEISU_CUDA(cudaMemcpyToSymbolAsync(c_fwd_bank, base, kBase * sizeof(float), 0, cudaMemcpyDeviceToDevice, stream));
+    AEISU_CUDA(cudaMemcpyToSymbolAsync(c_fwd_bank, basis, (kBank - kBase) * sizeof(float), kBase * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, stream));
     k_recon_fwd<<<unsigned(grid), kRThreads, 0, stream>>>(j);
     AEISU_CUDA(cudaGetLastError());
+    AEISU_CUDA(cudaEventRecord(ds.fwd_done, stream));
 }
 
 void reconstruct_backward_f32(const float* src, const float* meta, const float* basis, const float* grad, int n,
