@@ -127,24 +127,29 @@ __global__ void __launch_bounds__(kRThreads) k_recon_fwd(ReconJob j) {
         __syncthreads();
         const int y = y0 + ty, x = x0 + tx;
         if (y >= j.ch || x >= j.cw) continue;
-        float c[16];
+        float2 cc[16];   // (c, c): one coefficient for both lanes of a phase pair
         const float* mp = j.meta + meta_at(j, b, y, x);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) c[k] = clamp_coef(__ldg(mp + k * kplane));
+        for (int k = 0; k < 16; ++k) {
+            const float c = clamp_coef(__ldg(mp + k * kplane));
+            cc[k] = make_float2(c, c);
+        }
         float2 o01[3], o23[3];   // phases (0, 1) and (2, 3) per channel
 #pragma unroll
         for (int ch = 0; ch < 3; ++ch) o01[ch] = o23[ch] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int t = 0; t < 25; ++t) {   // every bank index is a compile-time constant
             const int ky = t / 5, kx = t % 5;
-            float w[4] = {0.f, 0.f, 0.f, 0.f};
+            float2 w01 = make_float2(0.f, 0.f), w23 = w01;
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
-#pragma unroll
-                for (int p = 0; p < 4; ++p) w[p] = fmaf(c[k], c_fwd_bank[kBase + (t * 16 + k) * 4 + p], w[p]);
+            for (int k = 0; k < 16; ++k) {
+                const float* bk = c_fwd_bank + kBase + (t * 16 + k) * 4;
+                w01 = __ffma2_rn(cc[k], make_float2(bk[0], bk[1]), w01);
+                w23 = __ffma2_rn(cc[k], make_float2(bk[2], bk[3]), w23);
+            }
             // the reference's einsum, then the base add (reconstruction.py:70)
-            const float2 a = make_float2(__fadd_rn(c_fwd_bank[t * 4 + 0], w[0]), __fadd_rn(c_fwd_bank[t * 4 + 1], w[1]));
-            const float2 d = make_float2(__fadd_rn(c_fwd_bank[t * 4 + 2], w[2]), __fadd_rn(c_fwd_bank[t * 4 + 3], w[3]));
+            const float2 a = __fadd2_rn(make_float2(c_fwd_bank[t * 4 + 0], c_fwd_bank[t * 4 + 1]), w01);
+            const float2 d = __fadd2_rn(make_float2(c_fwd_bank[t * 4 + 2], c_fwd_bank[t * 4 + 3]), w23);
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
                 const float sv = s_win[ch][ty + ky][tx + kx];

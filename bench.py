@@ -349,8 +349,10 @@ def measure_train(dev, batch, sm_mhz=None):
         out.backward(grad)
         ev[3 * r + 2].record(stream)
     torch.cuda.synchronize(dev)
-    fwd = sum(ev[3 * r].elapsed_time(ev[3 * r + 1]) for r in range(runs)) / runs
-    bwd = sum(ev[3 * r + 1].elapsed_time(ev[3 * r + 2]) for r in range(runs)) / runs
+    # medians over the steps: autograd enqueues the backward from its worker thread, so one
+    # step's interval can include a host-side stall (GIL) during which the GPU idles
+    fwd = statistics.median(ev[3 * r].elapsed_time(ev[3 * r + 1]) for r in range(runs))
+    bwd = statistics.median(ev[3 * r + 1].elapsed_time(ev[3 * r + 2]) for r in range(runs))
     px = batch * ch * cw
     sel = batch * ((ch + stride - 1) // stride) * ((cw + stride - 1) // stride)
     # FP32 FLOPs: filter assembly 2 x 1,600 + apply 2 x 300 per core pixel forward; filter
@@ -376,8 +378,8 @@ def measure_train(dev, batch, sm_mhz=None):
             "cpu_port": {"value": 4 * ch * cw / cpu_s / 1e6, "unit": "output Mpix/s (forward + backward)",
                          "cores": 1, "kind": "port", "sample": f"1 source {w}x{h}, trim {trim}, stride {stride}, numpy FP32"},
             "config": f"batch {batch} x 3x{h}x{w} float32 sources, trim {trim} -> {2 * cw}x{2 * ch} outputs, "
-                      f"gradient_stride {stride}, phase 0; {runs} steps after {warm} warm-up steps, grads set to "
-                      "None before each step, CUDA events on the current stream"}
+                      f"gradient_stride {stride}, phase 0; medians of {runs} steps after {warm} warm-up steps, grads "
+                      "set to None before each step, CUDA events on the current stream"}
 
 
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
