@@ -12,7 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libaeisu_b200.so"
 
 OK, INVALID_ARG, BAD_ARTIFACT, CUDA, NONFINITE, TIMEOUT, UNSUPPORTED, OOM = range(8)
-PRECISIONS = {"fp32": 0, "fp16": 1, "mixed": 2}
+PRECISIONS = {"fp32": 0, "fp16": 1, "mixed": 2, "int8": 3}
 IO_HOST, IO_DEVICE = 0, 1
 FOLDED_VALUES = 115996
 
@@ -35,7 +35,19 @@ class Timings(C.Structure):
                 ("reconstruction_ms", C.c_float), ("total_ms", C.c_float), ("detailed", C.c_int)]
 
 
+class Int8Artifact(C.Structure):
+    """aeisu_int8_artifact of include/aeisu.h: the shader_precision_v1 arrays."""
+    _fields_ = [
+        ("analysis", C.c_void_p), ("base", C.c_void_p), ("bank", C.c_void_p),
+        ("project_w", C.c_void_p), ("refine_w", C.c_void_p), ("tail_w", C.c_void_p),
+        ("project_b", C.c_void_p), ("refine_b", C.c_void_p), ("tail_b", C.c_void_p),
+        ("int8_w", C.c_void_p * 6), ("int8_factor", C.c_void_p * 6), ("int8_bias", C.c_void_p * 6),
+        ("activation_scales", C.c_void_p),
+    ]
+
+
 _SIGNATURES = {
+    "aeisu_open_int8": (C.c_int, [C.POINTER(Int8Artifact), C.c_int, C.POINTER(C.c_void_p)]),
     "aeisu_open_spyr8": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
     "aeisu_validate_spyr8": (C.c_int, [C.c_void_p, C.c_size_t, C.c_char_p]),
     "aeisu_open_spyr8_memory": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),

@@ -90,6 +90,16 @@ int aeisu_open_spyr8(const char* path, int precision, int device, aeisu_t** out)
     });
 }
 
+int aeisu_open_int8(const aeisu_int8_artifact* artifact, int device, aeisu_t** out) {
+    return guarded([&] {
+        aeisu::require(out != nullptr, "output handle pointer is null");
+        *out = nullptr;
+        aeisu::require(artifact != nullptr, "artifact pointer is null");
+        aeisu::HostModel m = aeisu::load_int8(*artifact);
+        open_model(std::move(m), AEISU_PRECISION_INT8, device, out);
+    });
+}
+
 int aeisu_open_folded(const float* values, size_t count, float basis_l1_scale, int precision, int device,
                       aeisu_t** out) {
     return guarded([&] {

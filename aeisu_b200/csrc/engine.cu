@@ -156,12 +156,15 @@ struct Engine::DeviceGuard {
 
 Engine::Engine(HostModel model, int precision, int device)
     : model_(std::move(model)), precision_(precision), device_(device) {
-    require(precision >= AEISU_PRECISION_FP32 && precision <= AEISU_PRECISION_MIXED, "unknown precision");
+    require(precision >= AEISU_PRECISION_FP32 && precision <= AEISU_PRECISION_INT8, "unknown precision");
     int count = 0;
     AEISU_CUDA(cudaGetDeviceCount(&count));
     require(device >= 0 && device < count, "device index out of range");
     if (precision == AEISU_PRECISION_MIXED && !model_.has_fp8)
         fail(AEISU_ERR_UNSUPPORTED, "MIXED precision needs the FP8 weights and scales of a SPYR8 artifact");
+    if ((precision == AEISU_PRECISION_INT8) != model_.has_int8)
+        fail(AEISU_ERR_UNSUPPORTED, model_.has_int8 ? "the INT8 artifact runs only at INT8 precision"
+                                                    : "INT8 precision needs the INT8/FP16 artifact (aeisu_open_int8)");
     DeviceGuard guard(device_);
     cudaDeviceProp dp{};
     AEISU_CUDA(cudaGetDeviceProperties(&dp, device_));
@@ -180,9 +183,11 @@ Engine::Engine(HostModel model, int precision, int device)
     os << "aeisu-b200: device " << device_ << " " << prop.name << " (sm_" << prop.major << prop.minor << ", "
        << prop.multiProcessorCount << " SMs); model " << model_.format << " " << model_.architecture;
     if (!model_.checksum_hex.empty()) os << " sha256 " << model_.checksum_hex;
-    os << "; precision " << (precision_ == 0 ? "fp32" : precision_ == 1 ? "fp16" : "mixed");
+    os << "; precision " << (precision_ == 0 ? "fp32" : precision_ == 1 ? "fp16" : precision_ == 2 ? "mixed" : "int8");
     if (precision_ == AEISU_PRECISION_FP32) os << "; route simt-fp32 controller + fp32 head";
     else if (precision_ == AEISU_PRECISION_FP16) os << "; route tcgen05 f16 controller + tcgen05 head";
+    else if (precision_ == AEISU_PRECISION_INT8)
+        os << "; route tcgen05 int8-code/f16 controller (codes as f16, exact integer sums) + tcgen05 head";
     else os << "; route tcgen05 e4m3/f16 mixed controller + tcgen05 head";
     report_ = os.str();
 }
@@ -248,7 +253,7 @@ void Engine::upload_weights() {
     flag_.ensure(256, stream_);
     AEISU_CUDA(cudaMemset(flag_.get(), 0, 256));
     if (precision_ == AEISU_PRECISION_FP32) return;
-    const TcHostPack P = pack_tc(model_, precision_ == AEISU_PRECISION_MIXED);
+    const TcHostPack P = pack_tc(model_, tc_route_of(precision_));
     tc_bytes_.ensure(P.bytes.size(), stream_);
     tc_floats_.ensure(P.floats.size() * 4, stream_);
     AEISU_CUDA(cudaMemcpy(tc_bytes_.get(), P.bytes.data(), P.bytes.size(), cudaMemcpyHostToDevice));
@@ -401,7 +406,7 @@ void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& 
         mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
         const bool predict = c.mode == Mode::Predict;
         if (tcr) {
-            launch_tc_controller(fp8, src, rs, tcw_, enc540_.get(), encu_.get(), low_a_.get(), low_b_.get(),
+            launch_tc_controller(tc_route_of(precision_), src, rs, tcw_, enc540_.get(), encu_.get(), low_a_.get(), low_b_.get(),
                                  dec540_.get(), meta_.get(), predict ? raw_.as<float>() : nullptr,
                                  flag_.as<int>() + 1, s, &launches, mark);
         } else {

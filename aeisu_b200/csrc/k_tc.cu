@@ -57,7 +57,7 @@ using namespace tcd;
 constexpr int kProjRing = 8;
 constexpr int kProjTW = 2 * kM + 2;   // 258 LR columns per strip
 
-template <bool FP8>
+template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet rs, const float* __restrict__ stencil,
                                                          const uint8_t* __restrict__ wimg, const float* __restrict__ bias,
                                                          float slope, float inv_s1, void* __restrict__ enc540,
@@ -168,6 +168,24 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
                     pack_e4m3x32(q, o8);
 #pragma unroll
                     for (int c = 0; c < 2; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 8, p * 2 + c, lw, qx >> 1) = o8[c];
+                } else if (I8) {
+                    // compress input: int8 codes of (f16 skip value * 1/s1), held as f16
+                    // (int8_kernels.cuh:26: quantize_s8(skip, inverse_in))
+                    float q[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const __half2* h2 = reinterpret_cast<const __half2*>(&o[c]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 w = __fmul2_rn(__half22float2(h2[e]), f2(inv_s1));
+                            q[8 * c + 2 * e] = s8_code(w.x);
+                            q[8 * c + 2 * e + 1] = s8_code(w.y);
+                        }
+                    }
+                    uint4 o16[4];
+                    pack_f16x32(q, o16);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 16, p * 4 + c, lw, qx >> 1) = o16[c];
                 } else {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) *cp_at(encu, sb.r, lh, qy >> 1, 16, p * 4 + c, lw, qx >> 1) = o[c];
@@ -264,7 +282,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
 // ---- 1x1 convolutions at low resolution --------------------------------------------------------
 // compress_270 (K = 128, N = 64) and expand_270 (K = 64, N = 128 in phase-major order).
 // FP8: A/B e4m3 (16 per chunk); else f16 (8 per chunk).
-template <bool FP8>
+template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
                                                           const void* __restrict__ encu, void* __restrict__ out, int* err) {
     constexpr int KCH = FP8 ? 8 : 16;   // chunks of K = 128
@@ -322,7 +340,8 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + h * 32, v);
 #pragma unroll
-            epi_fma_leaky(v, s_scale + h * 32, s_bias + h * 32, ep.slope, FP8 ? ep.out_inv : 1.f);
+            epi_fma_leaky(v, s_scale + h * 32, s_bias + h * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+            if (I8) s8_codes32(v);
             if (x < lw) {
                 if (FP8) {
                     uint4 o[2];
@@ -344,7 +363,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
 // expand_270 + LeakyReLU + pixel_shuffle + enc540 skip -> dec540 (f16, packed grid).
 // Output channel order of B is phase-major (n = phase*32 + c), so TMEM columns
 // [32p, 32p+32) are the 32 channels of output pixel (2y + p/2, 2x + p%2).
-template <bool FP8>
+template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
                                                         const void* __restrict__ low, const void* __restrict__ enc540,
                                                         void* __restrict__ dec, int* err) {
@@ -410,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
             if (x < lw) {
                 const int oy = 2 * y + (p >> 1), ox = 2 * x + (p & 1);
                 const __half2* skh = reinterpret_cast<const __half2*>(sk[p]);
-                epi_fma_leaky(v, s_scale + p * 32, s_bias + p * 32, ep.slope, FP8 ? ep.out_inv : 1.f);
+                epi_fma_leaky(v, s_scale + p * 32, s_bias + p * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
                 if (FP8) {   // K8: requantise to e4m3 at 1/s7, dequantise
 #pragma unroll
                     for (int n = 0; n < 32; n += 4) {
@@ -420,11 +439,20 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
                         for (int j = 0; j < 4; ++j) v[n + j] = q[j] * ep.out_deq;
                     }
                 }
+                if (I8) {   // int8 code at 1/s7, then code * s7 + skip in one rounding (int8_kernels.cuh:56-59)
 #pragma unroll
-                for (int n = 0; n < 32; n += 2) {   // + the f16 skip
-                    const float2 a = __fadd2_rn(make_float2(v[n], v[n + 1]), __half22float2(skh[n / 2]));
-                    v[n] = a.x;
-                    v[n + 1] = a.y;
+                    for (int n = 0; n < 32; n += 2) {
+                        const float2 sk = __half22float2(skh[n / 2]);
+                        v[n] = fmaf(s8_code(v[n]), ep.out_deq, sk.x);
+                        v[n + 1] = fmaf(s8_code(v[n + 1]), ep.out_deq, sk.y);
+                    }
+                } else {
+#pragma unroll
+                    for (int n = 0; n < 32; n += 2) {   // + the f16 skip
+                        const float2 a = __fadd2_rn(make_float2(v[n], v[n + 1]), __half22float2(skh[n / 2]));
+                        v[n] = a.x;
+                        v[n + 1] = a.y;
+                    }
                 }
                 uint4 o[4];
                 pack_f16x32(v, o);
@@ -499,7 +527,7 @@ struct Ring {
 // (slot_free).
 constexpr int kWsThreads = 160;
 
-template <bool FP8>
+template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                         const uint8_t* __restrict__ wimg, EpiParams ep,
                                                         void* __restrict__ out, int band, int* err) {
@@ -638,7 +666,8 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
-                    epi_fma_leaky(v, s_scale, s_bias, ep.slope, FP8 ? ep.out_inv : 1.f);
+                    epi_fma_leaky(v, s_scale, s_bias, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+                    if (I8) s8_codes32(v);
                     if (t < kConvStrip && x < lw) {
                         if (FP8) {
                             uint4 q[2];
@@ -1234,11 +1263,12 @@ int pick_band_balanced(long long strips_x_regions, int rows, int slots) {
 
 }  // namespace
 
-void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
+void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
                           int* err, cudaStream_t s, int* launches, const StageMark& mark) {
     const int sms = sm_count();
     const bool pdl = use_pdl(rs);
+    const bool fp8 = route == kRouteE4M3, i8 = route == kRouteI8;
     const int ph = rs.rh / 2, pw = rs.rw / 2, lh = rs.rh / 4, lw = rs.rw / 4;
     const long long low_tiles = (long long)rs.R * lh * ((lw + kM - 1) / kM);
     {
@@ -1246,15 +1276,17 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const int band = pick_band(strips, ph, sms * 4);
         const long long items = strips * ((ph + band - 1) / band);
         const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;
-        if (fp8) { smem_attr(k_tc_project<true>, bytes); launch(pdl, k_tc_project<true>, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err); }
-        else { smem_attr(k_tc_project<false>, bytes); launch(pdl, k_tc_project<false>, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, 0.f, enc540, encu, band, err); }
+        auto kp = fp8 ? k_tc_project<true> : i8 ? k_tc_project<false, true> : k_tc_project<false>;
+        smem_attr(kp, bytes);
+        launch(pdl, kp, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err);
     }
     mark(1);
     {
         const int kch = fp8 ? 8 : 16;
         const int bytes = kch * kM * 16 + kch * 64 * 16 + 2 * 64 * 4;
-        if (fp8) { smem_attr(k_tc_compress<true>, bytes); launch(pdl, k_tc_compress<true>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
-        else { smem_attr(k_tc_compress<false>, bytes); launch(pdl, k_tc_compress<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err); }
+        auto kc = fp8 ? k_tc_compress<true> : i8 ? k_tc_compress<false, true> : k_tc_compress<false>;
+        smem_attr(kc, bytes);
+        launch(pdl, kc, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err);
     }
     {
         // one group per CTA (two CTAs per work item), four CTAs per SM; bands hold whole row pairs
@@ -1269,18 +1301,18 @@ void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, con
         const CUtensorMap map_b = make_row_window_map(low_b, rs.R, lh, ich, lw, kM, cpg);
         void* bufs[2] = {low_a, low_b};
         const CUtensorMap* maps[2] = {&map_a, &map_b};
-        if (fp8) smem_attr(k_tc_core<true>, bytes); else smem_attr(k_tc_core<false>, bytes);
-        for (int i = 0; i < 4; ++i) {
-            if (fp8) launch(pdl, k_tc_core<true>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-            else launch(pdl, k_tc_core<false>, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
-        }
+        auto kk = fp8 ? k_tc_core<true> : i8 ? k_tc_core<false, true> : k_tc_core<false>;
+        smem_attr(kk, bytes);
+        for (int i = 0; i < 4; ++i)
+            launch(pdl, kk, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
     }
     mark(2);
     {
         const int kch = fp8 ? 4 : 8;
         const int bytes = kch * kM * 16 + kch * 128 * 16 + 2 * 128 * 4;
-        if (fp8) { smem_attr(k_tc_expand<true>, bytes); launch(pdl, k_tc_expand<true>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
-        else { smem_attr(k_tc_expand<false>, bytes); launch(pdl, k_tc_expand<false>, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err); }
+        auto ke = fp8 ? k_tc_expand<true> : i8 ? k_tc_expand<false, true> : k_tc_expand<false>;
+        smem_attr(ke, bytes);
+        launch(pdl, ke, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err);
     }
     mark(3);
     {

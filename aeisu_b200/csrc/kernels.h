@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "../../include/aeisu.h"
+
 namespace aeisu {
 
 // Source frames.  Padded-grid coordinate p maps to source pixel clamp(p - pad, 0, dim-1):
@@ -56,10 +58,10 @@ void launch_f32_controller(const SrcDesc& src, const RegionSet& rs, const float*
                            const StageMark& mark, float* peaks = nullptr, double* sums = nullptr);
 // Epilogue parameters of a tensor-core convolution layer.
 struct EpiParams {
-    const float* scale;   // per output channel: accumulator multiplier (FP8: s_in * w_scale)
+    const float* scale;   // per output channel: accumulator multiplier (FP8: s_in * w_scale; INT8: factor)
     const float* bias;    // per output channel
     float slope;          // LeakyReLU negative slope
-    float out_inv;        // FP8 output quantisation: 1/s_out
+    float out_inv;        // FP8 / INT8 output quantisation: 1/s_out
     float out_deq;        // expand: dequantisation s_out
 };
 
@@ -70,7 +72,7 @@ struct TcWeights {
     const uint8_t* project;        // [4 chunks][32][16 B] f16
     const float* project_bias;
     float slope;
-    float inv_s1;                  // 1/activation_scales[1] (mixed route)
+    float inv_s1;                  // 1/activation_scales[1] (e4m3 and int8 routes; else 1)
     const uint8_t* compress;       // [K/epc][64][16 B], K order phase*32 + c
     EpiParams compress_ep;
     const uint8_t* core[4];        // 2 groups x [9*32/epc][32][16 B], K order tap*32 + c
@@ -84,10 +86,18 @@ struct TcWeights {
     const uint8_t* head;           // 3 x [2][128][16 B] f16: basis hi, basis lo, base hi|lo
 };
 
-// Tensor-core route (k_tc.cu).  fp8 selects the mixed FP8/FP16 route, else FP16.
+// Controller routes of the tensor-core kernels: f16 activations everywhere; e4m3 compress /
+// core / expand (the SPYR8 mixed route); int8 codes held as f16 in compress / core / expand
+// (the shader_precision_v1 route: f16 MMAs over the codes give its exact integer sums).
+enum TcRoute : int { kRouteF16 = 0, kRouteE4M3 = 1, kRouteI8 = 2 };
+inline int tc_route_of(int precision) {
+    return precision == AEISU_PRECISION_MIXED ? kRouteE4M3 : precision == AEISU_PRECISION_INT8 ? kRouteI8 : kRouteF16;
+}
+
+// Tensor-core route (k_tc.cu).
 // Buffers are chunk-planar: enc540 [R][ph][4][pw][16], encu [R][lh][K/epc][lw][16],
 // low [R][lh][64/epc][lw][16], dec540 [R][ph][4][pw][16], meta [R][rh][2][rw][16].
-void launch_tc_controller(bool fp8, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
+void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
                           int* err, cudaStream_t s, int* launches, const StageMark& mark);
 void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const void* meta,

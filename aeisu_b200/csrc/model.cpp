@@ -325,4 +325,74 @@ HostModel load_spyr8(const uint8_t* data, size_t size) {
     return m;
 }
 
+HostModel load_int8(const aeisu_int8_artifact& a) {
+    // Checks of MixedRuntime.__init__ (optimized/shader/runtime.py:37-59) that concern the
+    // arrays themselves; the format and precision policy are checked by the caller, which
+    // reads the .pt record.
+    auto bad = [](const std::string& msg) { fail(AEISU_ERR_BAD_ARTIFACT, "INT8 artifact: " + msg); };
+    auto finite = [&](const float* p, size_t n, const char* what) {
+        if (!p) bad(std::string(what) + " is missing");
+        for (size_t i = 0; i < n; ++i)
+            if (!std::isfinite(p[i])) bad(std::string(what) + " has a non-finite value");
+    };
+    HostModel m;
+    m.format = "shader_int8";
+    m.architecture = "shader_precision_v1 int8/fp16";
+    m.has_int8 = true;
+    finite(a.analysis, 24, "analysis_parameters");
+    finite(a.base, 100, "base");
+    finite(a.bank, 1600, "bank");
+    finite(a.activation_scales, 10, "activation_scales");
+    std::copy(a.analysis, a.analysis + 24, m.stencil);
+    std::copy(a.base, a.base + 100, m.base);
+    std::copy(a.bank, a.bank + 1600, m.basis);
+    for (int i = 0; i < 10; ++i) {
+        if (!(a.activation_scales[i] > 0.f)) bad("activation scales must be positive");
+        m.act_scales[i] = a.activation_scales[i];
+    }
+    auto half_layer = [&](int l, const uint16_t* w, const float* b, const char* name) {
+        const LayerSpec& sp = kLayerSpecs[l];
+        const size_t n = size_t(sp.cout) * sp.cin_per_group * sp.k * sp.k;
+        if (!w) bad(std::string(name) + " weights are missing");
+        LayerWeights& L = m.layers[l];
+        L.w_fp16.assign(w, w + n);
+        L.w.resize(n);
+        for (size_t i = 0; i < n; ++i) {
+            L.w[i] = f16_bits_to_f32(w[i]);
+            if (!std::isfinite(L.w[i])) bad(std::string(name) + " weights have a non-finite value");
+        }
+        finite(b, sp.cout, name);
+        L.bias.assign(b, b + sp.cout);
+        L.bias_fp8 = L.bias;
+        L.slope.assign(sp.cout, l == kTail ? 1.0f : 0.1f);
+    };
+    half_layer(kProject, a.project_w, a.project_b, "project");
+    half_layer(kRefine, a.refine_w, a.refine_b, "refine");
+    half_layer(kTail, a.tail_w, a.tail_b, "tail");
+    static const int kInt8Layers[6] = {kCompress, kCore0, kCore1, kCore2, kCore3, kExpand};
+    static const char* kNames[6] = {"compress", "bottleneck0", "bottleneck1", "bottleneck2", "bottleneck3", "expand"};
+    for (int i = 0; i < 6; ++i) {
+        const int l = kInt8Layers[i];
+        const LayerSpec& sp = kLayerSpecs[l];
+        const size_t n = size_t(sp.cout) * sp.cin_per_group * sp.k * sp.k;
+        if (!a.int8_w[i]) bad(std::string(kNames[i]) + " weights are missing");
+        finite(a.int8_factor[i], sp.cout, kNames[i]);
+        finite(a.int8_bias[i], sp.cout, kNames[i]);
+        LayerWeights& L = m.layers[l];
+        L.w.resize(n);
+        L.w_fp16.resize(n);
+        for (size_t k = 0; k < n; ++k) {
+            const int q = a.int8_w[i][k];
+            if (q < -127 || q > 127) bad(std::string(kNames[i]) + " has a weight code outside [-127, 127]");
+            L.w[k] = float(q);
+            L.w_fp16[k] = f32_to_f16_bits(float(q));   // exact: |q| <= 127
+        }
+        L.factor.assign(a.int8_factor[i], a.int8_factor[i] + sp.cout);
+        L.bias.assign(a.int8_bias[i], a.int8_bias[i] + sp.cout);
+        L.bias_fp8 = L.bias;
+        L.slope.assign(sp.cout, 0.1f);
+    }
+    return m;
+}
+
 }  // namespace aeisu

@@ -6,6 +6,8 @@
 #include <string>
 #include <vector>
 
+#include "../../include/aeisu.h"
+
 namespace aeisu {
 
 // Controller layers in execution order (aeisu/model.py:473-492).  The four grouped
@@ -26,6 +28,8 @@ struct LayerWeights {
     std::vector<uint16_t> w_fp16;  // OIHW IEEE half bits
     std::vector<uint8_t> w_fp8;    // OIHW E4M3 codes (SPYR8 only)
     std::vector<float> w_scale;    // per-output-channel FP8 weight scale (SPYR8 only)
+    std::vector<float> factor;     // per-output-channel INT8 accumulator multiplier (INT8 artifact only;
+                                   // w / w_fp16 then hold the int8 codes)
 };
 
 struct HostModel {
@@ -37,7 +41,8 @@ struct HostModel {
     LayerWeights layers[kLayerCount];
     float act_scales[10] = {};  // SPYR8 activation scales (Appendix of the artifact contract)
     bool has_fp8 = false;
-    std::string format;         // "folded" or "spyr8"
+    bool has_int8 = false;      // INT8 artifact: compress/core/expand as int8 codes and factors
+    std::string format;         // "folded", "spyr8" or "shader_int8"
     std::string checksum_hex;   // SPYR8 SHA-256
     std::string architecture;
 };
@@ -47,6 +52,9 @@ HostModel load_folded(const float* values, size_t count, float basis_l1_scale);
 
 // SPYR8 v1 artifact bytes (parsing and validation of SrcPyrModel.cpp:243-470, restated).
 HostModel load_spyr8(const uint8_t* data, size_t bytes);
+
+// INT8/FP16 artifact arrays (shader_precision_v1), validated.
+HostModel load_int8(const aeisu_int8_artifact& a);
 
 // IEEE binary16 helpers (round to nearest even).
 uint16_t f32_to_f16_bits(float f);

@@ -133,7 +133,7 @@ void upscale_u8_noalloc(Engine& e, const uint8_t* src, int n, int h, int w, uint
         uint8_t* meta = p;
         StageMark none;
         if (tcr) {
-            launch_tc_controller(fp8, sd, rs, *res.tc, enc540, encu, low_a, low_b_, dec540, meta, nullptr,
+            launch_tc_controller(tc_route_of(prec), sd, rs, *res.tc, enc540, encu, low_a, low_b_, dec540, meta, nullptr,
                                  res.flags + 1, s, &launches, none);
             launch_tc_head(sd, rs, dd, meta, res.head_img, res.flags, res.flags + 1, s, &launches);
         } else {

@@ -38,6 +38,15 @@ __device__ __forceinline__ void epi_fma_leaky(float (&v)[32], const float* scale
         v[2 * i + 1] = a.y;
     }
 }
+// INT8 route: the int8 code of an already scaled value, as the shader route's quantize_s8
+// (optimized/shader/src/int8_kernels.cuh:2-4): round to nearest even, clamp to [-127, 127]
+// (NaN gives 0).  Kept as a float: f16 holds every code exactly, so f16 MMAs over the codes
+// accumulate the exact integer dot products (|sum| <= 576 * 127^2 < 2^24 in FP32).
+__device__ __forceinline__ float s8_code(float v) { return float(max(-127, min(127, __float2int_rn(v)))); }
+__device__ __forceinline__ void s8_codes32(float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = s8_code(v[i]);
+}
 //   v = leaky(v + bias)
 __device__ __forceinline__ void epi_add_leaky(float (&v)[32], const float* bias, float slope) {
     const float2* b2 = reinterpret_cast<const float2*>(bias);

@@ -23,17 +23,21 @@ float round_f16(float v) { return f16_bits_to_f32(f32_to_f16_bits(v)); }
 
 }  // namespace
 
-TcHostPack pack_tc(const HostModel& m, bool fp8) {
+TcHostPack pack_tc(const HostModel& m, int route) {
+    const bool fp8 = route == kRouteE4M3, i8 = route == kRouteI8;
     require(!fp8 || m.has_fp8, "the mixed route needs the FP8 weights and scales of a SPYR8 artifact",
             AEISU_ERR_UNSUPPORTED);
+    require(i8 == m.has_int8, "the INT8 route needs, and only runs, the INT8 artifact", AEISU_ERR_UNSUPPORTED);
     TcHostPack P;
     // Activation scales of the artifact times a power-of-two headroom.  E4M3 is a floating
     // point format, so the factor leaves the rounding of every value below the old limit
     // bit-identical and only stops values in [448 s, 448 hs) from saturating (the artifact was
     // calibrated on natural images; high-contrast content exceeds its range in the later
     // bottleneck layers).
+    // The INT8 route uses the artifact's scales as they are: int8 codes saturate at +-127 there
+    // exactly as in the reference's kernels.
     float s[10];
-    for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * kFp8ActivationHeadroom;
+    for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * (i8 ? 1.0f : kFp8ActivationHeadroom);
     // one LeakyReLU slope for every activated layer (the tail is linear), in [0, 1] so that the
     // kernels may evaluate it as max(v, slope * v)
     P.slope = m.layers[kProject].slope[0];
@@ -43,7 +47,7 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
             for (float v : m.layers[l].slope)
                 require(v == P.slope, "the tensor-core routes need one activation slope for all layers",
                         AEISU_ERR_UNSUPPORTED);
-    P.inv_s1 = fp8 ? 1.0f / s[1] : 1.f;
+    P.inv_s1 = (fp8 || i8) ? 1.0f / s[1] : 1.f;
     P.stencil = append_floats(P.floats, std::vector<float>(m.stencil, m.stencil + 24));
 
     // project_540: [32 out][32 in], K = torch input channel order (feature c*4 + phase)
@@ -57,12 +61,12 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         std::vector<float> scale(n), bias(n);
         for (int i = 0; i < n; ++i) {
             const int o = perm(i);
-            scale[i] = fp8 ? s_in * L.w_scale[o] : 1.f;
+            scale[i] = fp8 ? s_in * L.w_scale[o] : i8 ? L.factor[o] : 1.f;
             bias[i] = fp8 ? L.bias_fp8[o] : L.bias[o];
         }
         out.scale = append_floats(P.floats, scale);
         out.bias = append_floats(P.floats, bias);
-        out.out_inv = fp8 ? 1.0f / s_out : 1.f;
+        out.out_inv = (fp8 || i8) ? 1.0f / s_out : 1.f;
     };
     const int es = fp8 ? 1 : 2;
     auto elem = [&](const LayerWeights& L, size_t idx) -> uint32_t { return fp8 ? L.w_fp8[idx] : L.w_fp16[idx]; };
@@ -99,7 +103,7 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
             return elem(L, size_t(torch_out(n)) * 64 + k);
         }));
         epilogue(P.expand, L, 128, s[6], s[7], torch_out);
-        P.expand.out_deq = fp8 ? s[7] : 1.f;
+        P.expand.out_deq = (fp8 || i8) ? s[7] : 1.f;
     }
     // refine_540: [64][9 taps x 32] f16 in both routes, chunks ordered [kx][k4][ky] (k4: 8 input
     // channels) so that the blocks of tap rows ky and ky+1 are adjacent and one N = 128 operand
@@ -114,7 +118,9 @@ TcHostPack pack_tc(const HostModel& m, bool fp8) {
         const LayerWeights& T = m.layers[kTail];
         P.tail = append_bytes(P.bytes, pack_operand(64, 64, 2, [&](int n, int k) { return T.w_fp16[n * 64 + k]; }));
         std::vector<float> tb(64);
-        for (int i = 0; i < 64; ++i) tb[i] = round_f16(T.bias[i]);  // f16 tail bias (Refine.cuh:494-495)
+        // f16 tail bias on the native routes (Refine.cuh:494-495); the INT8 route's finish adds
+        // its FP32 bias (optimized/shader/runtime.py:221, finish_controller)
+        for (int i = 0; i < 64; ++i) tb[i] = i8 ? T.bias[i] : round_f16(T.bias[i]);
         P.tail_bias = append_floats(P.floats, tb);
     }
     // head: 100 of 128 columns, FP32 bank split into hi + lo f16.  Columns 0..79 hold the

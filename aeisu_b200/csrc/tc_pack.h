@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <vector>
 
+#include "kernels.h"
 #include "model.h"
 
 namespace aeisu {
@@ -30,9 +31,11 @@ struct TcHostPack {
     float slope = 0.1f, inv_s1 = 1.f;
 };
 
-// fp8: mixed route (e4m3 compress/core/expand from the artifact's FP8 weights and scales);
-// otherwise FP16 route (f16 weights everywhere).
-TcHostPack pack_tc(const HostModel& m, bool fp8);
+// route (TcRoute of kernels.h): kRouteE4M3, the mixed route (e4m3 compress/core/expand from a
+// SPYR8 artifact's FP8 weights and scales); kRouteI8, the INT8 route (int8 codes as f16 with
+// the INT8 artifact's factors, biases and exact activation scales); kRouteF16, f16 weights
+// everywhere.
+TcHostPack pack_tc(const HostModel& m, int route);
 
 // Operand image of a logical [N][K] matrix: chunk c, row n at (c*N + n)*16 bytes; esize 2
 // (f16 bits, 8 per chunk) or 1 (e4m3 codes, 16 per chunk).  get(n, k) returns the element bits.

@@ -3,6 +3,7 @@
 Reference surface mirrored (paths relative to the AELabs42/AEISU checkout):
 
 * ``load_model(path, device)``  -> aeisu/runtime.py:45-56 (folded ``.pt``); also SPYR8 ``.bin``
+  and the INT8/FP16 ``shader_precision_v1`` ``.pt`` (optimized/shader/runtime.py:37-59)
 * ``upscale(model, source, tile=128)`` -> aeisu/runtime.py:70-103 (same padding, tiling,
   ValueError / FloatingPointError behaviour, clamped CHW float32 result)
 * ``model(src)`` / ``model.predict_coefficients(src)`` -> FoldedAEISU.forward /
@@ -40,6 +41,43 @@ FOLDED_KEYS = (
       for item in ((f"{name}.weight", (cout, cin, k, k)), (f"{name}.bias", (cout,)))),
 )
 SPYR8_MAGIC = b"SPYR8F8\0"
+# optimized/shader/runtime.py:34, 41-43: the one published INT8/FP16 policy
+INT8_LAYERS = ("compress", "bottleneck0", "bottleneck1", "bottleneck2", "bottleneck3", "expand")
+INT8_POLICY = {"project": "fp16", **{name: "int8" for name in INT8_LAYERS}, "refine": "fp16", "tail": "fp16"}
+
+
+def int8_arrays(record):
+    """The arrays of a shader_precision_v1 record (optimized/shader/weights/aeisu_int8_fp16.pt),
+    checked as MixedRuntime.__init__ checks them (optimized/shader/runtime.py:37-43), as
+    contiguous numpy arrays keyed by their aeisu_int8_artifact field."""
+    if not isinstance(record, dict) or record.get("format") != "shader_precision_v1" \
+            or record.get("precision_policy") != INT8_POLICY or record.get("all_int8"):
+        raise ValueError("This runner accepts only the published mixed INT8/FP16 policy")
+
+    def arr(value, dtype, shape):
+        a = np.ascontiguousarray(np.asarray(value.numpy() if hasattr(value, "numpy") else value).astype(dtype))
+        if a.shape != shape:
+            raise ValueError(f"INT8 artifact tensor has shape {a.shape}, expected {shape}")
+        return a
+
+    half, hb = record["half_weights"], record["half_biases"]
+    out = {"analysis": arr(record["analysis_parameters"], np.float32, (24,)),
+           "base": arr(record["base"], np.float32, (25, 4)),
+           "bank": arr(record["bank"], np.float32, (25, 16, 4)),
+           "project_w": arr(half["project"], np.float16, (32, 32, 1, 1)).view(np.uint16),
+           "refine_w": arr(half["refine"], np.float16, (64, 32, 3, 3)).view(np.uint16),
+           "tail_w": arr(half["tail"], np.float16, (64, 64, 1, 1)).view(np.uint16),
+           "project_b": arr(hb["project"], np.float32, (32,)),
+           "refine_b": arr(hb["refine"], np.float32, (64,)),
+           "tail_b": arr(hb["tail"], np.float32, (64,)),
+           "activation_scales": arr(record["activation_scales"], np.float32, (10,))}
+    shapes = {"compress": (64, 128, 1, 1), "expand": (128, 64, 1, 1)}
+    for name in INT8_LAYERS:
+        co = shapes.get(name, (64, 32, 3, 3))
+        out[f"{name}.w"] = arr(record["int8_weights"][name], np.int8, co)
+        out[f"{name}.factor"] = arr(record["int8_factors"][name], np.float32, (co[0],))
+        out[f"{name}.bias"] = arr(record["int8_biases"][name], np.float32, (co[0],))
+    return out
 
 
 def _device_index(device) -> int:
@@ -139,6 +177,23 @@ class Model:
         _lib.check(_lib.lib().aeisu_open_spyr8_memory(buf, len(data), _lib.PRECISIONS[precision], dev,
                                                       C.byref(h)))
         return cls(h, dev, precision)
+
+    @classmethod
+    def from_int8_record(cls, record, device="cuda"):
+        """The INT8/FP16 route of a shader_precision_v1 record (precision "int8" only)."""
+        a = int8_arrays(record)
+        dev = _device_index(device)
+        st = _lib.Int8Artifact()
+        for key in ("analysis", "base", "bank", "project_w", "refine_w", "tail_w", "project_b", "refine_b",
+                    "tail_b", "activation_scales"):
+            setattr(st, key, a[key].ctypes.data)
+        for i, name in enumerate(INT8_LAYERS):
+            st.int8_w[i] = a[f"{name}.w"].ctypes.data
+            st.int8_factor[i] = a[f"{name}.factor"].ctypes.data
+            st.int8_bias[i] = a[f"{name}.bias"].ctypes.data
+        h = C.c_void_p()
+        _lib.check(_lib.lib().aeisu_open_int8(C.byref(st), dev, C.byref(h)))
+        return cls(h, dev, "int8")
 
     def close(self):
         if getattr(self, "_h", None):
@@ -305,7 +360,9 @@ class Model:
 
 def load_model(path, device="cuda", precision=None) -> Model:
     """runtime.load_model (aeisu/runtime.py:45-56) for folded ``.pt`` checkpoints, plus
-    SPYR8 ``.bin`` artifacts.  precision defaults to fp32 for ``.pt`` and mixed for SPYR8."""
+    SPYR8 ``.bin`` artifacts and the INT8/FP16 ``shader_precision_v1`` ``.pt``
+    (optimized/shader/runtime.py:37-59).  precision defaults to fp32 for a folded ``.pt``,
+    mixed for SPYR8 and int8 (its only precision) for the INT8 artifact."""
     path = Path(path)
     with path.open("rb") as f:
         head = f.read(8)
@@ -313,6 +370,10 @@ def load_model(path, device="cuda", precision=None) -> Model:
         return Model.from_spyr8_bytes(path.read_bytes(), device, precision or "mixed")
     import torch  # checkpoint container only
     payload = torch.load(path, map_location="cpu", weights_only=True)
+    if isinstance(payload, dict) and payload.get("format") == "shader_precision_v1":
+        if precision not in (None, "int8"):
+            raise ValueError("the INT8/FP16 artifact runs only at precision int8")
+        return Model.from_int8_record(payload, device)
     state = _checkpoint_state(payload)
     scale = payload.get("basis_l1_scale", payload.get("config", {}).get("basis_l1_scale", 0.5)) \
         if isinstance(payload, dict) else 0.5

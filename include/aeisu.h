@@ -51,11 +51,17 @@ typedef enum aeisu_status {
  * FP32  : every layer FP32 (the parity path; aeisu/model.py semantics).
  * FP16  : FP16 operands, FP32 accumulate (reference "Fp16" route).
  * MIXED : FP8-E4M3 compress/core/expand, FP16 project/refine/tail, as laid out by
- *         the SPYR8 artifact (reference "Mixed" route, SrcPyrCudaRuntime.cu:4131-4873). */
+ *         the SPYR8 artifact (reference "Mixed" route, SrcPyrCudaRuntime.cu:4131-4873).
+ * INT8  : int8 compress/core/expand, FP16 project/refine/tail, as the shader_precision_v1
+ *         artifact lays out (conventional-CUDA route, optimized/shader/runtime.py:173-221):
+ *         int8 activation codes at the artifact's scales, per-channel factors and biases; the
+ *         codes run as f16 on the tensor cores, whose FP32 sums of them are the exact integer
+ *         dot products.  Only models opened with aeisu_open_int8 have it. */
 typedef enum aeisu_precision {
     AEISU_PRECISION_FP32 = 0,
     AEISU_PRECISION_FP16 = 1,
-    AEISU_PRECISION_MIXED = 2
+    AEISU_PRECISION_MIXED = 2,
+    AEISU_PRECISION_INT8 = 3
 } aeisu_precision;
 
 /* Flags for the I/O calls. */
@@ -89,6 +95,33 @@ int aeisu_open_spyr8_memory(const void* data, size_t bytes, int precision, int d
  * FP16 (MIXED needs the FP8 scales of a SPYR8 artifact). */
 int aeisu_open_folded(const float* values, size_t count, float basis_l1_scale,
                       int precision, int device, aeisu_t** out);
+
+/* The shader_precision_v1 INT8/FP16 artifact (optimized/shader/weights/aeisu_int8_fp16.pt as
+ * MixedRuntime reads it, optimized/shader/runtime.py:37-59) as plain host arrays; the Python
+ * binding (aeisu_b200.load_model) unpacks the .pt and checks its format and precision policy
+ * as runtime.py:41-43 does.  Weights are OIHW; the four bottleneck tensors hold both branches
+ * ([64][32][3][3], groups 2); half weights are IEEE binary16 bits.  Replaces
+ * MixedRuntime.__init__ (runtime.py:37-59). */
+typedef struct aeisu_int8_artifact {
+    const float* analysis;           /* [24] analysis_parameters (rgb basis, mix, dx, dy, d45, d135) */
+    const float* base;               /* [25][4] */
+    const float* bank;               /* [25][16][4] projected basis */
+    const uint16_t* project_w;       /* [32][32]          half_weights["project"] */
+    const uint16_t* refine_w;        /* [64][32][3][3]    half_weights["refine"] */
+    const uint16_t* tail_w;          /* [64][64]          half_weights["tail"] */
+    const float* project_b;          /* [32]  half_biases */
+    const float* refine_b;           /* [64] */
+    const float* tail_b;             /* [64] */
+    const int8_t* int8_w[6];         /* compress [64][128], bottleneck0..3 [64][32][3][3], expand [128][64] */
+    const float* int8_factor[6];     /* per output channel: accumulator multiplier */
+    const float* int8_bias[6];       /* per output channel */
+    const float* activation_scales;  /* [10] */
+} aeisu_int8_artifact;
+
+/* Open a model from the INT8/FP16 artifact on GPU `device`; its only precision is
+ * AEISU_PRECISION_INT8.  AEISU_ERR_BAD_ARTIFACT for a missing array, a non-finite value, a
+ * non-positive scale or a weight code outside [-127, 127]. */
+int aeisu_open_int8(const aeisu_int8_artifact* artifact, int device, aeisu_t** out);
 
 void aeisu_close(aeisu_t* handle);
 

@@ -15,6 +15,19 @@ Mixed FP8-E4M3/FP16 route of the reference's native runtime, quantisation point 
 * head (AdaptiveReconstruction.cuh:288-417): f16 coefficients, FP32 filter mix and apply.
 
 FP16 route: the same graph with f16 weights and f16-rounded activations at every layer output.
+
+INT8 route of the conventional-CUDA deployment (optimized/shader/runtime.py:173-221 over
+optimized/shader/src/int8_kernels.cuh), from the shader_precision_v1 record:
+
+* int8 code q(x) = clamp(round_half_even(x), -127, 127) (quantize_s8, int8_kernels.cuh:2-4)
+* compress (int8_body COMPRESS, :18-31, 46-52): q(skip * (1/s1)); integer dot products with the
+  int8 weights; acc*factor + bias in one rounding; LeakyReLU; q(y * (1/s2))
+* bottleneck 0..3 (int8_pair, :159-199, grouped 3x3, zero padding): outputs q(y * (1/s3..s6))
+* expand (int8_body EXPAND, :46-59): q(y * (1/s7)); code*s7 + skip in one rounding; f16
+* project, refine, tail and head as in this module's f16 layers (float accumulation; the
+  reference's own FP16 kernels accumulate some sums in half, fusion_kernels.cu:174-184), with the
+  tail adding its FP32 bias.
+
 E4M3 rounding here is an independent implementation (exponent/step arithmetic, ties to even,
 saturation at +-448), cross-checked in the CPU tests against torch.float8_e4m3fn.
 """
@@ -52,6 +65,34 @@ def e4m3_decode(codes):
     return np.where(c & 0x80, -mag, mag).astype(F32)
 
 
+def int8_code(x):
+    """quantize_s8 of an already scaled float32 value: round half to even, clamp to +-127."""
+    return np.clip(np.rint(np.asarray(x, F32)), -127, 127).astype(F32)
+
+
+def _fma(a, b, c):
+    """float32 a*b + c with one rounding (the products here are exact in float64)."""
+    return (np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)).astype(F32)
+
+
+INT8_LAYERS = ("compress", "bottleneck0", "bottleneck1", "bottleneck2", "bottleneck3", "expand")
+
+
+def int8_record_tensors(record):
+    """The tensors of a shader_precision_v1 record under this module's names."""
+    a = lambda v, dt=F32: np.asarray(v).astype(dt)
+    t = {"activation_scales": a(record["activation_scales"]), "adaptive_basis": a(record["bank"]),
+         "adaptive_base": a(record["base"]), "analysis_stencil": a(record["analysis_parameters"])}
+    for name in ("project", "refine", "tail"):
+        t[f"{name}.weight_fp16"] = a(record["half_weights"][name], np.float16)
+        t[f"{name}.bias"] = a(record["half_biases"][name])
+    for name in INT8_LAYERS:
+        t[f"{name}.weight_int8"] = a(record["int8_weights"][name], np.int8)
+        t[f"{name}.factor"] = a(record["int8_factors"][name])
+        t[f"{name}.bias_int8"] = a(record["int8_biases"][name])
+    return t
+
+
 def _unshuffle(x):
     b, h, w, c = x.shape
     return x.reshape(b, h // 2, 2, w // 2, 2, c).transpose(0, 1, 3, 5, 2, 4).reshape(b, h // 2, w // 2, c * 4)
@@ -68,8 +109,9 @@ def _conv(x, w, b, groups=1):
 
 
 class QuantizedModel:
-    """Reduced-precision restatement.  ``t`` holds SPYR8 tensors (names as in the artifact);
-    ``mode`` is "mixed" (FP8 compress/core/expand) or "fp16"."""
+    """Reduced-precision restatement.  ``t`` holds SPYR8 tensors (names as in the artifact) for
+    ``mode`` "mixed" (FP8 compress/core/expand) or "fp16", or the tensors of
+    ``int8_record_tensors`` for ``mode`` "int8"."""
 
     def __init__(self, t, mode="mixed", headroom=1.0):
         """headroom: power-of-two factor on the artifact's activation scales (1 = the
@@ -93,6 +135,11 @@ class QuantizedModel:
         scale = (F32(s_in) * np.asarray(self.t[f"{name}.weight_scale"], F32)).astype(F32)
         return O.leaky((acc * scale + np.asarray(self.t[f"{name}.bias_fp8"], F32)).astype(F32))
 
+    def _int8_layer(self, codes, name, groups=1):
+        """Integer dot products (exact in float32: |sum| < 2^24), acc*factor + bias, LeakyReLU."""
+        acc = _conv(codes, np.asarray(self.t[f"{name}.weight_int8"], F32), None, groups)
+        return O.leaky(_fma(acc, self.t[f"{name}.factor"], self.t[f"{name}.bias_int8"]))
+
     def _f16_layer(self, x, name, act=True, groups=1, bias=None):
         y = _conv(x, self.w16(name), np.asarray(self.t[f"{name}.bias"], F32) if bias is None else bias, groups)
         return O.leaky(y) if act else y
@@ -101,7 +148,14 @@ class QuantizedModel:
         s, t = self.s, self.t
         feat = np.ascontiguousarray(O.feature8(src, self.stencil).transpose(0, 2, 3, 1))
         skip = f16(self._f16_layer(f16(_unshuffle(feat)), "project"))
-        if self.mode == "mixed":
+        if self.mode == "int8":
+            inv = lambda i: F32(1) / s[i]
+            low = int8_code(self._int8_layer(int8_code(_unshuffle(skip) * inv(1)), "compress") * inv(2))
+            for i in range(4):
+                low = int8_code(self._int8_layer(low, f"bottleneck{i}", groups=2) * inv(i + 3))
+            q7 = int8_code(self._int8_layer(low, "expand") * inv(7))
+            dec = f16(_fma(_shuffle(q7), s[7], skip))
+        elif self.mode == "mixed":
             q = e4m3(_unshuffle(skip) * (F32(1) / s[1]))
             low = e4m3(self._fp8_layer(q, "compress", s[1]) * (F32(1) / s[2]))
             for i in range(4):
@@ -112,9 +166,11 @@ class QuantizedModel:
             for i in range(4):
                 low = f16(self._f16_layer(low, f"bottleneck{i}", groups=2))
             up = self._f16_layer(low, "expand")
-        dec = f16(_shuffle(up) + skip)
+        if self.mode != "int8":
+            dec = f16(_shuffle(up) + skip)
         ref = f16(self._f16_layer(dec, "refine"))
-        meta = f16(self._f16_layer(ref, "tail", act=False, bias=f16(np.asarray(t["tail.bias"], F32))))
+        tail_bias = np.asarray(t["tail.bias"], F32)
+        meta = f16(self._f16_layer(ref, "tail", act=False, bias=tail_bias if self.mode == "int8" else f16(tail_bias)))
         return np.ascontiguousarray(meta.transpose(0, 3, 1, 2))
 
     def __call__(self, src):
