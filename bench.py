@@ -40,6 +40,9 @@ WORKLOADS = {
     "mixed1080": (1, 1080, 1920, 0, "mixed", "adaptive_fp8.bin", "area"),
     "tiled1080": (32, 1080, 1920, 256, "fp16", "aeisu_bicubic.pt", "bicubic"),
     "stream4k": (8, 2160, 3840, 0, "mixed", "adaptive_fp8.bin", "area"),
+    # the conventional-CUDA INT8/FP16 deployment's artifact (optimized/shader/weights)
+    "int8_720": (64, 720, 1280, 0, "int8", "aeisu_int8_fp16.pt", "area"),
+    "int8_1080": (1, 1080, 1920, 0, "int8", "aeisu_int8_fp16.pt", "area"),
     # one 7680x4320 input frame split into one row band per GPU (strong scaling)
     "band8k": (1, 4320, 7680, 0, "mixed", "adaptive_fp8.bin", "area"),
 }
@@ -179,7 +182,12 @@ def measured_peaks():
 
 
 def _oracle_model(ckpt):
+    """The reference's FP32 CPU path for a workload's checkpoint.  The INT8 artifact was exported
+    from aeisu_area.pt (its FP16 weights are that checkpoint's, rounded), and the reference's
+    CPU path has no INT8 arithmetic, so its baseline is that checkpoint in FP32."""
     from oracle import aeisu_np as O
+    if ckpt == "aeisu_int8_fp16.pt":
+        ckpt = "aeisu_area.pt"
     path = WEIGHTS / ckpt
     if path.suffix == ".pt":
         return O.load_folded(path)
@@ -206,14 +214,14 @@ def _cpu_threads():
 
 
 def measure_latency(dev, runs, distinct=16):
-    """p50/p99 device latency of one 1920x1080 -> 3840x2160 frame (FP16 route and mixed route),
+    """p50/p99 device latency of one 1920x1080 -> 3840x2160 frame (FP16, mixed and INT8 routes),
     input resident in HBM, cycling `distinct` seeded frames, CUDA events around each call."""
     import torch
     from aeisu_b200 import load_model
     frames = torch.from_numpy(gen_frames(50_000, distinct, 1080, 1920, "area")).to(dev)
     out = torch.empty((3840 * 2160 * 3,), dtype=torch.uint8, device=dev).view(2160, 3840, 3)
     res = {}
-    for precision, ckpt in (("fp16", "aeisu_area.pt"), ("mixed", "adaptive_fp8.bin")):
+    for precision, ckpt in (("fp16", "aeisu_area.pt"), ("mixed", "adaptive_fp8.bin"), ("int8", "aeisu_int8_fp16.pt")):
         model = load_model(WEIGHTS / ckpt, f"cuda:{dev.index}", precision)
         stream = torch.cuda.Stream(dev)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
@@ -587,7 +595,7 @@ def main():
             "value": value, "unit": "output Mpix/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong" if band else "weak",
-            "vs_baseline": None, "dtype": {"fp32": "f32", "fp16": "f16", "mixed": "e4m3+f16"}[precision],
+            "vs_baseline": None, "dtype": {"fp32": "f32", "fp16": "f16", "mixed": "e4m3+f16", "int8": "s8 codes as f16+f16"}[precision],
             "data": "synthetic (seeded procedural scenes, 2x2 area / bicubic degradation)",
             "config": {"workload": args.workload, "frames_per_step_per_gpu": n, "frame": f"{w}x{h}",
                        "output": f"{2 * w}x{2 * h}", "tile": tile, "precision": precision, "checkpoint": ckpt,
