@@ -9,7 +9,7 @@
 //                     phase weights are base + sum_k c_k basis[tap][k] (the reference's einsum
 //                     then base add), applied to the three channels (phase pairs as packed
 //                     f32x2 FMAs).
-//   k_recon_bwd       same tiles, the basis in shared memory.  Per pixel and tap, the filter gradient
+//   k_recon_bwd       same tiles, the basis in constant memory.  Per pixel and tap, the filter gradient
 //                     gw[p] = sum_c grad[c][p] src[c][tap]; the coefficient gradient
 //                     gc[k] = sum_{tap,p} gw[p] basis[tap][k][p], through the clamp's derivative
 //                     (1 where |v| <= 2, 0.05 on the soft ramp up to 2.5 inclusive, else 0) into
@@ -62,14 +62,15 @@ struct ReconJob {
     int slots;             // slot capacity per tile (0 when stride == 0)
 };
 
-// The forward's bank is the same for every thread, so it sits in constant memory, where an FFMA
-// reads it as a direct operand: no load instruction and no shared-memory wavefront per FMA (a
-// broadcast 16-byte shared load costs two wavefronts; with the bank in shared memory they bound
-// the forward).  Each call copies its base/basis here on its own stream, after the previous
-// forward has finished with them (see reconstruct_f32).  The backward keeps its basis in shared
-// memory: streamed from constant memory it measured slower (0.46 against 0.37 ms per training
-// step), its constant operands missing the per-SM constant cache.
+// The bank is the same for every thread, so it sits in constant memory, where a packed f32x2
+// FMA reads a pair of it as a direct operand: no load instruction and no shared-memory
+// wavefront per FMA (a broadcast 16-byte shared load costs two wavefronts; with the bank in
+// shared memory they bound both kernels).  Scalar FMAs on constant operands were slower still
+// in the backward (0.46 ms per training step against 0.37 from shared memory and 0.31 with
+// pairs): one issue slot per FMA.  Each call copies its base/basis here on its own stream,
+// after the previous call of its kind has finished with them (see reconstruct_f32).
 __constant__ float c_fwd_bank[kBank];   // base [25][4], then basis [25][16][4]
+__constant__ float c_bwd_basis[kBank - kBase];   // backward: basis [25][16][4]
 
 __device__ __forceinline__ float clamp_coef(float v) {
     // reconstruction.py:15-17 with the reference's own operations and comparisons
@@ -184,13 +185,11 @@ __device__ __forceinline__ void zero_border(const ReconJob& j) {
 }
 
 __global__ void __launch_bounds__(kRThreads, 2) k_recon_bwd(ReconJob j) {
-    __shared__ __align__(16) float s_bank[kBank - kBase];   // basis only
     __shared__ float s_win[3][kRWinY][kRWinX];
     __shared__ int s_wsel[kRThreads / 32];
     extern __shared__ __align__(16) float s_dyn[];
     float* s_gw = s_dyn;                                   // [slots][100]
     float* s_mc = s_dyn + size_t(j.slots) * kSlotW;        // [slots][20]
-    for (int i = threadIdx.x; i < kBank - kBase; i += kRThreads) s_bank[i] = __ldg(j.basis + i);
     if (j.off > 0) zero_border(j);
     const int tx = threadIdx.x % kRTX, ty = threadIdx.x / kRTX;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -234,28 +233,23 @@ __global__ void __launch_bounds__(kRThreads, 2) k_recon_bwd(ReconJob j) {
 #pragma unroll
             for (int k = 0; k < 16; ++k) gc[k] = make_float2(0.f, 0.f);
             float* gw_slot = slot >= 0 ? s_gw + size_t(slot) * kSlotW : nullptr;
-#pragma unroll 1
-            for (int ky = 0; ky < 5; ++ky) {
 #pragma unroll
-                for (int kx = 0; kx < 5; ++kx) {
-                    const int t = ky * 5 + kx;
-                    float2 w01 = make_float2(0.f, 0.f), w23 = w01;
+            for (int t = 0; t < 25; ++t) {   // every bank index is a compile-time constant
+                const int ky = t / 5, kx = t % 5;
+                float2 w01 = make_float2(0.f, 0.f), w23 = w01;
 #pragma unroll
-                    for (int c = 0; c < 3; ++c) {
-                        const float sv = s_win[c][ty + ky][tx + kx];
-                        w01 = __ffma2_rn(make_float2(sv, sv), g01[c], w01);
-                        w23 = __ffma2_rn(make_float2(sv, sv), g23[c], w23);
-                    }
-                    const float4* bk = reinterpret_cast<const float4*>(s_bank + t * 64);
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const float4 bv = bk[k];
-                        gc[k] = __ffma2_rn(w01, make_float2(bv.x, bv.y), gc[k]);
-                        gc[k] = __ffma2_rn(w23, make_float2(bv.z, bv.w), gc[k]);
-                    }
-                    if (gw_slot)
-                        reinterpret_cast<float4*>(gw_slot)[t] = make_float4(w01.x, w01.y, w23.x, w23.y);
+                for (int c = 0; c < 3; ++c) {
+                    const float sv = s_win[c][ty + ky][tx + kx];
+                    w01 = __ffma2_rn(make_float2(sv, sv), g01[c], w01);
+                    w23 = __ffma2_rn(make_float2(sv, sv), g23[c], w23);
                 }
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float* bk = c_bwd_basis + (t * 16 + k) * 4;
+                    gc[k] = __ffma2_rn(w01, make_float2(bk[0], bk[1]), gc[k]);
+                    gc[k] = __ffma2_rn(w23, make_float2(bk[2], bk[3]), gc[k]);
+                }
+                if (gw_slot) reinterpret_cast<float4*>(gw_slot)[t] = make_float4(w01.x, w01.y, w23.x, w23.y);
             }
             // the raw coefficients are needed only now (the clamp's derivative and the slot)
             float v[16];
@@ -360,10 +354,10 @@ struct DeviceState {
     long long fwd_ctas = 0;                 // resident k_recon_fwd CTAs
     std::map<size_t, long long> bwd_ctas;   // resident k_recon_bwd CTAs per dynamic smem size
     cudaMemPool_t pool = nullptr;           // backward partials; keeps its memory between calls
-    // One constant bank per device: a forward's copy waits (on its own stream) for the previous
-    // forward's kernel to be done with it, and forwards are enqueued one at a time.
+    // One constant bank of each kind per device: a call's copy waits (on its own stream) for the
+    // previous call of its kind to be done with it, and calls are enqueued one at a time.
     std::mutex bank_mu;
-    cudaEvent_t fwd_done = nullptr;
+    cudaEvent_t fwd_done = nullptr, bwd_done = nullptr;
 };
 
 std::mutex g_state_mu;
@@ -388,6 +382,7 @@ DeviceState& state_of(int device) {
         uint64_t keep = UINT64_MAX;
         AEISU_CUDA(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
         AEISU_CUDA(cudaEventCreateWithFlags(&d.fwd_done, cudaEventDisableTiming));
+        AEISU_CUDA(cudaEventCreateWithFlags(&d.bwd_done, cudaEventDisableTiming));
         d.fwd_ctas = (long long)std::max(per_sm, 1) * sms;
         d.sms = sms;
     }
@@ -449,8 +444,19 @@ void reconstruct_backward_f32(const float* src, const float* meta, const float* 
         AEISU_CUDA(cudaMallocFromPoolAsync(&ws, size_t(grid) * kGrad * sizeof(float), ds.pool, stream));
         j.partial = static_cast<float*>(ws);
     }
-    k_recon_bwd<<<unsigned(grid), kRThreads, dyn, stream>>>(j);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = cudaSuccess;
+    {
+        std::lock_guard<std::mutex> lock(ds.bank_mu);
+        e = cudaStreamWaitEvent(stream, ds.bwd_done, 0);   // the previous backward has read the basis
+        if (e == cudaSuccess)
+            e = cudaMemcpyToSymbolAsync(c_bwd_basis, basis, (kBank - kBase) * sizeof(float), 0,
+                                        cudaMemcpyDeviceToDevice, stream);
+        if (e == cudaSuccess) {
+            k_recon_bwd<<<unsigned(grid), kRThreads, dyn, stream>>>(j);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(ds.bwd_done, stream);
+    }
     if (e == cudaSuccess && stride > 0) {
         k_recon_reduce<<<(kGrad + 31) / 32, 32 * kRedWarps, 0, stream>>>(j.partial, int(grid), gbase, gbasis);
         e = cudaGetLastError();
