@@ -1234,9 +1234,11 @@ void launch(bool pdl, void (*kernel)(KArgs...), unsigned grid, unsigned block, i
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = size_t(smem);
     cfg.stream = s;
+    // programmatic serialisation only on created streams, not on the legacy default stream
+    const bool legacy = s == nullptr || s == cudaStreamLegacy;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    attr[0].val.programmaticStreamSerializationAllowed = (pdl && !legacy) ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     AEISU_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));

@@ -41,6 +41,7 @@ FOLDED_KEYS = (
       for item in ((f"{name}.weight", (cout, cin, k, k)), (f"{name}.bias", (cout,)))),
 )
 SPYR8_MAGIC = b"SPYR8F8\0"
+CUDA_STREAM_LEGACY = 0x1   # cudaStreamLegacy of cuda_runtime_api.h
 # optimized/shader/runtime.py:34, 41-43: the one published INT8/FP16 policy
 INT8_LAYERS = ("compress", "bottleneck0", "bottleneck1", "bottleneck2", "bottleneck3", "expand")
 INT8_POLICY = {"project": "fp16", **{name: "int8" for name in INT8_LAYERS}, "refine": "fp16", "tail": "fp16"}
@@ -140,7 +141,10 @@ class _Array:
                 self.keep = value.to(want).contiguous()
                 self.ptr = self.keep.data_ptr()
                 self.device = True
-                self.stream = torch.cuda.current_stream(value.device).cuda_stream
+                # torch's default stream reports handle 0, which the C ABI reads as "the model's
+                # own stream" (non-blocking: unordered with the caller's work); name the legacy
+                # default stream explicitly instead (cudaStreamLegacy)
+                self.stream = torch.cuda.current_stream(value.device).cuda_stream or CUDA_STREAM_LEGACY
                 return
             self.keep = value.detach().to(want).contiguous().numpy()
         else:

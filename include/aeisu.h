@@ -68,7 +68,9 @@ typedef enum aeisu_precision {
 #define AEISU_IO_HOST   0u   /* src/dst are host pointers (pinned for full PCIe speed); the
                                 call copies, runs and waits (bounded by the handle timeout) */
 #define AEISU_IO_DEVICE 1u   /* src/dst are device pointers on the handle's GPU; the call only
-                                enqueues on `stream` (or the handle's stream when NULL)      */
+                                enqueues on `stream` (or the handle's stream when NULL, which
+                                is not ordered with the legacy default stream: pass
+                                cudaStreamLegacy to run after work queued there)              */
 
 /* Number of float values in a folded checkpoint (aeisu/model.py:554-583, 34 tensors,
  * tests/test_reference.py:69). */
