@@ -63,6 +63,25 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
+def rank_seed(rank):
+    """Frame seed of a rank: every rank upscales its own distinct frames (frame-parallel)."""
+    return 10_000 * (rank + 1)
+
+
+def output_pixels(h, w, frames_per_rank, world, band):
+    """2x output pixels one step produces over the whole job: frame-parallel ranks each upscale
+    their own batch; row-band ranks share one frame (each writes its own rows)."""
+    return 4 * h * w * frames_per_rank * (1 if band else world)
+
+
+def max_over_ranks(x, dist, device):
+    """The slowest rank's value: multi-GPU times are the maximum over ranks."""
+    import torch
+    t = torch.tensor([float(x)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def gen_frames(seed, count, h, w, degradation):
     """Distinct seeded frames, rendered in a spawn pool (before any CUDA use)."""
     from aeisu_b200.synthetic import make_frame
@@ -467,7 +486,7 @@ def main():
     rank, local_rank, world = dist_env()
 
     # host-side frame generation happens before any CUDA call (spawn pool)
-    frames = gen_frames(10_000 * (rank + 1), n, h, w, deg)
+    frames = gen_frames(rank_seed(rank), n, h, w, deg)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(frames, ckpt, tile, args.cpu_seconds)
@@ -524,11 +543,9 @@ def main():
     launches = model.kernel_launches - launches0
     ms = start.elapsed_time(end)
     if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = max_over_ranks(ms, dist, dev)
     ms_per_step = ms / args.steps
-    out_mpix = 4 * h * w * n * (1 if band else world)
+    out_mpix = output_pixels(h, w, n, world, band)
     value = out_mpix / (ms_per_step / 1e3) / 1e6
 
     # detailed per-stage pass over the timed steps for the roofline (separate, same stream)
@@ -560,9 +577,7 @@ def main():
         upscale(host_src, host_out)
     e2e_dt = time.perf_counter() - t0
     if world > 1:
-        t = torch.tensor([e2e_dt], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_dt = float(t.item())
+        e2e_dt = max_over_ranks(e2e_dt, dist, dev)
     e2e_value = out_mpix * e2e_steps / e2e_dt / 1e6
 
     # roofline of the dominant stage
