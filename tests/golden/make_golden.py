@@ -1,6 +1,7 @@
 """Generate the golden parity fixtures from the reference PyTorch implementation.
 
-Run in a container that has a reference checkout (default ``/root/reference``):
+Run where a checkout of the reference is available (its path via ``--reference``, or the
+``AEISU_REFERENCE`` environment variable):
 
     python tests/golden/make_golden.py [--reference PATH]
 
@@ -18,6 +19,7 @@ beside each output so a test can confirm it runs the same checkpoint.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import sys
 from pathlib import Path
@@ -36,7 +38,7 @@ def sha256(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("AEISU_REFERENCE", "/root/reference"))
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch

@@ -1,6 +1,7 @@
 """Generate tests/golden/metrics_distortion.npz from the reference's own metric function.
 
-Run in a container that has a reference checkout (default ``/root/reference``):
+Run where a checkout of the reference is available (its path via ``--reference``, or the
+``AEISU_REFERENCE`` environment variable):
 
     python tests/golden/make_metrics_golden.py [--reference PATH]
 
@@ -13,6 +14,7 @@ smallest size the crop allows.  The fixture is committed; tests never need the r
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -46,7 +48,7 @@ def pair(seed, h, w, noise):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("AEISU_REFERENCE", "/root/reference"))
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch

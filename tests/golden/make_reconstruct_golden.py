@@ -1,6 +1,7 @@
 """Generate the reconstruction forward/backward fixtures from the reference PyTorch code.
 
-Run in a container that has a reference checkout (default ``/root/reference``):
+Run where a checkout of the reference is available (its path via ``--reference``, or the
+``AEISU_REFERENCE`` environment variable):
 
     python tests/golden/make_reconstruct_golden.py [--reference PATH]
 
@@ -14,6 +15,7 @@ The fixture is committed; tests never need the reference at run time.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -48,7 +50,7 @@ def inputs(b, h, w, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("AEISU_REFERENCE", "/root/reference"))
     ap.add_argument("--out", default=str(HERE / "reconstruct_grad.npz"))
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
