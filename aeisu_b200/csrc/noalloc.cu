@@ -12,16 +12,21 @@
 //
 // Limits and sharing:
 //  * The array holds kNoAllocScratchBytes (64 MiB) on every GPU that loads this library, for
-//    the life of the process.  Frames whose padded grid needs more scratch than that (about
-//    0.8 megapixel of padded input for the mixed route, e.g. 960x540) are rejected with
-//    AEISU_ERR_INVALID_ARG; batches are split into as many launches as needed.
+//    the life of the process.  A frame needs about 80 bytes of scratch per padded input pixel
+//    on the mixed route, 96 on FP16 and INT8 and 224 on FP32 (the sums of the buffer sizes in
+//    upscale_u8_noalloc), so frames above about 0.83, 0.69 and 0.29 Mpixel of padded input are
+//    rejected with AEISU_ERR_INVALID_ARG (960x540 fits the tensor-core routes, 640x360 FP32).
+//    Batches run in as many passes of whole frames as the array needs.
 //  * The array is shared by every call on a device and keeps the last call's contents.
 //    Nothing in it has to start at zero (every byte a kernel reads was written earlier in the
 //    same call), but two calls whose GPU work overlaps in time -- on different streams, or
 //    from different handles on one device -- race on it.  Serialise them.
 //  * The first call on each device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current); make that first call before capturing
-//    a CUDA graph on the stream.
+//    cudaGetSymbolAddress (with that device current), and the first launch of each kernel on
+//    a device may set its shared-memory attribute and add an entry to the host-side cache of
+//    those attributes; make that first call before capturing a CUDA graph on the stream.  No
+//    device memory is ever allocated.  The address is cached for the life of the process:
+//    after cudaDeviceReset it is stale, so the library must not outlive a reset of the device.
 #include <cuda_runtime.h>
 
 #include <mutex>
