@@ -2,7 +2,8 @@
 
 Reference surface mirrored (paths relative to the AELabs42/AEISU checkout):
 
-* ``load_model(path, device)``  -> aeisu/runtime.py:45-56 (folded ``.pt``); also SPYR8 ``.bin``
+* ``load_model(path, device)``  -> aeisu/runtime.py:45-56 (folded ``.pt`` and training
+  checkpoints, folded on load by ``aeisu_b200.fold``); also SPYR8 ``.bin``
   and the INT8/FP16 ``shader_precision_v1`` ``.pt`` (optimized/shader/runtime.py:37-59)
 * ``upscale(model, source, tile=128)`` -> aeisu/runtime.py:70-103 (same padding, tiling,
   ValueError / FloatingPointError behaviour, clamped CHW float32 result)
@@ -22,7 +23,7 @@ from pathlib import Path
 
 import numpy as np
 
-from . import _lib
+from . import _lib, fold
 
 # FoldedAEISU.state_dict() order and shapes (aeisu/model.py:554-583).
 _CONVS = (
@@ -174,12 +175,14 @@ class Model:
         return cls(h, dev, precision, basis_l1_scale)
 
     @classmethod
-    def from_spyr8_bytes(cls, data: bytes, device="cuda", precision="mixed"):
+    def from_spyr8_bytes(cls, data: bytes, device="cuda", precision="mixed", activation_headroom=1.0):
+        """A SPYR8 artifact image.  activation_headroom (a power of two, mixed route only)
+        multiplies the artifact's FP8 activation scales; 1 runs its own quantisation points."""
         dev = _device_index(device)
         buf = C.create_string_buffer(data, len(data))
         h = C.c_void_p()
-        _lib.check(_lib.lib().aeisu_open_spyr8_memory(buf, len(data), _lib.PRECISIONS[precision], dev,
-                                                      C.byref(h)))
+        _lib.check(_lib.lib().aeisu_open_spyr8_headroom(buf, len(data), _lib.PRECISIONS[precision], dev,
+                                                        float(activation_headroom), C.byref(h)))
         return cls(h, dev, precision)
 
     @classmethod
@@ -362,16 +365,18 @@ class Model:
         return self._wrap(a, out)
 
 
-def load_model(path, device="cuda", precision=None) -> Model:
+def load_model(path, device="cuda", precision=None, activation_headroom=1.0) -> Model:
     """runtime.load_model (aeisu/runtime.py:45-56) for folded ``.pt`` checkpoints, plus
     SPYR8 ``.bin`` artifacts and the INT8/FP16 ``shader_precision_v1`` ``.pt``
     (optimized/shader/runtime.py:37-59).  precision defaults to fp32 for a folded ``.pt``,
-    mixed for SPYR8 and int8 (its only precision) for the INT8 artifact."""
+    mixed for SPYR8 and int8 (its only precision) for the INT8 artifact.  activation_headroom:
+    the power of two the mixed route multiplies a SPYR8 artifact's activation scales by (1, the
+    default, runs the artifact's own quantisation points)."""
     path = Path(path)
     with path.open("rb") as f:
         head = f.read(8)
     if head == SPYR8_MAGIC:
-        return Model.from_spyr8_bytes(path.read_bytes(), device, precision or "mixed")
+        return Model.from_spyr8_bytes(path.read_bytes(), device, precision or "mixed", activation_headroom)
     import torch  # checkpoint container only
     payload = torch.load(path, map_location="cpu", weights_only=True)
     if isinstance(payload, dict) and payload.get("format") == "shader_precision_v1":
@@ -381,8 +386,10 @@ def load_model(path, device="cuda", precision=None) -> Model:
     state = _checkpoint_state(payload)
     scale = payload.get("basis_l1_scale", payload.get("config", {}).get("basis_l1_scale", 0.5)) \
         if isinstance(payload, dict) else 0.5
-    if any(".rep_low_u" in key for key in state):
-        raise ValueError("training checkpoints must be folded first (export.py) before loading")
+    if fold.is_training_state(state):
+        # a train.py checkpoint: fold its training-only branches as load_model does
+        # (aeisu/runtime.py:49-52, fold_model of aeisu/model.py:599-602)
+        state = fold.fold_training_state(state)
     return Model.from_folded_state(state, device, precision or "fp32", scale)
 
 

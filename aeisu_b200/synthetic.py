@@ -210,3 +210,18 @@ def random_folded_state(seed, coeff_gain=1.0):
         st[f"{name}.weight"] = rng.normal(0, std, (cout, cin, k, k)).astype(F32)
         st[f"{name}.bias"] = rng.normal(0, 0.05, cout).astype(F32)
     return st
+
+
+def seeded_training_state(folded, seed, std=0.01):
+    """A training checkpoint state (the AEISU layout, aeisu/model.py:37-168) whose main tensors
+    are the given folded ones and whose training-only coordinates (low-rank, structural,
+    template and mixed-bank branches, analysis gains) are N(0, std) draws from a seeded
+    generator, in state_dict order; folding it changes every deployed tensor."""
+    from .fold import training_shapes
+    rng = np.random.default_rng(seed)
+    out = {}
+    for key, shape in training_shapes().items():
+        out[key] = (np.array(folded[key], F32) if key in folded
+                    else rng.normal(0, std, shape).astype(F32))
+    return out
+

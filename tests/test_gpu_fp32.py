@@ -161,3 +161,23 @@ def test_full_1080p_frame_against_oracle():
         assert_u8_close(model.upscale_u8(frame, 0), O.chw_to_u8(ref))
     finally:
         model.close()
+
+
+def test_training_checkpoint_loads_folded(tmp_path):
+    """load_model of a train.py-style checkpoint (training coordinates not folded) folds it as the
+    reference's load_model does (aeisu/runtime.py:49-52) and matches the reference's upscale of
+    it (tests/golden/training_checkpoint.npz) within the FP32 bar."""
+    import torch
+    from aeisu_b200.synthetic import seeded_training_state
+    d = np.load(GOLDEN / "training_checkpoint.npz")
+    state = seeded_training_state(random_folded_state(int(d["weight_seed"])), int(d["branch_seed"]),
+                                  float(d["branch_std"]))
+    path = tmp_path / "training.pt"
+    torch.save({"model": {k: torch.from_numpy(v) for k, v in state.items()}, "basis_l1_scale": 0.5}, path)
+    model = load_model(path, "cuda:0")
+    try:
+        got = upscale(model, O.u8_to_chw(d["frame"]), 0)
+        np.testing.assert_allclose(got, d["upscale_f32"], atol=ATOL, rtol=0)
+        assert_u8_close(model.upscale_u8(d["frame"], 0), O.chw_to_u8(d["upscale_f32"]))
+    finally:
+        model.close()
