@@ -51,6 +51,8 @@ _SIGNATURES = {
     "aeisu_open_spyr8": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
     "aeisu_validate_spyr8": (C.c_int, [C.c_void_p, C.c_size_t, C.c_char_p]),
     "aeisu_open_spyr8_memory": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "aeisu_open_spyr8_headroom": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_float,
+                                            C.POINTER(C.c_void_p)]),
     "aeisu_open_folded": (C.c_int, [C.c_void_p, C.c_size_t, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
     "aeisu_close": (None, [C.c_void_p]),
     "aeisu_upscale_u8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
@@ -78,6 +80,7 @@ _SIGNATURES = {
                                                  C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "aeisu_synchronize": (C.c_int, [C.c_void_p, C.c_void_p, C.c_double]),
+    "aeisu_tensor_peak": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
     "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "aeisu_set_timeout": (C.c_int, [C.c_void_p, C.c_double]),

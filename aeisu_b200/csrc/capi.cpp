@@ -1,5 +1,6 @@
 // extern "C" boundary (include/aeisu.h).  Every entry point converts internal failures
 // into status codes and records the message for aeisu_last_error().
+#include <cmath>
 #include <cstring>
 #include <fstream>
 #include <iterator>
@@ -75,6 +76,19 @@ int aeisu_validate_spyr8(const void* data, size_t bytes, char* checksum_hex) {
 int aeisu_open_spyr8_memory(const void* data, size_t bytes, int precision, int device, aeisu_t** out) {
     return guarded([&] {
         aeisu::HostModel m = aeisu::load_spyr8(static_cast<const uint8_t*>(data), bytes);
+        open_model(std::move(m), precision, device, out);
+    });
+}
+
+int aeisu_open_spyr8_headroom(const void* data, size_t bytes, int precision, int device,
+                              float activation_headroom, aeisu_t** out) {
+    return guarded([&] {
+        const float h = activation_headroom;
+        int e = 0;
+        aeisu::require(h >= 1.f && h <= 64.f && std::frexp(h, &e) == 0.5f,
+                       "activation headroom must be a power of two in [1, 64]");
+        aeisu::HostModel m = aeisu::load_spyr8(static_cast<const uint8_t*>(data), bytes);
+        m.fp8_headroom = h;
         open_model(std::move(m), precision, device, out);
     });
 }
@@ -221,6 +235,13 @@ int aeisu_reconstruct_backward_f32(const float* source, const float* metadata, c
         aeisu::reconstruct_backward_f32(source, metadata, basis, grad_out, n, h, w, trim, gradient_stride, phase,
                                         device, grad_metadata, grad_base, grad_basis,
                                         static_cast<cudaStream_t>(stream));
+    });
+}
+
+int aeisu_tensor_peak(int device, int kind, int ctas_per_sm, int mmas_per_cta, int repeats, double* tflops) {
+    return guarded([&] {
+        aeisu::require(tflops != nullptr, "tflops pointer is null");
+        *tflops = aeisu::tensor_peak_tflops(device, kind, ctas_per_sm, mmas_per_cta, repeats);
     });
 }
 

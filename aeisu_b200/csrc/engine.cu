@@ -188,7 +188,7 @@ Engine::Engine(HostModel model, int precision, int device)
     else if (precision_ == AEISU_PRECISION_FP16) os << "; route tcgen05 f16 controller + tcgen05 head";
     else if (precision_ == AEISU_PRECISION_INT8)
         os << "; route tcgen05 int8-code/f16 controller (codes as f16, exact integer sums) + tcgen05 head";
-    else os << "; route tcgen05 e4m3/f16 mixed controller + tcgen05 head";
+    else os << "; route tcgen05 e4m3/f16 mixed controller + tcgen05 head; activation headroom x" << model_.fp8_headroom;
     report_ = os.str();
 }
 

@@ -40,6 +40,9 @@ struct HostModel {
     float basis[25 * 16 * 4];  // [tap][k][phase]  projected (reconstruction.py:8-12)
     LayerWeights layers[kLayerCount];
     float act_scales[10] = {};  // SPYR8 activation scales (Appendix of the artifact contract)
+    // Power-of-two factor the mixed route applies to act_scales (1 = the artifact's own
+    // quantisation points, as the reference's mixed route runs them)
+    float fp8_headroom = 1.0f;
     bool has_fp8 = false;
     bool has_int8 = false;      // INT8 artifact: compress/core/expand as int8 codes and factors
     std::string format;         // "folded", "spyr8" or "shader_int8"

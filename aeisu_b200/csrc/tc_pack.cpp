@@ -29,15 +29,16 @@ TcHostPack pack_tc(const HostModel& m, int route) {
             AEISU_ERR_UNSUPPORTED);
     require(i8 == m.has_int8, "the INT8 route needs, and only runs, the INT8 artifact", AEISU_ERR_UNSUPPORTED);
     TcHostPack P;
-    // Activation scales of the artifact times a power-of-two headroom.  E4M3 is a floating
-    // point format, so the factor leaves the rounding of every value below the old limit
-    // bit-identical and only stops values in [448 s, 448 hs) from saturating (the artifact was
-    // calibrated on natural images; high-contrast content exceeds its range in the later
-    // bottleneck layers).
+    // Activation scales of the artifact times the model's power-of-two headroom (1 unless the
+    // caller asked for more at load time: then the artifact's own quantisation points).  E4M3
+    // is a floating point format, so a factor h leaves the rounding of every value below the
+    // old limit bit-identical and only stops values in [448 s, 448 h s) from saturating (the
+    // artifact was calibrated on natural images; high-contrast content exceeds its range in
+    // the later bottleneck layers).
     // The INT8 route uses the artifact's scales as they are: int8 codes saturate at +-127 there
     // exactly as in the reference's kernels.
     float s[10];
-    for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * (i8 ? 1.0f : kFp8ActivationHeadroom);
+    for (int i = 0; i < 10; ++i) s[i] = m.act_scales[i] * (i8 ? 1.0f : m.fp8_headroom);
     // one LeakyReLU slope for every activated layer (the tail is linear), in [0, 1] so that the
     // kernels may evaluate it as max(v, slope * v)
     P.slope = m.layers[kProject].slope[0];

@@ -11,9 +11,6 @@
 
 namespace aeisu {
 
-// Power-of-two factor applied to the SPYR8 activation scales by the mixed route.
-constexpr float kFp8ActivationHeadroom = 2.0f;
-
 struct TcHostLayer {
     size_t image = 0;                  // byte offset of the B operand image
     size_t scale = 0, bias = 0;        // float offsets of the epilogue vectors

@@ -50,9 +50,12 @@ def inputs(b, h, w, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("AEISU_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("AEISU_REFERENCE"),
+                    help="checkout of the reference (default: $AEISU_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "reconstruct_grad.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference or AEISU_REFERENCE")
     sys.path.insert(0, args.reference)
     import torch
     from aeisu.reconstruction import reconstruct

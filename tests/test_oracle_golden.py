@@ -118,3 +118,24 @@ def test_trained_checkpoint_fixtures(name):
     u8 = O.chw_to_u8(out)
     diff = np.abs(u8.astype(int) - d["upscale_u8"].astype(int))
     assert diff.max() <= 1 and (diff > 0).mean() <= 1e-4
+
+
+def test_tile256_seams_at_full_size():
+    """Config 4 of the benchmark set at its own size: aeisu_bicubic.pt on a 1920x1080 bicubic
+    frame through the reference's tiled path (tile 256, 32-LR halos, aeisu/runtime.py:89-99).
+    The oracle must reproduce the reference's float output on every row and column beside a tile
+    seam and its uint8 output row by row."""
+    import hashlib
+    from aeisu_b200.synthetic import make_frame
+    d = np.load(GOLDEN / "aeisu_bicubic_f400_1080x1920_t256.npz")
+    path = staged(str(d["checkpoint"]))
+    assert hashlib.sha256(path.read_bytes()).hexdigest() == str(d["checkpoint_sha256"])
+    h, w, tile = int(d["h"]), int(d["w"]), int(d["tile"])
+    frame = make_frame(int(d["seed"]), h, w, str(d["degradation"]))
+    assert hashlib.sha256(frame.tobytes()).hexdigest() == str(d["frame_sha256"])
+    out = O.upscale(O.load_folded(path), O.u8_to_chw(frame), tile)
+    assert len(d["seam_rows"]) == 4 and len(d["seam_cols"]) == 7
+    np.testing.assert_allclose(out[:, d["row_index"], :], d["rows_f32"], atol=2e-6, rtol=0)
+    np.testing.assert_allclose(out[:, :, d["col_index"]], d["cols_f32"], atol=2e-6, rtol=0)
+    sums = O.chw_to_u8(out).astype(np.int64).sum(axis=(1, 2))
+    assert np.abs(sums - d["u8_row_sums"]).max() <= 4
