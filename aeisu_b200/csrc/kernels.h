@@ -115,6 +115,10 @@ int metric_launches_per_call(int crop);
 
 // PNG files of n frames (k_png.cu): kind 0 uint8 HWC, kind 1 float32 CHW quantised as save_rgb.
 uint64_t png_bound(int h, int w);
+
+// Dense tcgen05 throughput (TFLOP/s, best of `repeats` timed launches) of M = 128, N = 256 MMAs
+// of kind 0 (f16, K = 16) or 1 (e4m3, K = 32) on `device` (k_peak.cu).
+double tensor_peak_tflops(int device, int kind, int ctas_per_sm, int mmas, int repeats);
 void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, int device, uint8_t* out,
                 uint64_t capacity, uint64_t* sizes, cudaStream_t stream);
 int png_launches_per_call();

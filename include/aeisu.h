@@ -90,6 +90,17 @@ int aeisu_validate_spyr8(const void* data, size_t bytes, char* checksum_hex);
 int aeisu_open_spyr8_memory(const void* data, size_t bytes, int precision, int device,
                             aeisu_t** out);
 
+/* aeisu_open_spyr8_memory with the mixed route's FP8 activation scales multiplied by
+ * `activation_headroom`, a power of two in [1, 64] (1 gives exactly aeisu_open_spyr8_memory:
+ * the artifact's own scales, as the reference applies them, SrcPyrCudaRuntime.cu:4427-4451,
+ * 4587-4601).  E4M3 is a floating-point format, so a power-of-two factor h leaves the rounding
+ * of every activation below the artifact's saturation limit unchanged and only keeps values in
+ * [448 s, 448 h s) from saturating: content beyond the artifact's calibration range (the
+ * reference calibrated on natural images) then keeps its magnitude, at the cost of h times
+ * coarser rounding of values below 2^-6 s.  Only the mixed route reads it. */
+int aeisu_open_spyr8_headroom(const void* data, size_t bytes, int precision, int device,
+                              float activation_headroom, aeisu_t** out);
+
 /* Open a model from folded FP32 weights: the 34 tensors of FoldedAEISU.state_dict()
  * concatenated in that order (AEISU_FOLDED_VALUES floats), plus basis_l1_scale.
  * Replaces load_model(path) for folded .pt checkpoints (aeisu/runtime.py:45-56);
@@ -155,12 +166,19 @@ int aeisu_upscale_u8_band(aeisu_t* handle, const uint8_t* src, int h, int w, int
  * a caller that owns every buffer): all intermediate tensors live in one static device array
  * of 64 MiB that every GPU loading the library holds until exit.  src/dst are device
  * pointers (n frames of h x w x 3 uint8 in, 2h x 2w x 3 out); work is enqueued on `stream`
- * (NULL: the handle's stream) and the call returns without waiting.  Frames needing more
- * scratch than the array holds (about 0.8 Mpixel of padded input for the mixed route) are
- * rejected with AEISU_ERR_INVALID_ARG.  The array is shared and keeps the previous call's
- * contents: calls whose GPU work overlaps in time race and must be serialised.  The first
- * call on a device looks up the array's address; make it before any stream capture.
- * Non-finite outputs are reported by aeisu_synchronize. */
+ * (NULL: the handle's stream) and the call returns without waiting.  The scratch a frame
+ * needs is about 80 bytes per padded input pixel on the mixed route, 96 on FP16 and INT8 and
+ * 224 on FP32, so the largest frames are about 0.83, 0.69 and 0.29 Mpixel of padded input
+ * (the padded grid rounds h and w up to a multiple of 32 and adds 32): 960x540 fits the
+ * mixed, FP16 and INT8 routes, 640x360 the FP32 route.  Larger frames are rejected with
+ * AEISU_ERR_INVALID_ARG; batches run in as many passes of whole frames as the array needs.
+ * The array is shared and keeps the previous call's contents: calls whose GPU work overlaps
+ * in time race and must be serialised.  The first call on a device looks up the array's
+ * address, and the first call on a device and shape may set kernel attributes and add an
+ * entry to a small host-side cache of them; make that first call before any stream capture.
+ * The cached address is not refreshed after cudaDeviceReset: a handle and this entry point
+ * must not outlive a reset of their device.  Non-finite outputs are reported by
+ * aeisu_synchronize. */
 int aeisu_upscale_u8_noalloc(aeisu_t* handle, const uint8_t* src, int n, int h, int w,
                              uint8_t* dst, void* stream);
 
@@ -259,6 +277,16 @@ int aeisu_reconstruct_backward_f32(const float* source, const float* metadata, c
                                    const float* grad_out, int n, int h, int w, int trim, int gradient_stride,
                                    int phase, int device, float* grad_metadata, float* grad_base,
                                    float* grad_basis, void* stream);
+
+/* Measurement helper with no counterpart in the reference: the dense tensor-core throughput of
+ * GPU `device` for the instructions the controller kernels issue, as the roofline denominator
+ * of their stages.  kind 0: tcgen05.mma kind::f16 (f16 operands, K = 16); kind 1: kind::f8f6f4
+ * with E4M3 operands (K = 32).  Each of ctas_per_sm (1 or 2) CTAs per SM issues mmas_per_cta
+ * back-to-back M = 128, N = 256 MMAs from one thread into one TMEM accumulator; *tflops
+ * receives 2 * 128 * 256 * K * MMAs / time, the best of `repeats` launches timed with CUDA
+ * events (one untimed launch first).  Waits for completion; allocates 4 bytes of device
+ * memory for the kernel's error flag. */
+int aeisu_tensor_peak(int device, int kind, int ctas_per_sm, int mmas_per_cta, int repeats, double* tflops);
 
 /* Wait for all work enqueued on the handle's stream (or `stream`) for at most
  * timeout_ms; AEISU_ERR_TIMEOUT if it has not finished, AEISU_ERR_NONFINITE if a
