@@ -8,8 +8,8 @@
 // columns and has one thread issue `mmas` back-to-back M = 128, N = 256 MMAs into the same
 // accumulator, then one commit and a bounded wait.  N = 256 is the shape whose operands the
 // tensor core reads from shared memory at full rate; two CTAs per SM keep the pipe fed while
-// one of them is in its prologue or epilogue.  Operand values are zeros: they do not change
-// the instruction's timing.
+// one of them is in its prologue or epilogue.  Operands hold a hashed bit pattern of finite
+// values, so that the datapath toggles as it does on real data.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -33,10 +33,15 @@ __global__ void __launch_bounds__(128) k_mma_peak(int mmas, int* err) {
     __shared__ __align__(128) uint8_t s_b[kPeakBBytes];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
-    for (int i = threadIdx.x; i < (kPeakABytes + kPeakBBytes) / 16; i += blockDim.x) {
-        uint4* p = i < kPeakABytes / 16 ? reinterpret_cast<uint4*>(s_a) + i
-                                          : reinterpret_cast<uint4*>(s_b) + (i - kPeakABytes / 16);
-        *p = make_uint4(0, 0, 0, 0);
+    // operands: a fixed hashed bit pattern, masked so that every element is finite (f16
+    // exponent field below 31; e4m3 codes without the all-ones NaN pattern)
+    const uint32_t mask = FP8 ? 0x77777777u : 0x3BFF3BFFu;
+    for (int i = threadIdx.x; i < (kPeakABytes + kPeakBBytes) / 4; i += blockDim.x) {
+        uint32_t h = (uint32_t(i) + 0x9E3779B9u * (blockIdx.x + 1)) * 0x85EBCA6Bu;
+        h ^= h >> 13;
+        uint32_t* p = i < kPeakABytes / 4 ? reinterpret_cast<uint32_t*>(s_a) + i
+                                            : reinterpret_cast<uint32_t*>(s_b) + (i - kPeakABytes / 4);
+        *p = h & mask;
     }
     fence_async_smem();
     cta_setup(&s_tmem, &s_bar, 1, kPeakN);

@@ -11,9 +11,15 @@ CUDA events with barriers, max over ranks.  Prints one JSON line on rank 0.
 
 `value` times the device-resident path (inputs already in HBM; inputs+outputs are larger
 than L2, so no flush is needed).  `e2e` times the same batch through the public C ABI with
-pinned host buffers: host->device copy, compute, device->host copy inside the region.
-`--impl reference` times the reference algorithm's CPU implementation (the numpy port in
-oracle/, FP32) on the host cores with the same metric.
+pinned host buffers (allocated on the GPU's NUMA node): host->device copy, compute,
+device->host copy inside the region, beside the host link's ceiling for the same bytes.
+`roofline` holds the dominant stage against its bound and `roofline.step` the whole step
+against the north-star roofline, max(controller FLOPs at tensor peak, head bytes at HBM
+bandwidth), with the E4M3 rate measured in the run by a tcgen05 probe.  The default workload
+also records configuration 5 at this N (`stream4k`, `band8k`) and the 1080p latency over 1000
+distinct frames, device-resident and end to end.  `--impl reference` times the reference
+algorithm's CPU implementation (the numpy port in oracle/, FP32) on the host cores with the
+same metric.
 """
 from __future__ import annotations
 
@@ -50,9 +56,14 @@ BAND_WORKLOADS = {"band8k"}
 # controller FLOPs per padded LR pixel (paper MAC table: 11,520 MAC) and head bytes per LR pixel
 CONTROLLER_FLOP_PER_PX = 2 * 11520
 HEAD_BYTES_PER_PX = 3 + 32 + 12
-# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of the
-# workload (profiles/k_tc_head_mixed720_traffic.md); reported as roofline.traffic
-RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.688e9)}
+# controller MACs per padded LR pixel by arithmetic on the mixed route: f16 project 256 +
+# refine 4,608 + head 1,024; e4m3 compress 512 + bottlenecks 4,608 + expand 512
+MIXED_F16_MACS, MIXED_E4M3_MACS = 5888, 5632
+# DRAM bytes (read + write) of one launch of the dominant kernel on the default workload, from
+# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); reported as roofline.traffic
+# with its source, since a run cannot read DRAM counters itself
+RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.688e9,
+                                 "ncu capture of one k_tc_head launch, 64 x 1280x720 mixed")}
 
 
 def padded(h, w):
@@ -200,6 +211,93 @@ def measured_peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def tensor_probe(device_index):
+    """Dense tcgen05 throughput of this GPU (aeisu_tensor_peak): kind::f16 and kind::f8f6f4 with
+    E4M3 operands, M = 128, N = 256, two CTAs per SM, best of 5 launches of 4,096 MMAs each."""
+    import ctypes as C
+    from aeisu_b200 import _lib
+    out = {}
+    for name, kind in (("f16_tflops", 0), ("e4m3_tflops", 1)):
+        v = C.c_double()
+        _lib.check(_lib.lib().aeisu_tensor_peak(device_index, kind, 2, 4096, 5, C.byref(v)))
+        out[name] = v.value
+    out["how"] = "tcgen05.mma M=128 N=256, 296 CTAs x 4096 MMAs, one thread each, best of 5 launches"
+    return out
+
+
+def bind_to_gpu_numa(device_index):
+    """Restrict this process to the host CPUs NVML lists as closest to the GPU (its NUMA node),
+    so that pinned host buffers allocated afterwards are first touched on that node."""
+    try:
+        import pynvml
+        import torch
+        p = torch.cuda.get_device_properties(device_index)
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 64) + 63) // 64)
+        cpus = {64 * i + b for i, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return "not bound: no CPU of the GPU's node is available to this process"
+        os.sched_setaffinity(0, cpus)
+        return f"{len(cpus)} CPUs of the GPU's NUMA node"
+    except Exception as e:   # NVML absent or the query unsupported: leave the affinity as it is
+        return f"not bound: {type(e).__name__}"
+
+
+def host_link_ceiling(dev, d2h_bytes, h2d_bytes, dist, world, reps=3):
+    """Bytes per second of one plain pinned D2H copy of d2h_bytes and one H2D copy of
+    h2d_bytes, on their own streams at once, on every rank at once (max over ranks): the host
+    link's ceiling for the end-to-end step's traffic."""
+    import torch
+    dsrc = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    ddst = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    hdst = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    hsrc = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    s_out, s_in = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    best = float("inf")
+    for r in range(reps + 1):
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(s_out):
+            hdst.copy_(dsrc, non_blocking=True)
+        with torch.cuda.stream(s_in):
+            ddst.copy_(hsrc, non_blocking=True)
+        s_out.synchronize()
+        s_in.synchronize()
+        dt = time.perf_counter() - t0
+        if world > 1:
+            dt = max_over_ranks(dt, dist, dev)
+        if r > 0:
+            best = min(best, dt)
+    del dsrc, ddst, hdst, hsrc
+    return (d2h_bytes + h2d_bytes) / best
+
+
+def distinct_frames(dev, seed, scenes, count, h, w):
+    """`count` distinct seeded frames on the device: `scenes` rendered procedural scenes, the
+    first `scenes` frames as rendered, every later one a rendered scene circularly shifted by a
+    seeded offset and flipped by seeded bits (the scene statistics of the recipe, without
+    rendering every frame)."""
+    import torch
+    base = torch.from_numpy(gen_frames(seed, scenes, h, w, "area")).to(dev)
+    rng = np.random.default_rng(seed + 999)
+    out = torch.empty((count, h, w, 3), dtype=torch.uint8, device=dev)
+    for i in range(count):
+        f = base[i % scenes]
+        if i >= scenes:
+            dy, dx, flips = int(rng.integers(1, h)), int(rng.integers(1, w)), int(rng.integers(0, 4))
+            f = torch.roll(f, (dy, dx), (0, 1))
+            if flips & 1:
+                f = f.flip(0)
+            if flips & 2:
+                f = f.flip(1)
+        out[i] = f
+    return out
+
+
 def _oracle_model(ckpt):
     """The reference's FP32 CPU path for a workload's checkpoint.  The INT8 artifact was exported
     from aeisu_area.pt (its FP16 weights are that checkpoint's, rounded), and the reference's
@@ -232,13 +330,23 @@ def _cpu_threads():
         return os.cpu_count() or 1
 
 
-def measure_latency(dev, runs, distinct=16):
-    """p50/p99 device latency of one 1920x1080 -> 3840x2160 frame (FP16, mixed and INT8 routes),
-    input resident in HBM, cycling `distinct` seeded frames, CUDA events around each call."""
+def measure_latency(dev, runs, scenes=40):
+    """Latency of one 1920x1080 -> 3840x2160 frame (FP16, mixed and INT8 routes) over `runs`
+    distinct seeded frames (distinct_frames: `scenes` rendered scenes, the rest seeded shifts and
+    flips of them), p50 and p99:
+    * device: input resident in HBM, CUDA events around each call on the launching stream;
+    * end to end: through the public API with pinned host buffers, each call copying its uint8
+      frame in, upscaling and copying the uint8 result out before it returns (host clock)."""
     import torch
     from aeisu_b200 import load_model
-    frames = torch.from_numpy(gen_frames(50_000, distinct, 1080, 1920, "area")).to(dev)
-    out = torch.empty((3840 * 2160 * 3,), dtype=torch.uint8, device=dev).view(2160, 3840, 3)
+    frames = distinct_frames(dev, 50_000, min(scenes, runs), runs, 1080, 1920)
+    host_frames = frames.cpu().pin_memory()
+    out = torch.empty((2160, 3840, 3), dtype=torch.uint8, device=dev)
+    host_out = torch.empty((2160, 3840, 3), dtype=torch.uint8).pin_memory()
+
+    def pct(ms):
+        ms = sorted(ms)
+        return {"p50_ms": ms[len(ms) // 2], "p99_ms": ms[min(len(ms) - 1, int(len(ms) * 0.99))]}
     res = {}
     for precision, ckpt in (("fp16", "aeisu_area.pt"), ("mixed", "adaptive_fp8.bin"), ("int8", "aeisu_int8_fp16.pt")):
         model = load_model(WEIGHTS / ckpt, f"cuda:{dev.index}", precision)
@@ -246,17 +354,26 @@ def measure_latency(dev, runs, distinct=16):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
         with torch.cuda.stream(stream):
             for i in range(10):
-                model.upscale_u8(frames[i % distinct], 0, out=out)
+                model.upscale_u8(frames[i % runs], 0, out=out)
             for i in range(runs):
                 ev[i][0].record(stream)
-                model.upscale_u8(frames[i % distinct], 0, out=out)
+                model.upscale_u8(frames[i], 0, out=out)
                 ev[i][1].record(stream)
         torch.cuda.synchronize(dev)
-        ms = sorted(a.elapsed_time(b) for a, b in ev)
-        res[precision] = {"p50_ms": ms[len(ms) // 2], "p99_ms": ms[min(len(ms) - 1, int(len(ms) * 0.99))]}
+        res[precision] = pct([a.elapsed_time(b) for a, b in ev])
+        for i in range(10):
+            model.upscale_u8(host_frames[i % runs], 0, out=host_out)
+        wall = []
+        for i in range(runs):
+            t0 = time.perf_counter()
+            model.upscale_u8(host_frames[i], 0, out=host_out)
+            wall.append((time.perf_counter() - t0) * 1e3)
+        res[precision]["e2e"] = pct(wall)
         model.close()
-    res["config"] = (f"1920x1080 -> 3840x2160, batch 1, tile 0, {runs} runs over {distinct} distinct seeded frames, "
-                     "input in HBM, CUDA events per call on the launching stream")
+    res["config"] = (f"1920x1080 -> 3840x2160, batch 1, tile 0, {runs} distinct seeded frames "
+                     f"({min(scenes, runs)} rendered scenes and seeded shifts/flips of them); device: input in HBM, "
+                     "CUDA events per call on the launching stream; e2e: pinned host frame in, uint8 result in "
+                     "pinned host memory on return (6,220,800 B H2D + 24,883,200 B D2H per call), host clock")
     return res
 
 
@@ -409,6 +526,86 @@ def measure_train(dev, batch, sm_mhz=None):
                       "set to None before each step, CUDA events on the current stream"}
 
 
+def measure_config5(dev, dist, rank, world, barrier, stream_frames=512, batch=8, band_reps=5):
+    """Config 5 of the benchmark set at this job's N, on the mixed route:
+    * stream4k: a 512-frame stream of 3840x2160 frames split frame-parallel (512/N frames per
+      rank, calls of 8 frames, distinct seeded frames per rank);
+    * band8k: one 7680x4320 input frame (a 4K scene mirrored 2x2), one row band per rank.
+    Each with inputs resident in HBM (CUDA events) and end to end through the public API with
+    pinned host buffers (host clock); the slowest rank's time, whole-job output pixels."""
+    import torch
+    from aeisu_b200 import load_model
+    model = load_model(WEIGHTS / "adaptive_fp8.bin", f"cuda:{dev.index}", "mixed")
+    stream = torch.cuda.Stream(dev)
+    h, w = 2160, 3840
+    per_rank = stream_frames // world
+    frames = distinct_frames(dev, 70_000 + 1000 * rank, 4, per_rank, h, w)
+    outs = [torch.empty((batch, 2 * h, 2 * w, 3), dtype=torch.uint8, device=dev) for _ in range(2)]
+    calls = [(i, min(batch, per_rank - i)) for i in range(0, per_rank, batch)]
+
+    def timed(fn, reps=1):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1) / reps
+        return max_over_ranks(ms, dist, dev) if world > 1 else ms
+
+    def wall(fn, reps=1):
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+        return max_over_ranks(dt, dist, dev) if world > 1 else dt
+
+    def run_stream():
+        for k, (i, b) in enumerate(calls):
+            model.upscale_u8(frames[i:i + b], 0, out=outs[k & 1][:b])
+    with torch.cuda.stream(stream):
+        model.upscale_u8(frames[:batch], 0, out=outs[0][:min(batch, per_rank)])
+    stream_ms = timed(run_stream)
+    stream_px = 4 * h * w * per_rank * world
+    pool_n = min(per_rank, 32)
+    pool = frames[:pool_n].cpu().pin_memory()
+    host_out = torch.empty((batch, 2 * h, 2 * w, 3), dtype=torch.uint8).pin_memory()
+
+    def run_stream_e2e():
+        for i, b in calls:
+            j = i % pool_n if i % pool_n + b <= pool_n else 0
+            model.upscale_u8(pool[j:j + b], 0, out=host_out[:b])
+    stream_e2e_s = wall(run_stream_e2e)
+    big = torch.cat([torch.cat([frames[0], frames[0].flip(1)], 1), torch.cat([frames[0].flip(0), frames[0].flip(0).flip(1)], 1)], 0)
+    del frames, outs, pool, host_out
+    big = big.contiguous()
+    big_out = torch.zeros((2 * 4320, 2 * 7680, 3), dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        model.upscale_u8_band(big, rank, world, out=big_out)
+    band_ms = timed(lambda: model.upscale_u8_band(big, rank, world, out=big_out), band_reps)
+    host_big = big.cpu().pin_memory()
+    host_big_out = torch.zeros((2 * 4320, 2 * 7680, 3), dtype=torch.uint8).pin_memory()
+    model.upscale_u8_band(host_big, rank, world, out=host_big_out)
+    band_e2e_s = wall(lambda: model.upscale_u8_band(host_big, rank, world, out=host_big_out), band_reps)
+    band_px = 4 * 4320 * 7680
+    model.close()
+    return {
+        "stream4k": {"value": stream_px / (stream_ms / 1e3) / 1e6, "unit": "output Mpix/s", "ms": stream_ms,
+                     "e2e": {"value": stream_px / stream_e2e_s / 1e6, "unit": "output Mpix/s",
+                             "h2d_bytes": per_rank * h * w * 3, "d2h_bytes": per_rank * 4 * h * w * 3},
+                     "scaling": "strong", "config": f"{stream_frames} frames 3840x2160 -> 7680x4320, mixed, "
+                     f"{per_rank} per GPU in calls of {batch}; distinct seeded frames per rank (4 rendered scenes and "
+                     f"seeded shifts/flips); e2e: frames cycled through {pool_n} pinned host frames per rank"},
+        "band8k": {"value": band_px / (band_ms / 1e3) / 1e6, "unit": "output Mpix/s", "ms": band_ms,
+                   "e2e": {"value": band_px / band_e2e_s / 1e6, "unit": "output Mpix/s"},
+                   "scaling": "strong", "config": f"one 7680x4320 frame -> 15360x8640, mixed, {world} row band(s) of "
+                   f"the padded grid with 32-row recomputed halos, one per GPU; mean of {band_reps} calls"},
+    }
+
+
 def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
     """Time the reference algorithm's CPU implementation (the oracle port, FP32, all host
     threads) on a bounded sample of the workload's frames."""
@@ -476,6 +673,9 @@ def main():
                     help="image pairs per call of the evaluation-metrics measurement (0 disables)")
     ap.add_argument("--train-batch", type=int, default=32,
                     help="sources per step of the training-reconstruction measurement (0 disables)")
+    ap.add_argument("--e2e-steps", type=int, default=20, help="steps of the end-to-end measurement")
+    ap.add_argument("--no-config5", dest="config5", action="store_false",
+                    help="skip the 4K-stream and 8K-band measurements of the default workload")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -559,6 +759,7 @@ def main():
     model.set_detailed_timing(False)
     stage_ms = {k: v / args.steps for k, v in stage_sum.items() if k.endswith("_ms")}
 
+    probe = tensor_probe(local_rank)
     latency = measure_latency(dev, args.latency_runs) if (rank == 0 and args.latency_runs > 0) else None
     metric_line = (measure_metrics(dev, out, args.metric_pairs)
                    if (rank == 0 and args.metric_pairs > 0 and not band) else None)
@@ -566,43 +767,79 @@ def main():
     train_line = (measure_train(dev, args.train_batch, clocks.summary().get("sm_mhz"))
                   if (rank == 0 and args.train_batch > 0 and not band) else None)
 
-    # end-to-end through the public API with pinned host buffers
+    # end-to-end through the public API with pinned host buffers, allocated after binding the
+    # process to the GPU's NUMA node
+    numa = bind_to_gpu_numa(local_rank)
+    share = 1.0 / world if band else 1.0   # a row-band rank moves about 1/N of the frame
+    h2d_bytes, d2h_bytes = int(n * h * w * 3 * share), int(n * 4 * h * w * 3 * share)
     host_src = torch.from_numpy(frames).pin_memory()
     host_out = torch.empty((n, 2 * h, 2 * w, 3), dtype=torch.uint8).pin_memory()
     upscale(host_src, host_out)
     barrier()
     t0 = time.perf_counter()
-    e2e_steps = max(2, min(args.steps, 5))
+    e2e_steps = max(args.e2e_steps, 2)
     for _ in range(e2e_steps):
         upscale(host_src, host_out)
     e2e_dt = time.perf_counter() - t0
     if world > 1:
         e2e_dt = max_over_ranks(e2e_dt, dist, dev)
     e2e_value = out_mpix * e2e_steps / e2e_dt / 1e6
+    del host_src, host_out
+    ceiling = host_link_ceiling(dev, d2h_bytes, h2d_bytes, dist, world)
+    e2e_rate = (h2d_bytes + d2h_bytes) * e2e_steps / e2e_dt
+
+    # the other box-scale configurations: a 512-frame 4K stream split across the ranks, and one
+    # 7680x4320 frame in one row band per rank
+    extra = {}
+    if args.workload == "mixed720" and args.config5:
+        del out, src
+        extra = measure_config5(dev, dist, rank, world, barrier)
 
     # roofline of the dominant stage
     hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    e4m3_peak = probe["e4m3_tflops"]
     hp, wp = padded(h, w)
     stage_names = ["analysis_project_ms", "compress_core_ms", "expand_ms", "refine_tail_ms", "reconstruction_ms"]
     dom = max(stage_names, key=lambda k: stage_ms.get(k, 0.0))
     # per-stage MAC per padded LR pixel (aeisu/model.py CONVOLUTIONS x pixel rates)
     macs = {"analysis_project_ms": 256, "compress_core_ms": 512 + 4608, "expand_ms": 512,
             "refine_tail_ms": 4608 + 1024}
-    share = 1.0 / world if band else 1.0   # rank 0 times its own band: about 1/N of the frame
+    e4m3_stages = {"compress_core_ms", "expand_ms"} if precision == "mixed" else set()
     if dom == "reconstruction_ms":
         algo = HEAD_BYTES_PER_PX * h * w * n * share
         achieved = algo / (stage_ms[dom] / 1e3) / 1e9
         rec = RECORDED_TRAFFIC.get(args.workload)
-        traffic = rec[1] if rec and rec[0] == dom and not args.precision else None
+        recorded = rec and rec[0] == dom and not args.precision
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": traffic, "algorithmic_bytes": algo, "stage": "reconstruction head",
+                "traffic": rec[1] if recorded else None, "traffic_source": rec[2] if recorded else None,
+                "algorithmic_bytes": algo, "stage": "reconstruction head",
                 "kernel": "k_tc_head" if precision != "fp32" else "k_f32_head", "peak_kind": peak_kind}
     else:
         algo = 2 * macs[dom] * hp * wp * n * share
         achieved = algo / (stage_ms[dom] / 1e3) / 1e12
-        peak = tf_burst if precision != "mixed" else tf_burst  # FP8 peak not measured: bf16 figure
+        fp8 = dom in e4m3_stages
+        peak = e4m3_peak if fp8 else tf_burst
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None, "stage": dom[:-3], "peak_kind": peak_kind}
+                "frac": achieved / peak, "traffic": None, "stage": dom[:-3],
+                "peak_kind": "e4m3 tcgen05 probe (this run)" if fp8 else peak_kind}
+    # the whole step against the north-star roofline: max(controller FLOPs at tensor peak, head
+    # bytes at HBM bandwidth); the mixed route's FP8 share at the E4M3 probe's rate
+    pad_px = hp * wp * n * share
+    if precision == "mixed":
+        f16_flop, e4m3_flop = 2 * MIXED_F16_MACS * pad_px, 2 * MIXED_E4M3_MACS * pad_px
+    else:
+        f16_flop, e4m3_flop = CONTROLLER_FLOP_PER_PX * pad_px, 0.0
+    t_ctrl = f16_flop / (tf_burst * 1e12) + e4m3_flop / (e4m3_peak * 1e12)
+    head_bytes = HEAD_BYTES_PER_PX * h * w * n * share
+    t_head = head_bytes / (hbm * 1e9)
+    t_roof = max(t_ctrl, t_head)
+    roof["step"] = {"controller_flop": f16_flop + e4m3_flop, "controller_f16_flop": f16_flop,
+                    "controller_e4m3_flop": e4m3_flop, "head_bytes": head_bytes,
+                    "t_controller_ms": t_ctrl * 1e3, "t_head_ms": t_head * 1e3, "t_roof_ms": t_roof * 1e3,
+                    "ms_per_step": ms_per_step, "frac": t_roof * 1e3 / ms_per_step,
+                    "peaks": {"hbm_gbs": hbm, "f16_tflops": tf_burst, "e4m3_tflops": e4m3_peak,
+                              "f16_kind": f"cuBLAS bf16 burst ({peak_kind})", "e4m3_kind": "tcgen05 probe, this run"}}
+    roof["tensor_probe"] = probe
 
     if rank == 0:
         line = {
@@ -621,8 +858,13 @@ def main():
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "output Mpix/s",
-                    "h2d_bytes_per_step": int(n * h * w * 3 * share), "d2h_bytes_per_step": int(n * 4 * h * w * 3 * share),
-                    "steps": e2e_steps},
+                    "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes, "steps": e2e_steps,
+                    "host_bytes_per_s": e2e_rate, "host_link_ceiling_bytes_per_s": ceiling,
+                    "host_link_frac": e2e_rate / ceiling, "numa": numa,
+                    "ceiling_how": "one plain pinned D2H copy of the step's output bytes and one H2D copy of its "
+                                   "input bytes, on two streams at once, on every rank at once (max over ranks), "
+                                   "best of 3"},
+            **extra,
             "gpu_launches": int(launches),
             "latency_1080p": latency,
             "evaluation_metrics": metric_line,
