@@ -946,18 +946,29 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
 }
 
 // ---- reconstruction head -------------------------------------------------------------------
-// Work item: a strip of 128 LR pixels of a region's core rectangle and a band of rows.  Per
-// row: D[px][tap*4 + phase] = sum_k c_k * basis_hi + sum_k c_k * basis_lo + base_hi + base_lo
-// (three K=16 MMAs; the FP32 bank is split in two f16 terms so the filters keep FP32-level
-// accuracy), then each thread applies its 25x4 weights to the 5x5 RGB neighbourhood.  The
-// source rows slide through an 8-row ring (each source row converted once per strip); the
-// next row's coefficients are prefetched with cp.async and its new source row is loaded into
-// registers while the current row computes.  Four CTAs share an SM, so one CTA's MMA and
-// TMEM waits hide behind the others' FMAs.
+// Work item: a strip of PX * 128 LR pixels of a region's core rectangle and a band of rows.
+// Thread t owns pixels x0 + t + 128 i (tile i < PX) of every row of the band.  Per row, one
+// elected thread loads the tiles' clamped f16 coefficients with TMA row-window loads (128
+// pixels x 2 chunks each) and, per tile, issues
+//   D[px][tap*4 + phase] = sum_k c_k * basis_hi + sum_k c_k * basis_lo + base_hi + base_lo
+// (three K = 16 MMAs; the FP32 bank is split into two f16 terms, so the filters keep FP32-level
+// accuracy) into that tile's 128 TMEM columns.  Each thread then applies its pixels' 25 x 4
+// weights to their 5 x 5 RGB neighbourhoods on the CUDA cores.  Source rows slide through an
+// 8-row ring in shared memory, converted once per strip and stored as (s[x], s[x+1]) pairs that
+// feed packed f32x2 FMAs directly; the next row's coefficients arrive by TMA and its new source
+// row is loaded into registers while the current row computes; the TMEM loads of one column
+// group are issued before the FMAs of the previous one.  Several CTAs share an SM, so one CTA's
+// MMA and TMA waits hide behind the others' FMAs.  The kernel is specialised on the source
+// (uint8 HWC or float32 CHW) and destination (uint8 HWC or float32 CHW) formats.
 constexpr int kHeadRing = 8;
-constexpr int kHeadTW = kM + 4;
-constexpr int kHeadBCH = 2 * 128 * 16;   // one B operand: 2 chunks x 128 rows
-constexpr int kHeadSmem = 3 * kHeadBCH + 2 * 2 * kM * 16 + 2 * kM * 16 + kHeadRing * 3 * kHeadTW * 8;
+constexpr int kHeadBCH = 2 * 128 * 16;             // one B operand: N = 128 rows, 2 K chunks
+constexpr int kHeadTile = 2 * kM * 16;             // one tile's A operand: 2 K chunks x 128 rows (one TMA box)
+// PX pixels per thread: a strip of PX * 128 LR pixels, PX * 128 TMEM columns per CTA
+constexpr int head_strip(int px) { return px * kM; }
+constexpr int head_tw(int px) { return px * kM + 4; }   // source columns of a strip (2 halo columns each side)
+constexpr int head_smem(int px) {
+    return 1024 + 2 * px * kHeadTile + 3 * kHeadBCH + kM * 16 * 2 + kHeadRing * 3 * (head_tw(px) + 1) * 8;
+}
 
 // floor(clamp(v, 0, 1) * 255 + 0.5) with separate multiply and add (runtime.py:24-25 in
 // float32), for two values at once (packed f32x2 arithmetic rounds each lane as the scalar
@@ -969,222 +980,289 @@ __device__ __forceinline__ uint2 u8_code_bits2(float a, float b) {
     return make_uint2(__float_as_uint(f.x), __float_as_uint(f.y));
 }
 
-__global__ void __launch_bounds__(kThreads) k_tc_head(SrcDesc src, RegionSet rs, DstDesc dst,
-                                                      const void* __restrict__ meta, const uint8_t* __restrict__ bimg,
-                                                      int band, int* nonfinite, int* err) {
-    constexpr int BCH = kHeadBCH;
+template <int PX, bool SRC_U8, bool DST_U8>
+__global__ void __launch_bounds__(kThreads, PX == 1 ? 4 : 2) k_tc_head(const __grid_constant__ CUtensorMap tcoef, SrcDesc src,
+                                                         RegionSet rs, DstDesc dst, const uint8_t* __restrict__ bimg,
+                                                         int band, int* nonfinite, int* err) {
+    constexpr int kHeadStrip = head_strip(PX), kHeadTW = head_tw(PX), kHeadABytes = PX * kHeadTile;
+    constexpr uint32_t kCols = 128 * PX;                  // TMEM columns: 128 per tile
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* sB = smem_raw;                                   // basis hi, basis lo, base
-    uint8_t (*sA)[2 * kM * 16] = reinterpret_cast<uint8_t (*)[2 * kM * 16]>(sB + 3 * BCH);   // [2 rows]
-    uint8_t* sOnes = sB + 3 * BCH + 2 * 2 * kM * 16;          // [2 chunks][128][16 B]
-    // source ring, per slot and channel the pairs (s[x], s[x+1]) of adjacent columns, so a
-    // horizontal tap pair is one 8-byte load that feeds packed f32x2 FMAs directly
-    float2 (*s_pair)[3][kHeadTW] = reinterpret_cast<float2 (*)[3][kHeadTW]>(sOnes + 2 * kM * 16);
+    uint8_t* smem = align_smem(smem_raw);
+    uint8_t* sA = smem;                                   // [2 rows][PX tiles][2 chunks][128][16 B] (TMA)
+    uint8_t* sB = smem + 2 * kHeadABytes;                 // basis hi, basis lo, base
+    uint8_t* sOnes = sB + 3 * kHeadBCH;                   // [2 chunks][128][16 B]
+    // source ring: per slot and channel the pairs (s[x], s[x+1]) of adjacent columns, so a
+    // horizontal tap pair is one 8-byte load that feeds packed f32x2 FMAs directly.  Each row
+    // starts with one spare pair, the target of column 0's second half, so puts need no test.
+    float2 (*s_pair)[3][kHeadTW + 1] = reinterpret_cast<float2 (*)[3][kHeadTW + 1]>(sOnes + 2 * kM * 16);
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
-    __shared__ alignas(8) uint64_t s_bar;
-    copy_image(sB, bimg, 3 * BCH);
+    __shared__ alignas(8) uint64_t s_bar[3];              // MMA round done; coefficient rows of A buffer 0, 1
+    copy_image(sB, bimg, 3 * kHeadBCH);
     for (int i = threadIdx.x; i < 2 * kM; i += blockDim.x) {
         const uint32_t one2 = 0x3C003C00u;   // f16 1.0, 1.0
         *reinterpret_cast<uint4*>(sOnes + i * 16) = (i < kM) ? make_uint4(one2, 0, 0, 0) : make_uint4(0, 0, 0, 0);
     }
-    fill_lut(s_lut);
+    if (SRC_U8) fill_lut(s_lut);
     fence_async_smem();
-    cta_setup(&s_tmem, &s_bar, 1, 128);
+    cta_setup(&s_tmem, s_bar, 3, kCols);
     const uint32_t tmem = s_tmem;
-    uint32_t phase = 0;
     const int t = threadIdx.x, warp = t >> 5;
-    const int nstrip = (rs.core_w + kM - 1) / kM, nband = (rs.core_h + band - 1) / band;
+    const uint32_t lane = uint32_t(32 * warp) << 16;
+    const int nstrip = (rs.core_w + kHeadStrip - 1) / kHeadStrip, nband = (rs.core_h + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
-    const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB);
+    const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB), a0 = smem_addr(sA);
     constexpr uint32_t idesc = idesc_m128(128);
-    // Work beside the apply is spread over the warps, so that no warp arrives late at the row
-    // barrier: the last warp stages the four extra window columns, warp 1 issues the MMAs.
-    constexpr int kExtra = kHeadTW - kThreads;   // window columns beyond one per thread (4)
-    const bool two = t >= kThreads - kExtra;    // this thread stages a second window column
-    const int issuer = 32;
-    bool ok = true;
-    bool pend = false;   // issuing thread: an MMA round was committed and not yet waited for
-    auto issue = [&](int b) {   // MMA round of the row whose coefficients sit in sA[b]
-        fence_after_sync();
-        const uint64_t a = sdesc(smem_addr(sA[b]), kM * 16, 128);
-        mma_f16(tmem, a, sdesc(b0, 128 * 16, 128), idesc, 0);
-        mma_f16(tmem, a, sdesc(b0 + BCH, 128 * 16, 128), idesc, 1);
-        mma_f16(tmem, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * BCH, 128 * 16, 128), idesc, 1);
-        commit(&s_bar);
-        pend = true;
+    // Work beside the apply is spread over the warps: warp 1 issues the loads and MMAs, the last
+    // four threads stage the four window columns beyond PX per thread.
+    constexpr int kExtra = kHeadTW - PX * kThreads;
+    const bool extra = t >= kThreads - kExtra;
+    // strip column of source column j of this thread: t + 128 j, and for j = PX the extra column
+    auto col_of = [&](int j) { return j < PX ? t + j * kThreads : PX * kThreads + t - (kThreads - kExtra); };
+    const bool issuer = t == 32;
+    uint32_t mma_phase = 0, tma_phase = 0, tma_pend = 0;   // tma bits: per A buffer
+    bool ok = true, mma_pend = false;
+    // coefficient rows of row y into A buffer b: PX boxes of 128 pixels x 2 chunks
+    auto load_coef = [&](int r, int y, int x0, int b) {
+        mbar_arrive_expect_tx(&s_bar[1 + b], uint32_t(kHeadABytes));
+#pragma unroll
+        for (int h = 0; h < PX; ++h)
+            tma_load_4d(sA + b * kHeadABytes + h * kHeadTile, &tcoef, 2 * (x0 + h * kM), 0, y, r, &s_bar[1 + b]);
+        tma_pend |= 1u << b;
+    };
+    // MMA round of the row whose coefficients are (being) loaded into A buffer b.  On an expired
+    // wait no MMA is issued, but the commit still arrives, so that no thread waits for it in vain.
+    auto issue = [&](int b) {
+        const uint32_t par = (tma_phase >> b) & 1u;
+        const bool landed = mbar_try_wait(&s_bar[1 + b], par) || mbar_wait_bounded(&s_bar[1 + b], par, err, kErrTimeout);
+        if (landed) {
+            tma_phase ^= 1u << b;
+            tma_pend &= ~(1u << b);
+            fence_after_sync();
+#pragma unroll
+            for (int tile = 0; tile < PX; ++tile) {
+                const uint64_t a = sdesc(a0 + b * kHeadABytes + tile * kHeadTile, kM * 16, 128);
+                const uint32_t d = tmem + tile * 128;
+                mma_f16(d, a, sdesc(b0, 128 * 16, 128), idesc, 0);
+                mma_f16(d, a, sdesc(b0 + kHeadBCH, 128 * 16, 128), idesc, 1);
+                mma_f16(d, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * kHeadBCH, 128 * 16, 128), idesc, 1);
+            }
+        }
+        commit(&s_bar[0]);
+        mma_pend = true;
+        return landed;
     };
 
     for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
-
         last_item(item, items);
         const int r = int(item / ((long long)nstrip * nband));
         const int bi = int((item / nstrip) % nband), si = int(item % nstrip);
         const int4 core = rs.cores[r];
-        const int y0 = core.x + bi * band, x0 = core.y + si * kM;
+        const int y0 = core.x + bi * band, x0 = core.y + si * kHeadStrip;
         if (y0 >= core.z || x0 >= core.w) continue;            // uniform across the CTA
-        const int y1 = min(y0 + band, core.z), xe = min(x0 + kM, core.w);
+        const int y1 = min(y0 + band, core.z);
         const int4 reg = rs.regions[r];
-        // source columns this thread stages (window columns t and t + 128), clamped once
-        int sx[2];
+        // this thread's source columns (col_of(j)), clamped once per item: region replicate
+        // padding, then the frame's
+        int scol[PX + 1];
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
-            sx[j] = clampi(reg.z + clampi(x0 - 2 + t + j * kExtra, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
-        auto src_raw = [&](int row, int j) -> uint3 {
+        for (int j = 0; j <= PX; ++j)
+            scol[j] = clampi(reg.z + clampi(x0 - 2 + col_of(j), 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+        const size_t plane = size_t(src.H) * src.W;
+        const uint8_t* sfu8 = static_cast<const uint8_t*>(src.ptr) + size_t(reg.x) * plane * 3;
+        const float* sff = static_cast<const float*>(src.ptr) + size_t(reg.x) * plane * 3;
+        auto src_row = [&](int row) {   // element offset of the frame row that region row `row` reads
             const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
-            if (src.kind == 0) {
-                const uint8_t* p = static_cast<const uint8_t*>(src.ptr) + ((size_t(reg.x) * src.H + sy) * src.W + sx[j]) * 3;
+            return size_t(sy) * src.W;
+        };
+        auto src_raw = [&](size_t ro, int j) -> uint3 {
+            if (SRC_U8) {
+                const uint8_t* p = sfu8 + (ro + scol[j]) * 3;
                 return make_uint3(p[0], p[1], p[2]);
             }
-            const size_t plane = size_t(src.H) * src.W;
-            const float* p = static_cast<const float*>(src.ptr) + size_t(reg.x) * 3 * plane + size_t(sy) * src.W + sx[j];
+            const float* p = sff + ro + scol[j];
             return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
         };
         auto slot = [&](int row) { return (row - y0 + 2) & (kHeadRing - 1); };
-        auto put = [&](int row, int j, uint3 raw) {   // value of column col: first of pair col, second of col-1
-            const float3 v = finish_src(src, raw, s_lut);
-            const int col = t + j * kExtra;
-            float2(&ps)[3][kHeadTW] = s_pair[slot(row)];
-            ps[0][col].x = v.x; ps[1][col].x = v.y; ps[2][col].x = v.z;
-            if (col > 0) { ps[0][col - 1].y = v.x; ps[1][col - 1].y = v.y; ps[2][col - 1].y = v.z; }
+        auto put = [&](int row, int j, uint3 raw) {   // column col: first of pair col, second of pair col - 1
+            float v[3];
+            if (SRC_U8) {
+                v[0] = s_lut[raw.x]; v[1] = s_lut[raw.y]; v[2] = s_lut[raw.z];
+            } else {
+                v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y); v[2] = __uint_as_float(raw.z);
+            }
+            float* ps = &s_pair[slot(row)][0][col_of(j) + 1].x;
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                ps[ch * 2 * (kHeadTW + 1)] = v[ch];
+                ps[ch * 2 * (kHeadTW + 1) - 1] = v[ch];
+            }
         };
-        // coefficients of row y: meta[r][y][chunk][X][16 B], X = this thread's column
-        const uint8_t* cbase = static_cast<const uint8_t*>(meta) +
-                               ((size_t)r * rs.rh * 2 * rs.rw + min(x0 + t, rs.rw - 1)) * 16;
-        const size_t crow = size_t(2) * rs.rw * 16;
-        auto coef = [&](int y, int b) {
-            const uint8_t* g = cbase + size_t(y) * crow;
-            cp_async16(&sA[b][t * 16], g);
-            cp_async16(&sA[b][(kM + t) * 16], g + size_t(rs.rw) * 16);
-            cp_async_commit();
-        };
+        // output: frame base and this thread's first output column of each tile
+        const int oxA = 2 * (reg.z + x0 + t - dst.pad_x);
+
         // prologue: source rows y0-2 .. y0+2, coefficients of y0, MMA(y0)
+        if (issuer) load_coef(r, y0, x0, 0);
         for (int row = y0 - 2; row <= y0 + 2; ++row) {
-            put(row, 0, src_raw(row, 0));
-            if (two) put(row, 1, src_raw(row, 1));
+            const size_t ro = src_row(row);
+#pragma unroll
+            for (int j = 0; j < PX; ++j) put(row, j, src_raw(ro, j));
+            if (extra) put(row, PX, src_raw(ro, PX));
         }
-        coef(y0, 0);
-        cp_async_wait_all();
-        fence_async_smem();
-        fence_before_sync();
         __syncthreads();
-        if (t == issuer) issue(0);
+        if (issuer) ok = issue(0);
         for (int y = y0; y < y1; ++y) {
             const int b = (y - y0) & 1;
-            // prefetch: next row's coefficients (async) and source row y+3 (registers)
+            // prefetch: next row's coefficients (TMA) and source row y+3 (registers)
             const bool next = y + 1 < y1;
-            uint3 pre0 = make_uint3(0u, 0u, 0u), pre1 = pre0;
+            uint3 pre[PX + 1] = {};
             if (next) {
-                coef(y + 1, b ^ 1);
-                pre0 = src_raw(y + 3, 0);
-                if (two) pre1 = src_raw(y + 3, 1);
+                if (issuer) load_coef(r, y + 1, x0, b ^ 1);
+                const size_t ro = src_row(y + 3);
+#pragma unroll
+                for (int j = 0; j < PX; ++j) pre[j] = src_raw(ro, j);
+                if (extra) pre[PX] = src_raw(ro, PX);
             }
-            ok = mbar_wait_bounded(&s_bar, phase, err, kErrTimeout);
-            if (ok) {
-                phase ^= 1u;
-                pend = false;
+            if (!mbar_try_wait(&s_bar[0], mma_phase) && !mbar_wait_bounded(&s_bar[0], mma_phase, err, kErrTimeout)) ok = false;
+            else {
+                mma_phase ^= 1u;
+                mma_pend = false;
             }
             fence_after_sync();
-            // apply the 25 x 4 filter weights of this pixel.  acc[p][ch] is a pair of partial sums
-            // (taps with even kx and the fifth column | taps with odd kx); TMEM columns: tap
+            // the window rows y-2 .. y+2 of this row, one ring slot each
+            const float2(*rows[5])[kHeadTW + 1];
+#pragma unroll
+            for (int ky = 0; ky < 5; ++ky) rows[ky] = s_pair[slot(y - 2 + ky)];
+            const int oy = 2 * (reg.y + y - dst.pad_y);
+            const size_t orow_bytes = size_t(dst.OW) * 3;   // uint8 destination: this row pair's first byte
+            uint8_t* orow = static_cast<uint8_t*>(dst.ptr) + (size_t(reg.x) * dst.OH + oy) * orow_bytes;
+            // apply the 25 x 4 filter weights of both pixels, interleaved (two independent sets of
+            // accumulator chains per TMEM wait).  acc[tile][p][ch] is a pair of partial sums (taps
+            // with even kx and the fifth column | taps with odd kx); TMEM columns of a tile: tap
             // pairs (ky, 0|1) and (ky, 2|3) at (ky*2 + j)*8 + phase*2 + lane, then (ky, 4) at
             // 80 + ky*4 + phase
-            float2 acc[4][3];
+            float2 acc[PX][4][3];
 #pragma unroll
-            for (int p = 0; p < 4; ++p)
+            for (int tile = 0; tile < PX; ++tile)
 #pragma unroll
-                for (int ch = 0; ch < 3; ++ch) acc[p][ch] = make_float2(0.f, 0.f);
+                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                    for (int ch = 0; ch < 3; ++ch) acc[tile][p][ch] = make_float2(0.f, 0.f);
+            const uint32_t tcol = tmem + lane;
+            // weights in four column groups per tile (0-31, 32-63, 64-95, 96-99); the loads of
+            // group q+1 are issued before the FMAs of group q, so their latency hides behind them
+            uint32_t wr[2][PX][32];   // [group parity][tile][column]
+#pragma unroll
+            for (int tile = 0; tile < PX; ++tile) tmem_ld_x32(tcol + tile * 128, wr[0][tile]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int tile = 0; tile < PX; ++tile) tmem_regs_ready(wr[0][tile]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                float w[32];
-                tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + q * 32, w);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
+                for (int tile = 0; tile < PX; ++tile) {
+                    if (q + 1 < 3) tmem_ld_x32(tcol + tile * 128 + (q + 1) * 32, wr[(q + 1) & 1][tile]);
+                    else if (q + 1 == 3) tmem_ld_x4(tcol + tile * 128 + 96, wr[1][tile]);
+                }
+                const uint32_t(&wu)[PX][32] = wr[q & 1];
+#pragma unroll
+                for (int i = 0; i < (q < 3 ? 32 : 4); ++i) {
                     const int n = q * 32 + i;
-                    if (n < 80 && i % 8 == 0) {   // tap pair (ky, 2j), (ky, 2j+1): 12 packed FMAs
+                    if (n < 80 && i % 8 == 0) {   // tap pair (ky, 2j), (ky, 2j+1): 12 packed FMAs per pixel
                         const int pair = n / 8, ky = pair / 2, j = pair % 2;
-                        const float2(&ps)[3][kHeadTW] = s_pair[slot(y - 2 + ky)];
-#pragma unroll
-                        for (int ch = 0; ch < 3; ++ch) {
-                            const float2 sv = ps[ch][t + 2 * j];
-#pragma unroll
-                            for (int p = 0; p < 4; ++p)
-                                acc[p][ch] = __ffma2_rn(sv, make_float2(w[i + 2 * p], w[i + 2 * p + 1]), acc[p][ch]);
-                        }
-                    } else if (n >= 80 && n < 100 && (n - 80) % 4 == 0) {   // tap (ky, 4): 12 FMAs
-                        const int ky = (n - 80) / 4;
-                        const float2(&ps)[3][kHeadTW] = s_pair[slot(y - 2 + ky)];
-#pragma unroll
-                        for (int ch = 0; ch < 3; ++ch) {
-                            const float sv = ps[ch][t + 4].x;
-#pragma unroll
-                            for (int p = 0; p < 4; ++p) acc[p][ch].x = fmaf(sv, w[i + p], acc[p][ch].x);
-                        }
-                    }
-                }
-            }
-            float out[4][3];
-#pragma unroll
-            for (int p = 0; p < 4; ++p)
-#pragma unroll
-                for (int ch = 0; ch < 3; ++ch) out[p][ch] = acc[p][ch].x + acc[p][ch].y;
-            // each thread stores its own 2x2 output pixels: 6 bytes per output row as three
-            // 16-bit words (always 2-byte aligned: the row offset is a multiple of 6), or two
-            // floats per channel plane
-            if (x0 + t < xe) {
-                // One test for all twelve values: a non-finite term makes the sum non-finite.  Only
-                // float sources can make one: with uint8 sources every tap value lies in [0, 1]
-                // and every filter weight is finite (clamped coefficients times a finite bank).
-                if (src.kind != 0) {
-                    float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
-                    all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
-                    all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
-                    if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
-                }
-                const int ox = 2 * (reg.z + x0 + t - dst.pad_x);
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int oy = 2 * (reg.y + y - dst.pad_y) + i;
-                    if (dst.kind == 1) {
 #pragma unroll
                         for (int ch = 0; ch < 3; ++ch)
-                            *reinterpret_cast<float2*>(static_cast<float*>(dst.ptr) +
-                                                       ((size_t(reg.x) * 3 + ch) * dst.OH + oy) * dst.OW + ox) =
-                                make_float2(out[2 * i][ch], out[2 * i + 1][ch]);
-                    } else {
-                        // bytes r0 g0 b0 r1 g1 b1 of the two output pixels (phases 2i, 2i+1)
-                        const uint2 q01 = u8_code_bits2(out[2 * i][0], out[2 * i][1]);
-                        const uint2 q23 = u8_code_bits2(out[2 * i][2], out[2 * i + 1][0]);
-                        const uint2 q45 = u8_code_bits2(out[2 * i + 1][1], out[2 * i + 1][2]);
-                        uint16_t* o = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst.ptr) +
-                                                                  ((size_t(reg.x) * dst.OH + oy) * dst.OW + ox) * 3);
-                        // streaming stores: the frame is read back only by the host copy
-                        __stcs(reinterpret_cast<unsigned short*>(o), (unsigned short)__byte_perm(q01.x, q01.y, 0x0040));
-                        __stcs(reinterpret_cast<unsigned short*>(o + 1), (unsigned short)__byte_perm(q23.x, q23.y, 0x0040));
-                        __stcs(reinterpret_cast<unsigned short*>(o + 2), (unsigned short)__byte_perm(q45.x, q45.y, 0x0040));
+#pragma unroll
+                            for (int tile = 0; tile < PX; ++tile) {
+                                const float2 sv = rows[ky][ch][1 + t + tile * kM + 2 * j];
+#pragma unroll
+                                for (int p = 0; p < 4; ++p)
+                                    acc[tile][p][ch] = __ffma2_rn(
+                                        sv, make_float2(__uint_as_float(wu[tile][i + 2 * p]), __uint_as_float(wu[tile][i + 2 * p + 1])),
+                                        acc[tile][p][ch]);
+                            }
+                    } else if (n >= 80 && n < 100 && (n - 80) % 4 == 0) {   // tap (ky, 4): 12 FMAs per pixel
+                        const int ky = (n - 80) / 4;
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch)
+#pragma unroll
+                            for (int tile = 0; tile < PX; ++tile) {
+                                const float sv = rows[ky][ch][1 + t + tile * kM + 4].x;
+#pragma unroll
+                                for (int p = 0; p < 4; ++p)
+                                    acc[tile][p][ch].x = fmaf(sv, __uint_as_float(wu[tile][i + p]), acc[tile][p][ch].x);
+                            }
+                    }
+                }
+                if (q + 1 < 4) {
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int tile = 0; tile < PX; ++tile) tmem_regs_ready(wr[(q + 1) & 1][tile]);
+                }
+            }
+#pragma unroll
+            for (int tile = 0; tile < PX; ++tile) {
+                float out[4][3];
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                    for (int ch = 0; ch < 3; ++ch) out[p][ch] = acc[tile][p][ch].x + acc[tile][p][ch].y;
+                if (x0 + tile * kM + t < core.w) {
+                    // One test for all twelve values: a non-finite term makes the sum non-finite.  Only
+                    // float sources can make one: with uint8 sources every tap value lies in [0, 1]
+                    // and every filter weight is finite (clamped coefficients times a finite bank).
+                    if (!SRC_U8) {
+                        float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
+                        all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
+                        all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
+                        if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
+                    }
+                    const int ox = oxA + tile * 2 * kM;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        if (!DST_U8) {
+                            float* o = static_cast<float*>(dst.ptr) + (size_t(reg.x) * 3 * dst.OH + oy + i) * dst.OW + ox;
+                            const size_t chs = size_t(dst.OH) * dst.OW;
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch)
+                                *reinterpret_cast<float2*>(o + ch * chs) = make_float2(out[2 * i][ch], out[2 * i + 1][ch]);
+                        } else {
+                            // bytes r0 g0 b0 r1 g1 b1 of the two output pixels (phases 2i, 2i+1), as
+                            // three 16-bit words (2-byte aligned: the row offset is a multiple of 6)
+                            const uint2 q01 = u8_code_bits2(out[2 * i][0], out[2 * i][1]);
+                            const uint2 q23 = u8_code_bits2(out[2 * i][2], out[2 * i + 1][0]);
+                            const uint2 q45 = u8_code_bits2(out[2 * i + 1][1], out[2 * i + 1][2]);
+                            unsigned short* o = reinterpret_cast<unsigned short*>(orow + i * orow_bytes + size_t(ox) * 3);
+                            // streaming stores: the frame is read back only by the host copy
+                            __stcs(o, (unsigned short)__byte_perm(q01.x, q01.y, 0x0040));
+                            __stcs(o + 1, (unsigned short)__byte_perm(q23.x, q23.y, 0x0040));
+                            __stcs(o + 2, (unsigned short)__byte_perm(q45.x, q45.y, 0x0040));
+                        }
                     }
                 }
             }
             // source row y+3 into the ring (read after this row's barrier)
             if (next) {
-                put(y + 3, 0, pre0);
-                if (two) put(y + 3, 1, pre1);
+#pragma unroll
+                for (int j = 0; j < PX; ++j) put(y + 3, j, pre[j]);
+                if (extra) put(y + 3, PX, pre[PX]);
             }
-            cp_async_wait_all();
-            fence_async_smem();
             fence_before_sync();
             if (__syncthreads_or(!ok)) {
                 ok = false;
                 break;
             }
-            if (t == issuer && next) issue(b ^ 1);
+            if (issuer && next && !issue(b ^ 1)) ok = false;   // voted at the next row's barrier
         }
     }
-    if (!ok) {   // abort path: let in-flight copies and MMAs land before TMEM is freed
-        cp_async_wait_all();
-        if (t == issuer && pend) mbar_wait_bounded(&s_bar, phase, err, kErrTimeout, 200000000LL);
+    // abort path: let in-flight copies and MMAs land before TMEM and shared memory are released
+    if (issuer) {
+        if (mma_pend) mbar_wait_bounded(&s_bar[0], mma_phase, err, kErrTimeout, 200000000LL);
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+            if (tma_pend & (1u << b)) mbar_wait_bounded(&s_bar[1 + b], (tma_phase >> b) & 1u, err, kErrTimeout, 200000000LL);
     }
-    cta_teardown(tmem, 128);
+    cta_teardown(tmem, kCols);
 }
 
 // Per-call host work is part of a frame's latency: device properties and kernel attributes are
@@ -1331,16 +1409,35 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     mark(4);
 }
 
+namespace {
+
+template <int PX>
+void launch_tc_head_px(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const CUtensorMap& map,
+                       const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s) {
+    const int sms = sm_count();
+    const bool pdl = use_pdl(rs);
+    constexpr int per_sm = PX == 1 ? 4 : 2;
+    const long long strips = (long long)rs.R * ((rs.core_w + head_strip(PX) - 1) / head_strip(PX));
+    const int band = pick_band_balanced(strips, rs.core_h, sms * per_sm);
+    const long long items = strips * ((rs.core_h + band - 1) / band);
+    auto k = src.kind == 0 ? (dst.kind == 0 ? k_tc_head<PX, true, true> : k_tc_head<PX, true, false>)
+                           : (dst.kind == 0 ? k_tc_head<PX, false, true> : k_tc_head<PX, false, false>);
+    smem_attr(k, head_smem(PX));
+    launch(pdl, k, grid_for(items, per_sm, sms), kThreads, head_smem(PX), s, map, src, rs, dst, head_img, band,
+           nonfinite, err);
+}
+
+}  // namespace
+
 void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const void* meta,
                     const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, int* launches) {
     if ((long long)rs.R * rs.core_h * rs.core_w == 0) return;
-    const int sms = sm_count();
-    const bool pdl = use_pdl(rs);
-    const long long strips = (long long)rs.R * ((rs.core_w + kM - 1) / kM);
-    const int band = pick_band_balanced(strips, rs.core_h, sms * 4);
-    const long long items = strips * ((rs.core_h + band - 1) / band);
-    smem_attr(k_tc_head, kHeadSmem);
-    launch(pdl, k_tc_head, grid_for(items, 4, sms), kThreads, kHeadSmem, s, src, rs, dst, meta, head_img, band, nonfinite, err);
+    // coefficient rows: the chunk-planar [R][rh][2][rw][16 B] tensor, one box = 128 pixels x 2 chunks
+    const CUtensorMap map = make_row_window_map(meta, rs.R, rs.rh, 2, rs.rw, kM);
+    // one pixel per thread: four CTAs of 128 TMEM columns per SM (16 warps) hide the per-row MMA
+    // and barrier waits better than two pixels per thread at two CTAs of 256 columns, which
+    // measured 2.4% slower on 64 x 720p despite 15% fewer instructions per pixel
+    launch_tc_head_px<1>(src, rs, dst, map, head_img, nonfinite, err, s);
     AEISU_CUDA(cudaGetLastError());
     *launches += 1;
 }
