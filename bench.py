@@ -62,8 +62,9 @@ MIXED_F16_MACS, MIXED_E4M3_MACS = 5888, 5632
 # DRAM bytes (read + write) of one launch of the dominant kernel on the default workload, from
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); reported as roofline.traffic
 # with its source, since a run cannot read DRAM counters itself
-RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.08e9 + 0.688e9,
-                                 "ncu capture of one k_tc_head launch, 64 x 1280x720 mixed")}
+RECORDED_TRAFFIC = {"mixed720": ("reconstruction_ms", 2.075e9 + 0.687e9,
+                                 "ncu capture of one k_tc_head<1, true, true> launch (TMA coefficient "
+                                 "rows), 64 x 1280x720 mixed")}
 
 
 def padded(h, w):
