@@ -54,6 +54,7 @@ _SIGNATURES = {
     "aeisu_open_spyr8_headroom": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_float,
                                             C.POINTER(C.c_void_p)]),
     "aeisu_open_folded": (C.c_int, [C.c_void_p, C.c_size_t, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "aeisu_open_sibling": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "aeisu_close": (None, [C.c_void_p]),
     "aeisu_upscale_u8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                    C.c_uint, C.c_void_p]),

@@ -124,6 +124,17 @@ int aeisu_open_folded(const float* values, size_t count, float basis_l1_scale, i
     });
 }
 
+int aeisu_open_sibling(aeisu_t* handle, aeisu_t** out) {
+    return guarded([&] {
+        aeisu::require(out != nullptr, "output handle pointer is null");
+        *out = nullptr;
+        const aeisu::Engine& parent = engine_of(handle);
+        auto h = std::make_unique<aeisu_engine>();
+        h->engine = std::make_unique<aeisu::Engine>(parent, aeisu::Engine::Sibling{});
+        *out = h.release();
+    });
+}
+
 void aeisu_close(aeisu_t* handle) { delete handle; }
 
 int aeisu_upscale_u8(aeisu_t* handle, const uint8_t* src, int n, int h, int w, int tile, uint8_t* dst,

@@ -170,12 +170,7 @@ Engine::Engine(HostModel model, int precision, int device)
     AEISU_CUDA(cudaGetDeviceProperties(&dp, device_));
     if (precision != AEISU_PRECISION_FP32 && !(dp.major == 10 && dp.minor == 0))
         fail(AEISU_ERR_UNSUPPORTED, "the tensor-core routes need an sm_100 (B200) device");
-    int lo = 0, hi = 0;
-    AEISU_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
-    AEISU_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
-    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking));
-    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking));
-    for (auto& e : ev_) AEISU_CUDA(cudaEventCreate(&e));
+    create_streams();
     upload_weights();
     cudaDeviceProp prop{};
     AEISU_CUDA(cudaGetDeviceProperties(&prop, device_));
@@ -192,16 +187,42 @@ Engine::Engine(HostModel model, int precision, int device)
     report_ = os.str();
 }
 
+void Engine::create_streams() {
+    int lo = 0, hi = 0;
+    AEISU_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    AEISU_CUDA(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, hi));
+    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking));
+    AEISU_CUDA(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking));
+    AEISU_CUDA(cudaStreamCreateWithPriority(&lane_, cudaStreamNonBlocking, hi));
+    AEISU_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
+    AEISU_CUDA(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming));
+    for (auto& e : ev_) AEISU_CUDA(cudaEventCreate(&e));
+    flag_.ensure(256, stream_);
+    AEISU_CUDA(cudaMemset(flag_.get(), 0, 256));
+}
+
+Engine::Engine(const Engine& parent, Sibling)
+    : model_(parent.model_), precision_(parent.precision_), device_(parent.device_), report_(parent.report_),
+      timeout_ms_(parent.timeout_ms_), weights_(parent.weights_), stencil_(parent.stencil_), base_(parent.base_),
+      basis_(parent.basis_), tcw_(parent.tcw_), head_img_(parent.head_img_), workspace_cap_(parent.workspace_cap_) {
+    for (int l = 0; l < kLayerCount; ++l) f32_layers_[l] = parent.f32_layers_[l];
+    DeviceGuard guard(device_);
+    create_streams();
+    report_ += "; sibling handle (shared weights)";
+}
+
 Engine::~Engine() {
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
-    for (cudaStream_t c : {copy_in_, copy_out_})
+    for (cudaStream_t c : {copy_in_, copy_out_, lane_})
         if (c) cudaStreamSynchronize(c);
-    DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_, &refined_,
-                     &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
+    DevBuf* all[] = {&src_, &dst_, &tables_, &flag_, &stats_};
     for (DevBuf* b : all) b->reset();
+    for (Workspace& w : ws_)
+        for (DevBuf* b : {&w.enc540, &w.low_a, &w.low_b, &w.dec540, &w.refined, &w.meta, &w.encu, &w.raw}) b->reset();
+    weights_.reset();   // freed here when this is the last handle sharing them
     table_cache_.clear();
     staging_.reset();
     for (auto& e : ev_)
@@ -209,16 +230,21 @@ Engine::~Engine() {
     for (auto& e : pool_) cudaEventDestroy(e);
     for (auto& e : chunk_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
-    for (cudaStream_t c : {copy_in_, copy_out_})
+    for (cudaStream_t c : {copy_in_, copy_out_, lane_})
         if (c) cudaStreamDestroy(c);
+    for (cudaEvent_t e : {fork_, join_})
+        if (e) cudaEventDestroy(e);
     if (prev >= 0) cudaSetDevice(prev);
 }
 
 uint64_t Engine::device_bytes() const {
-    const DevBuf* all[] = {&w_f32_, &src_, &dst_, &tables_, &flag_, &enc540_, &low_a_, &low_b_, &dec540_,
-                           &refined_, &meta_, &encu_, &raw_, &tc_bytes_, &tc_floats_};
+    const DevBuf* all[] = {&src_, &dst_, &tables_, &flag_, &stats_, &weights_->w_f32, &weights_->tc_bytes,
+                           &weights_->tc_floats};
     uint64_t total = 0;
     for (auto* b : all) total += b->capacity();
+    for (const Workspace& w : ws_)
+        for (const DevBuf* b : {&w.enc540, &w.low_a, &w.low_b, &w.dec540, &w.refined, &w.meta, &w.encu, &w.raw})
+            total += b->capacity();
     return total;
 }
 
@@ -242,24 +268,26 @@ void Engine::upload_weights() {
         for (float s : L.slope)
             if (s != L.slope[0]) fail(AEISU_ERR_UNSUPPORTED, "per-channel activation slopes are not supported");
     }
-    w_f32_.ensure(host.size() * 4, stream_);
-    AEISU_CUDA(cudaMemcpy(w_f32_.get(), host.data(), host.size() * 4, cudaMemcpyHostToDevice));
-    const float* d = w_f32_.as<float>();
+    weights_ = std::make_shared<ResidentWeights>();
+    DevBuf& w_f32 = weights_->w_f32;
+    w_f32.ensure(host.size() * 4, stream_);
+    AEISU_CUDA(cudaMemcpy(w_f32.get(), host.data(), host.size() * 4, cudaMemcpyHostToDevice));
+    const float* d = w_f32.as<float>();
     stencil_ = d + o_st;
     base_ = d + o_base;
     basis_ = d + o_basis;
     for (int l = 0; l < kLayerCount; ++l)
         f32_layers_[l] = {d + o_w[l], d + o_b[l], model_.layers[l].slope[0]};
-    flag_.ensure(256, stream_);
-    AEISU_CUDA(cudaMemset(flag_.get(), 0, 256));
     if (precision_ == AEISU_PRECISION_FP32) return;
     const TcHostPack P = pack_tc(model_, tc_route_of(precision_));
-    tc_bytes_.ensure(P.bytes.size(), stream_);
-    tc_floats_.ensure(P.floats.size() * 4, stream_);
-    AEISU_CUDA(cudaMemcpy(tc_bytes_.get(), P.bytes.data(), P.bytes.size(), cudaMemcpyHostToDevice));
-    AEISU_CUDA(cudaMemcpy(tc_floats_.get(), P.floats.data(), P.floats.size() * 4, cudaMemcpyHostToDevice));
-    const uint8_t* B = tc_bytes_.as<uint8_t>();
-    const float* F = tc_floats_.as<float>();
+    DevBuf& tc_bytes = weights_->tc_bytes;
+    DevBuf& tc_floats = weights_->tc_floats;
+    tc_bytes.ensure(P.bytes.size(), stream_);
+    tc_floats.ensure(P.floats.size() * 4, stream_);
+    AEISU_CUDA(cudaMemcpy(tc_bytes.get(), P.bytes.data(), P.bytes.size(), cudaMemcpyHostToDevice));
+    AEISU_CUDA(cudaMemcpy(tc_floats.get(), P.floats.data(), P.floats.size() * 4, cudaMemcpyHostToDevice));
+    const uint8_t* B = tc_bytes.as<uint8_t>();
+    const float* F = tc_floats.as<float>();
     auto ep = [&](const TcHostLayer& L) {
         return EpiParams{F + L.scale, F + L.bias, P.slope, L.out_inv, L.out_deq};
     };
@@ -281,7 +309,7 @@ void Engine::upload_weights() {
     tcw_.refine_bias = F + P.refine_bias;
     tcw_.tail_bias = F + P.tail_bias;
     tcw_.head = B + P.head;
-    tc_head_off_ = P.head;
+    head_img_ = B + P.head;
 }
 
 void Engine::record(int stage, cudaStream_t s) {
@@ -347,96 +375,135 @@ void Engine::synchronize(cudaStream_t s, double timeout_ms) {
     if (flag[0]) fail(AEISU_ERR_NONFINITE, "Non-finite model reconstruction");
 }
 
+namespace {
+
+struct RegionBytes {
+    size_t enc, encu, low, dec, ref, meta, raw;
+    size_t per_region() const { return enc + encu + 2 * low + dec + ref + meta + raw; }
+};
+
+// Workspace bytes per region: f32 NHWC for the FP32 route; chunk-planar f16/e4m3 otherwise.
+RegionBytes region_bytes(int precision, int rh, int rw, bool predict) {
+    const size_t packed = size_t(rh / 2) * (rw / 2), low = size_t(rh / 4) * (rw / 4);
+    const bool tcr = precision != AEISU_PRECISION_FP32, fp8 = precision == AEISU_PRECISION_MIXED;
+    RegionBytes b;
+    b.enc = tcr ? packed * 64 : packed * 32 * 4;
+    b.encu = tcr ? low * (fp8 ? 128 : 256) : 0;
+    b.low = tcr ? low * (fp8 ? 64 : 128) : low * 64 * 4;
+    b.dec = tcr ? packed * 64 : packed * 32 * 4;
+    b.ref = tcr ? 0 : packed * 64 * 4;
+    b.meta = tcr ? size_t(rh) * rw * 32 : packed * 64 * 4;
+    b.raw = (tcr && predict) ? packed * 64 * 4 : 0;
+    return b;
+}
+
+// Regions per batch from which a batch is split across two streams: below it the halves
+// are too small to gain from overlapping (measured +4.7% at 64 frames of 1280x720).
+constexpr int kSplitRegions = 8;
+
+}  // namespace
+
 void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
                        const DstDesc& dst, cudaStream_t s) {
-    const int rh = grp.rh, rw = grp.rw;
-    const size_t packed = size_t(rh / 2) * (rw / 2), low = size_t(rh / 4) * (rw / 4);
-    const bool tcr = precision_ != AEISU_PRECISION_FP32, fp8 = precision_ == AEISU_PRECISION_MIXED;
-    // workspace bytes per region: f32 NHWC for the FP32 route; chunk-planar f16/e4m3 otherwise
-    const size_t enc_b = tcr ? packed * 64 : packed * 32 * 4;
-    const size_t encu_b = tcr ? low * (fp8 ? 128 : 256) : 0;
-    const size_t low_b = tcr ? low * (fp8 ? 64 : 128) : low * 64 * 4;
-    const size_t dec_b = tcr ? packed * 64 : packed * 32 * 4;
-    const size_t ref_b = tcr ? 0 : packed * 64 * 4;
-    const size_t meta_b = tcr ? size_t(rh) * rw * 32 : packed * 64 * 4;
-    const size_t raw_b = (tcr && c.mode == Mode::Predict) ? packed * 64 * 4 : 0;
-    const size_t per_region = enc_b + encu_b + 2 * low_b + dec_b + ref_b + meta_b + raw_b;
-    const size_t chunk = std::max<size_t>(1, std::min<size_t>(grp.regions.size(), workspace_cap_ / per_region));
+    const RegionBytes rb = region_bytes(precision_, grp.rh, grp.rw, c.mode == Mode::Predict);
+    const size_t chunk = std::max<size_t>(1, std::min<size_t>(grp.regions.size(), workspace_cap_ / rb.per_region()));
     for (size_t first = 0; first < grp.regions.size(); first += chunk) {
         const int R = int(std::min(chunk, grp.regions.size() - first));
-        std::vector<int4> table(2 * size_t(R));
-        int core_h = 0, core_w = 0;
-        for (int i = 0; i < R; ++i) {
-            const Region& r = grp.regions[first + i];
-            table[i] = make_int4(r.frame, r.oy, r.ox, 0);
-            table[R + i] = make_int4(r.cy0, r.cx0, r.cy1, r.cx1);
-            core_h = std::max(core_h, r.cy1 - r.cy0);
-            core_w = std::max(core_w, r.cx1 - r.cx0);
+        // Two halves on two streams: upscale calls of the tensor-core routes with enough regions,
+        // unless the stage split is being timed (its marks are recorded on one stream).
+        const bool split = precision_ != AEISU_PRECISION_FP32 && c.mode == Mode::Upscale && !detailed_ &&
+                           R >= kSplitRegions;
+        if (!split) {
+            run_regions(c, grp, first, R, src, dst, s, ws_[0]);
+            continue;
         }
-        // Region tables are uploaded once per call geometry and kept on the device: an upload
-        // from pageable memory would wait for the stream to drain on every call.
-        const TableKey key{int(c.mode), c.n, c.h, c.w, c.tile, rh * 65536 + rw, int(first), c.band, c.bands};
-        auto it = table_cache_.find(key);
-        if (it == table_cache_.end()) {
-            if (table_cache_.size() >= 256) {
-                AEISU_CUDA(cudaStreamSynchronize(s));
-                table_cache_.clear();
-            }
-            auto buf = std::make_unique<DevBuf>();
-            buf->ensure(table.size() * sizeof(int4), s);
-            AEISU_CUDA(cudaMemcpy(buf->get(), table.data(), table.size() * sizeof(int4), cudaMemcpyHostToDevice));
-            it = table_cache_.emplace(key, std::move(buf)).first;
-        }
-        RegionSet rs{};
-        rs.regions = it->second->as<int4>();
-        rs.cores = it->second->as<int4>() + R;
-        rs.R = R; rs.rh = rh; rs.rw = rw; rs.core_h = core_h; rs.core_w = core_w;
-        enc540_.ensure(enc_b * R, s);
-        dec540_.ensure(dec_b * R, s);
-        if (ref_b) refined_.ensure(ref_b * R, s);
-        if (encu_b) encu_.ensure(encu_b * R, s);
-        if (raw_b) raw_.ensure(raw_b * R, s);
-        meta_.ensure(meta_b * R, s);
-        low_a_.ensure(low_b * R, s);
-        low_b_.ensure(low_b * R, s);
-        int launches = 0;
-        struct Ctx { Engine* e; cudaStream_t s; } ctx{this, s};
-        StageMark mark;
-        mark.ctx = &ctx;
-        mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
-        const bool predict = c.mode == Mode::Predict;
-        if (tcr) {
-            launch_tc_controller(tc_route_of(precision_), src, rs, tcw_, enc540_.get(), encu_.get(), low_a_.get(), low_b_.get(),
-                                 dec540_.get(), meta_.get(), predict ? raw_.as<float>() : nullptr,
-                                 flag_.as<int>() + 1, s, &launches, mark);
-        } else {
-            launch_f32_controller(src, rs, stencil_, f32_layers_, enc540_.as<float>(), low_a_.as<float>(),
-                                  low_b_.as<float>(), dec540_.as<float>(), refined_.as<float>(), meta_.as<float>(), s,
-                                  &launches, mark,
-                                  c.mode == Mode::Calibrate ? reinterpret_cast<float*>(stats_.as<double>() + 448) : nullptr,
-                                  c.mode == Mode::Calibrate ? stats_.as<double>() : nullptr);
-        }
-        if (c.mode == Mode::Calibrate) {
-            // activation maxima only
-        } else if (predict) {
-            // one region per frame, covering it: metadata NHWC [h/2, w/2, 64] per frame
-            const size_t bytes = 4 * packed * 64;
-            const char* meta = tcr ? raw_.as<char>() : meta_.as<char>();
-            for (int i = 0; i < R; ++i) {
-                const int f = grp.regions[first + i].frame;
-                char* out = static_cast<char*>(c.host ? dst_.get() : c.dst) + size_t(f) * bytes;
-                AEISU_CUDA(cudaMemcpyAsync(out, meta + size_t(i) * bytes, bytes, cudaMemcpyDeviceToDevice, s));
-            }
-        } else if (tcr) {
-            launch_tc_head(src, rs, dst, meta_.get(), tc_bytes_.as<uint8_t>() + tc_head_off_, flag_.as<int>(),
-                           flag_.as<int>() + 1, s, &launches);
-        } else {
-            launch_f32_head(src, rs, dst, meta_.as<float>(), base_, basis_, flag_.as<int>(), s, &launches);
-        }
-        record(5, s);
-        launches_ += uint64_t(launches);
+        const int R0 = (R + 1) / 2;
+        AEISU_CUDA(cudaEventRecord(fork_, s));
+        AEISU_CUDA(cudaStreamWaitEvent(lane_, fork_, 0));
+        run_regions(c, grp, first, R0, src, dst, s, ws_[0]);
+        run_regions(c, grp, first + R0, R - R0, src, dst, lane_, ws_[1]);
+        AEISU_CUDA(cudaEventRecord(join_, lane_));
+        AEISU_CUDA(cudaStreamWaitEvent(s, join_, 0));
     }
     (void)g;
+}
+
+void Engine::run_regions(const Call& c, const Geometry::Group& grp, size_t first, int R, const SrcDesc& src,
+                         const DstDesc& dst, cudaStream_t s, Workspace& ws) {
+    const int rh = grp.rh, rw = grp.rw;
+    const size_t packed = size_t(rh / 2) * (rw / 2);
+    const bool tcr = precision_ != AEISU_PRECISION_FP32;
+    const RegionBytes rb = region_bytes(precision_, rh, rw, c.mode == Mode::Predict);
+    std::vector<int4> table(2 * size_t(R));
+    int core_h = 0, core_w = 0;
+    for (int i = 0; i < R; ++i) {
+        const Region& r = grp.regions[first + i];
+        table[i] = make_int4(r.frame, r.oy, r.ox, 0);
+        table[R + i] = make_int4(r.cy0, r.cx0, r.cy1, r.cx1);
+        core_h = std::max(core_h, r.cy1 - r.cy0);
+        core_w = std::max(core_w, r.cx1 - r.cx0);
+    }
+    // Region tables are uploaded once per call geometry and kept on the device: an upload
+    // from pageable memory would wait for the stream to drain on every call.
+    const TableKey key{int(c.mode), c.n, c.h, c.w, c.tile, rh * 65536 + rw, int(first), R, c.band, c.bands};
+    auto it = table_cache_.find(key);
+    if (it == table_cache_.end()) {
+        if (table_cache_.size() >= 256) {
+            AEISU_CUDA(cudaDeviceSynchronize());
+            table_cache_.clear();
+        }
+        auto buf = std::make_unique<DevBuf>();
+        buf->ensure(table.size() * sizeof(int4), s);
+        AEISU_CUDA(cudaMemcpy(buf->get(), table.data(), table.size() * sizeof(int4), cudaMemcpyHostToDevice));
+        it = table_cache_.emplace(key, std::move(buf)).first;
+    }
+    RegionSet rs{};
+    rs.regions = it->second->as<int4>();
+    rs.cores = it->second->as<int4>() + R;
+    rs.R = R; rs.rh = rh; rs.rw = rw; rs.core_h = core_h; rs.core_w = core_w;
+    ws.enc540.ensure(rb.enc * R, s);
+    ws.dec540.ensure(rb.dec * R, s);
+    if (rb.ref) ws.refined.ensure(rb.ref * R, s);
+    if (rb.encu) ws.encu.ensure(rb.encu * R, s);
+    if (rb.raw) ws.raw.ensure(rb.raw * R, s);
+    ws.meta.ensure(rb.meta * R, s);
+    ws.low_a.ensure(rb.low * R, s);
+    ws.low_b.ensure(rb.low * R, s);
+    int launches = 0;
+    struct Ctx { Engine* e; cudaStream_t s; } ctx{this, s};
+    StageMark mark;
+    mark.ctx = &ctx;
+    mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
+    const bool predict = c.mode == Mode::Predict;
+    if (tcr) {
+        launch_tc_controller(tc_route_of(precision_), src, rs, tcw_, ws.enc540.get(), ws.encu.get(), ws.low_a.get(),
+                             ws.low_b.get(), ws.dec540.get(), ws.meta.get(), predict ? ws.raw.as<float>() : nullptr,
+                             flag_.as<int>() + 1, s, &launches, mark);
+    } else {
+        launch_f32_controller(src, rs, stencil_, f32_layers_, ws.enc540.as<float>(), ws.low_a.as<float>(),
+                              ws.low_b.as<float>(), ws.dec540.as<float>(), ws.refined.as<float>(), ws.meta.as<float>(), s,
+                              &launches, mark,
+                              c.mode == Mode::Calibrate ? reinterpret_cast<float*>(stats_.as<double>() + 448) : nullptr,
+                              c.mode == Mode::Calibrate ? stats_.as<double>() : nullptr);
+    }
+    if (c.mode == Mode::Calibrate) {
+        // activation maxima only
+    } else if (predict) {
+        // one region per frame, covering it: metadata NHWC [h/2, w/2, 64] per frame
+        const size_t bytes = 4 * packed * 64;
+        const char* meta = tcr ? ws.raw.as<char>() : ws.meta.as<char>();
+        for (int i = 0; i < R; ++i) {
+            const int f = grp.regions[first + i].frame;
+            char* out = static_cast<char*>(c.host ? dst_.get() : c.dst) + size_t(f) * bytes;
+            AEISU_CUDA(cudaMemcpyAsync(out, meta + size_t(i) * bytes, bytes, cudaMemcpyDeviceToDevice, s));
+        }
+    } else if (tcr) {
+        launch_tc_head(src, rs, dst, ws.meta.get(), head_img_, flag_.as<int>(), flag_.as<int>() + 1, s, &launches);
+    } else {
+        launch_f32_head(src, rs, dst, ws.meta.as<float>(), base_, basis_, flag_.as<int>(), s, &launches);
+    }
+    record(5, s);
+    launches_ += uint64_t(launches);
 }
 
 // Host-buffer upscale of several frames from and to page-locked memory: frames go through in

@@ -88,9 +88,21 @@ struct Call {
     int band = 0, bands = 0;        // bands > 0: one row band of a single frame (plan_band)
 };
 
+// Device copies of one model's weights.  Sibling engines (aeisu_open_sibling) share one copy;
+// it is released with the last of them.
+struct ResidentWeights {
+    DevBuf w_f32;                // all FP32 tensors, packed
+    DevBuf tc_bytes, tc_floats;  // tensor-core routes: operand images, epilogue vectors
+};
+
 class Engine {
 public:
     Engine(HostModel model, int precision, int device);
+    // A sibling of `parent`: same model, precision and device, sharing its device weights, with
+    // its own stream, workspace, status flags and timings (SrcPyrCudaRuntime.cu:5392-5402 shares
+    // the engine; here only the weights are shared, so siblings may run concurrently).
+    struct Sibling {};
+    Engine(const Engine& parent, Sibling);
     ~Engine();
     Engine(const Engine&) = delete;
     Engine& operator=(const Engine&) = delete;
@@ -127,7 +139,7 @@ public:
         cudaStream_t stream;
     };
     Resident resident() const {
-        return {&tcw_, tc_bytes_.as<uint8_t>() + tc_head_off_, stencil_, f32_layers_, base_, basis_,
+        return {&tcw_, head_img_, stencil_, f32_layers_, base_, basis_,
                 flag_.as<int>(), stream_};
     }
     void count_launches(int n) { launches_ += uint64_t(n); }
@@ -135,8 +147,17 @@ public:
 private:
     struct DeviceGuard;
     void upload_weights();
+    void create_streams();
+    // Intermediate activations of one batch of regions.  Large batches run as two halves on two
+    // streams at once (the compute stream and lane_), each with its own workspace: the two
+    // halves' kernels fill each other's tails and waits.
+    struct Workspace {
+        DevBuf enc540, low_a, low_b, dec540, refined, meta, encu, raw;
+    };
     void run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
                    const DstDesc& dst, cudaStream_t s);
+    void run_regions(const Call& c, const Geometry::Group& grp, size_t first, int R, const SrcDesc& src,
+                     const DstDesc& dst, cudaStream_t s, Workspace& ws);
     void run_pipelined(const Call& c, cudaStream_t s);
     void finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t dst_bytes);
     void wait(cudaStream_t s, double timeout_ms);
@@ -152,28 +173,30 @@ private:
     uint64_t launches_ = 0;
     aeisu_timings timings_{};
 
-    // resident weights
+    // resident weights (shared with siblings) and the pointers into them
     DevBuf stats_;               // calibration: channel sums (double[448]) then maxima (float[10])
-    DevBuf w_f32_;               // all FP32 tensors, packed
+    std::shared_ptr<ResidentWeights> weights_;
     const float* stencil_ = nullptr;
     const float* base_ = nullptr;
     const float* basis_ = nullptr;
     F32Layer f32_layers_[kLayerCount]{};
-    DevBuf tc_bytes_, tc_floats_;  // tensor-core routes: operand images, epilogue vectors
     TcWeights tcw_{};
-    size_t tc_head_off_ = 0;
+    const uint8_t* head_img_ = nullptr;
 
     // planned geometry per call shape (mode, n, h, w, tile, band, bands)
     std::map<std::array<int, 7>, Geometry> plan_cache_;
     const Geometry& plan(const Call& c);
-    // region tables per call geometry (mode, n, h, w, tile, group shape, first region, band, bands)
-    using TableKey = std::array<int, 9>;
+    // region tables per call geometry (mode, n, h, w, tile, group shape, first region, regions,
+    // band, bands)
+    using TableKey = std::array<int, 10>;
     std::map<TableKey, std::unique_ptr<DevBuf>> table_cache_;
 
     // workspace
     DevBuf src_, dst_, tables_, flag_;
     HostBuf staging_;
-    DevBuf enc540_, low_a_, low_b_, dec540_, refined_, meta_, encu_, raw_;
+    Workspace ws_[2];
+    cudaStream_t lane_ = nullptr;                     // second stream of a split batch
+    cudaEvent_t fork_ = nullptr, join_ = nullptr;
     size_t workspace_cap_ = size_t(6) << 30;
 
     // timing events: [0] call start, [1]/[2] detailed stage marks, [6] call end, [7] waits

@@ -202,6 +202,14 @@ class Model:
         _lib.check(_lib.lib().aeisu_open_int8(C.byref(st), dev, C.byref(h)))
         return cls(h, dev, "int8")
 
+    def sibling(self):
+        """Another handle on the same model and GPU sharing this one's device weights, with its
+        own stream and workspace (aeisu_open_sibling; CudaRuntime::CreateSibling,
+        SrcPyrCudaRuntime.cu:5392-5402): one handle per host thread, one weight copy."""
+        h = C.c_void_p()
+        _lib.check(_lib.lib().aeisu_open_sibling(self._handle(), C.byref(h)))
+        return type(self)(h, self.device_index, self.precision, self.basis_l1_scale)
+
     def close(self):
         if getattr(self, "_h", None):
             _lib.lib().aeisu_close(self._h)

@@ -3,8 +3,7 @@
  *
  * One handle = one model resident on one GPU (weights, packed operand layouts,
  * workspace, CUDA stream).  Calls on one handle are not thread-safe; use one handle
- * per host thread (handles opened from the same artifact on the same device are
- * independent, like the reference's sibling slots).  The caller owns every I/O
+ * per host thread: aeisu_open_sibling gives another handle that shares the weights.  The caller owns every I/O
  * buffer; the library owns weights and workspace.  Every entry point returns an
  * aeisu_status (never throws); aeisu_last_error() gives the calling thread's last
  * message.
@@ -135,6 +134,14 @@ typedef struct aeisu_int8_artifact {
  * AEISU_PRECISION_INT8.  AEISU_ERR_BAD_ARTIFACT for a missing array, a non-finite value, a
  * non-positive scale or a weight code outside [-127, 127]. */
 int aeisu_open_int8(const aeisu_int8_artifact* artifact, int device, aeisu_t** out);
+
+/* A sibling of `handle`, like CudaRuntime::CreateSibling (SrcPyrCudaRuntime.cu:5392-5402): the
+ * same model, precision and GPU, sharing the handle's device weights (one copy per model and
+ * device, released with the last handle that shares it), with its own CUDA stream, workspace,
+ * status flags and timings.  Unlike the reference's siblings, which share one engine and stream,
+ * siblings may run on different host threads at the same time; each handle is still used by one
+ * thread at a time.  Closing the original handle first is allowed. */
+int aeisu_open_sibling(aeisu_t* handle, aeisu_t** out);
 
 void aeisu_close(aeisu_t* handle);
 
@@ -320,7 +327,7 @@ int aeisu_set_workspace_limit(aeisu_t* handle, uint64_t bytes);
  * CudaRuntime::StartupReport (SrcPyrCudaRuntime.cu:3739-3783).  Valid until close. */
 const char* aeisu_report(aeisu_t* handle);
 
-/* Bytes of device memory the handle holds (weights + workspace). */
+/* Bytes of device memory the handle holds (weights, shared ones included, + workspace). */
 uint64_t aeisu_device_bytes(aeisu_t* handle);
 
 /* Number of kernels the library launched on this handle since it was opened. */
