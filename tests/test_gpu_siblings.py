@@ -68,3 +68,4 @@ def test_siblings_run_concurrently_on_their_own_threads():
     finally:
         for h in handles:
             h.close()
+
