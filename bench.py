@@ -625,6 +625,18 @@ def cpu_baseline(frames_u8, ckpt, tile, seconds=12.0):
                       f"port of aeisu.runtime.upscale, {dt:.1f} s"}
 
 
+def arm_config(workload, wl, precision, world):
+    """The `config` of a bench line: the same dict on both arms (the reference arm samples
+    this workload; its sampling is stated in its cpu_baseline.sample)."""
+    n, h, w, tile, _, ckpt, _ = wl
+    band = workload in BAND_WORKLOADS
+    return {"workload": workload, "frames_per_step_per_gpu": n, "frame": f"{w}x{h}",
+            "output": f"{2 * w}x{2 * h}", "tile": tile, "precision": precision, "checkpoint": ckpt,
+            "l2": "inputs+outputs per step exceed the 126 MB L2; no flush needed",
+            "parallelism": (f"row bands x{world} (32-row halos recomputed, no exchange)" if band
+                            else f"frame-parallel x{world}")}
+
+
 def run_reference(args, wl):
     rank, _, world = dist_env()
     if rank != 0:
@@ -644,13 +656,15 @@ def run_reference(args, wl):
     line = {
         "impl": "reference", "metric": "2x output Mpix/s per B200 (FP8 mixed) frame-parallel; whole-job aggregate",
         "value": value, "unit": "output Mpix/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded procedural scenes)",
-        "config": {"workload": args.workload, "frames_per_step": threads, "frame": f"{w}x{h}", "tile": tile,
-                   "checkpoint": ckpt, "sample": f"{threads} of the workload's {n} frames per step"},
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if args.workload in BAND_WORKLOADS else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded procedural scenes, 2x2 area / bicubic degradation)",
+        "config": arm_config(args.workload, wl, args.precision or precision, world),
         "cpu_baseline": {"value": value, "unit": "output Mpix/s", "cores": threads, "kind": "port",
-                         "sample": f"{threads} frames of {w}x{h} per step, one per host thread, FP32 numpy "
-                                   f"port of aeisu.runtime.upscale"},
+                         "sample": f"{threads} of the workload's {n} frames of {w}x{h} per step (a bounded sample), "
+                                   f"one per host thread, through the FP32 numpy port of aeisu.runtime.upscale "
+                                   f"(the reference's CPU path has FP32 arithmetic only; within 3% of its torch "
+                                   f"path on the build container), on rank 0 only"},
         "e2e": {"value": value, "unit": "output Mpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -850,11 +864,7 @@ def main():
             "scaling": "strong" if band else "weak",
             "vs_baseline": None, "dtype": {"fp32": "f32", "fp16": "f16", "mixed": "e4m3+f16", "int8": "s8 codes as f16+f16"}[precision],
             "data": "synthetic (seeded procedural scenes, 2x2 area / bicubic degradation)",
-            "config": {"workload": args.workload, "frames_per_step_per_gpu": n, "frame": f"{w}x{h}",
-                       "output": f"{2 * w}x{2 * h}", "tile": tile, "precision": precision, "checkpoint": ckpt,
-                       "l2": "inputs+outputs per step exceed the 126 MB L2; no flush needed",
-                       "parallelism": (f"row bands x{world} (32-row halos recomputed, no exchange)" if band
-                                       else f"frame-parallel x{world}")},
+            "config": arm_config(args.workload, wl, precision, world),
             "stage_ms": stage_ms,
             "roofline": roof,
             "cpu_baseline": cpu,
