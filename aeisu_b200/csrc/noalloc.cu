@@ -23,8 +23,9 @@
 //    from different handles on one device -- race on it.  Serialise them.
 //  * The first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current), and the first launch of each kernel on
-//    a device may set its shared-memory attribute and add an entry to the host-side cache of
-//    those attributes; make that first call before capturing a CUDA graph on the stream.  No
+//    a device may set its shared-memory attribute and add entries to the host-side caches of
+//    those attributes and of the TMA tensor maps over the array (one per shape); make that
+//    first call before capturing a CUDA graph on the stream.  No
 //    device memory is ever allocated.  The address is cached for the life of the process:
 //    after cudaDeviceReset it is stale, so the library must not outlive a reset of the device.
 #include <cuda_runtime.h>

@@ -1,7 +1,7 @@
 // Upscale into caller-provided device buffers using only the library's static scratch array
-// (no device allocation; the first call per device and kernel may fill small host-side caches
-// of the array's address and of kernel attributes); see noalloc.cu for the limits and the
-// sharing rules.
+// (no device allocation; the first call per device and shape may fill small host-side caches
+// of the array's address, kernel attributes and tensor maps); see noalloc.cu for the limits and
+// the sharing rules.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -181,8 +181,9 @@ int aeisu_upscale_u8_band(aeisu_t* handle, const uint8_t* src, int h, int w, int
  * AEISU_ERR_INVALID_ARG; batches run in as many passes of whole frames as the array needs.
  * The array is shared and keeps the previous call's contents: calls whose GPU work overlaps
  * in time race and must be serialised.  The first call on a device looks up the array's
- * address, and the first call on a device and shape may set kernel attributes and add an
- * entry to a small host-side cache of them; make that first call before any stream capture.
+ * address, and the first call on a device and shape may set kernel attributes and add entries
+ * to small host-side caches (kernel attributes, TMA tensor maps of the scratch array); make
+ * that first call before any stream capture.
  * The cached address is not refreshed after cudaDeviceReset: a handle and this entry point
  * must not outlive a reset of their device.  Non-finite outputs are reported by
  * aeisu_synchronize. */
