@@ -75,6 +75,10 @@ _SIGNATURES = {
     "aeisu_png_encode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint, C.c_int,
                                    C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
     "aeisu_png_bound": (C.c_uint64, [C.c_int, C.c_int]),
+    "aeisu_png_info": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                 C.POINTER(C.c_int)]),
+    "aeisu_png_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint,
+                                   C.c_int, C.c_void_p, C.c_void_p]),
     "aeisu_reconstruct_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "aeisu_reconstruct_backward_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,

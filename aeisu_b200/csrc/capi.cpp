@@ -230,6 +230,26 @@ int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned
     });
 }
 
+int aeisu_png_info(const uint8_t* file, uint64_t bytes, int* h, int* w, int* color_type) {
+    return guarded([&] {
+        aeisu::require(h && w && color_type, "output pointers are null");
+        const aeisu::PngFileInfo info = aeisu::png_parse(file, size_t(bytes), nullptr);
+        aeisu::png_check_supported(info);
+        *h = info.h;
+        *w = info.w;
+        *color_type = info.color;
+    });
+}
+
+int aeisu_png_decode(const uint8_t* files, const uint64_t* offsets, const uint64_t* sizes, int n, int h, int w,
+                     unsigned flags, int device, uint8_t* out, void* stream) {
+    return guarded([&] {
+        aeisu::require(flags == AEISU_IO_HOST || flags == AEISU_IO_DEVICE, "unknown I/O flags");
+        aeisu::png_decode(files, offsets, sizes, n, h, w, flags == AEISU_IO_HOST, device, out,
+                          static_cast<cudaStream_t>(stream));
+    });
+}
+
 int aeisu_reconstruct_f32(const float* source, const float* metadata, const float* base, const float* basis, int n,
                           int h, int w, int trim, int device, float* out, void* stream) {
     return guarded([&] {

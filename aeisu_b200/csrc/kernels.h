@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "../../include/aeisu.h"
 
@@ -122,6 +123,21 @@ double tensor_peak_tflops(int device, int kind, int ctas_per_sm, int mmas, int r
 void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, int device, uint8_t* out,
                 uint64_t capacity, uint64_t* sizes, cudaStream_t stream);
 int png_launches_per_call();
+
+// PNG ingress (k_pngdec.cu): the header facts of one file and, when `stream` is given, its zlib
+// stream (the IDAT payloads concatenated); every chunk's CRC is checked.
+struct PngFileInfo {
+    int w, h, depth, color, interlace, npal;
+    uint8_t palette[768];
+    unsigned long long idat_bytes;
+};
+PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<uint8_t>* stream);
+// AEISU_ERR_UNSUPPORTED unless 8-bit samples, colour type 0/2/3/4/6, no interlacing.
+void png_check_supported(const PngFileInfo& info);
+// n PNG files (host memory) of one size h x w -> n uint8 RGB frames h x w x 3 in `out` (host or
+// device memory); waits for completion.
+void png_decode(const uint8_t* data, const uint64_t* offsets, const uint64_t* sizes, int n, int h, int w,
+                bool host_out, int device, uint8_t* out, cudaStream_t stream);
 
 // reconstruct() of aeisu/reconstruction.py:29-83 on caller-given metadata, base and basis, FP32,
 // and its backward (k_recon.cu).  Device pointers; both only enqueue on `stream`.

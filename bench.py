@@ -457,6 +457,53 @@ def measure_png(out_u8, frames):
                       f"{runs} calls after 2 warm-up calls"}
 
 
+def measure_png_ingress(frames_u8, count):
+    """PNG ingress (aeisu_png_decode): `count` of the step's input frames, encoded by PIL as
+    save_rgb writes them (zlib level 6), decoded per call from host memory (the upload inside the
+    timed region) into a host array reused across calls (the download inside the timed region)
+    and, beside it, into a CUDA tensor (frames left on the GPU for the upscaler); beside both
+    read_rgb's decoder (PIL open + convert("RGB")) on a few of the same files, one core."""
+    import io
+    import torch
+    from PIL import Image
+    from aeisu_b200 import codec
+    m = min(count, frames_u8.shape[0])
+    files = []
+    for i in range(m):
+        buf = io.BytesIO()
+        Image.fromarray(frames_u8[i]).save(buf, format="PNG")
+        files.append(buf.getvalue())
+    host = codec.decode_png(files)
+    exact = bool(np.array_equal(host, frames_u8[:m]))
+    dev = codec.decode_png(files, out="device")
+    torch.cuda.synchronize()
+    runs = 3
+    t0 = time.perf_counter()
+    for _ in range(runs):
+        codec.decode_png(files, out=host)
+    dt = (time.perf_counter() - t0) / runs
+    t0 = time.perf_counter()
+    for _ in range(runs):
+        codec.decode_png(files, out=dev)
+    torch.cuda.synchronize()
+    dt_dev = (time.perf_counter() - t0) / runs
+    _, H, W, _ = frames_u8.shape
+    sample = min(4, m)
+    c0 = time.perf_counter()
+    for i in range(sample):
+        with Image.open(io.BytesIO(files[i])) as im:
+            np.asarray(im.convert("RGB"))
+    pil_s = (time.perf_counter() - c0) / sample
+    return {"value": m / dt, "unit": "frames/s decoded", "ms_per_call": dt * 1e3, "frames_per_call": m,
+            "to_device": {"value": m / dt_dev, "unit": "frames/s decoded", "ms_per_call": dt_dev * 1e3},
+            "frame": f"{W}x{H}", "bytes_per_file": sum(len(f) for f in files) / m, "pixels_equal_input": exact,
+            "cpu_reference": {"value": 1.0 / pil_s, "unit": "frames/s decoded", "cores": 1, "kind": "reference",
+                              "sample": f"PIL open + convert('RGB') of {sample} of the same files (read_rgb's decoder)"},
+            "config": "PIL-written files (save_rgb's encoder, zlib level 6) in host memory, pixels into a host array "
+                      f"reused across calls (to_device: into a CUDA tensor); wall clock over {runs} calls after 1 "
+                      "warm-up call"}
+
+
 def measure_train(dev, batch, sm_mhz=None):
     """Training reconstruction (aeisu_reconstruct_f32 + aeisu_reconstruct_backward_f32 through the
     autograd drop-in aeisu_b200.reconstruction.reconstruct) at the reference recipe's shape
@@ -684,6 +731,8 @@ def main():
                     help="1080p->4K single-frame latency runs (0 disables)")
     ap.add_argument("--png-frames", type=int, default=8,
                     help="frames per call of the PNG egress measurement (0 disables)")
+    ap.add_argument("--png-decode-frames", type=int, default=64,
+                    help="files per call of the PNG ingress measurement (0 disables)")
     ap.add_argument("--metric-pairs", type=int, default=8,
                     help="image pairs per call of the evaluation-metrics measurement (0 disables)")
     ap.add_argument("--train-batch", type=int, default=32,
@@ -779,6 +828,8 @@ def main():
     metric_line = (measure_metrics(dev, out, args.metric_pairs)
                    if (rank == 0 and args.metric_pairs > 0 and not band) else None)
     png_line = measure_png(out, args.png_frames) if (rank == 0 and args.png_frames > 0 and not band) else None
+    png_in_line = (measure_png_ingress(frames, args.png_decode_frames)
+                   if (rank == 0 and args.png_decode_frames > 0 and not band) else None)
     train_line = (measure_train(dev, args.train_batch, clocks.summary().get("sm_mhz"))
                   if (rank == 0 and args.train_batch > 0 and not band) else None)
 
@@ -880,6 +931,7 @@ def main():
             "latency_1080p": latency,
             "evaluation_metrics": metric_line,
             "png_egress": png_line,
+            "png_ingress": png_in_line,
             "reconstruct_train": train_line,
             "clocks": clocks.summary(),
             "report": model.report,

@@ -258,6 +258,32 @@ int aeisu_png_encode(const void* frames, int kind, int n, int h, int w, unsigned
 /* Largest PNG file aeisu_png_encode can produce for one h x w frame (0 for an empty size). */
 uint64_t aeisu_png_bound(int h, int w);
 
+/* PNG ingress, host side only: checks one PNG file in host memory as PIL's PngImagePlugin does
+ * (signature, chunk layout, the CRC of every chunk before the image data, IHDR, PLTE) and
+ * returns its size and colour type.  AEISU_ERR_UNSUPPORTED for
+ * what aeisu_png_decode does not take (bit depths other than 8, interlaced files);
+ * AEISU_ERR_INVALID_ARG for a broken file (PIL's PngImagePlugin raises for the same). */
+int aeisu_png_info(const uint8_t* file, uint64_t bytes, int* h, int* w, int* color_type);
+
+/* PNG ingress on the GPU: the decode of read_rgb (aeisu/runtime.py:17-20: PIL open, convert("RGB"),
+ * uint8 HWC) for n PNG files at once.  The files lie back to back or anywhere in host memory
+ * (file i at files + offsets[i], sizes[i] bytes) and must all be h x w; 8-bit samples of colour
+ * type 0 (grey), 2 (RGB), 3 (palette), 4 (grey + alpha) or 6 (RGBA), not interlaced.  out
+ * receives n frames of h x w x 3 uint8 RGB (HWC), in host or device memory on GPU `device`
+ * (flags AEISU_IO_HOST / AEISU_IO_DEVICE); grey is replicated, palettes looked up and alpha
+ * dropped, as convert("RGB") does, so the pixels equal PIL's.  The chunks are parsed and
+ * CRC-checked on the host as PIL checks them (the chunks before the image data); on the GPU one
+ * CTA per file: a warp inflates its zlib stream (deflate is sequential within a stream: the
+ * parallelism is across files) while a second warp undoes the scanline filters of each group of
+ * 32 rows already inflated, converts to RGB and checks the stream's Adler-32.  What PIL
+ * tolerates is tolerated (image data past the image, a missing Adler-32 trailer, bad CRCs from
+ * the first IDAT chunk on).  Waits for completion.  AEISU_ERR_INVALID_ARG for a broken or
+ * differently sized file (the message names it), AEISU_ERR_UNSUPPORTED as for aeisu_png_info.  Keeps its device buffers between calls (per
+ * device, grow-only; calls on one device take turns); like the no-allocation entry point's
+ * cache, they do not survive cudaDeviceReset. */
+int aeisu_png_decode(const uint8_t* files, const uint64_t* offsets, const uint64_t* sizes, int n, int h, int w,
+                     unsigned flags, int device, uint8_t* out, void* stream);
+
 /* reconstruct() of aeisu/reconstruction.py:29-83 as a standalone FP32 operator (the function
  * train.py:99-103 differentiates), no model handle needed.  All pointers are device memory on
  * GPU `device`, contiguous float32: source [n][3][h][w], metadata [n][64][h/2][w/2] (channel
