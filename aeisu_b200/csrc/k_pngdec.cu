@@ -244,6 +244,7 @@ struct Window {
     const uint8_t* mod;   // mod[32 * d + lane] = lane % d for 1 <= d < 32
     Handoff* ho;          // progress, published after every flush
     unsigned produced, flushed, limit;
+    unsigned next;        // the next event: min(flushed + kFlush, limit)
     __device__ void flush(unsigned upto, int lane) {
         __syncwarp();
         // loops with the same trip count on every lane (the body predicated), so the warp
@@ -258,17 +259,22 @@ struct Window {
             if (i < upto) out[i] = win[i & kWinMask];
         }
         flushed = upto;
+        next = min(flushed + unsigned(kFlush), limit);
         __threadfence_block();   // this lane's stores, before the progress the other warp reads
         __syncwarp();
         if (lane == 0) *reinterpret_cast<volatile unsigned*>(&ho->flushed) = upto;
     }
-    __device__ __forceinline__ void advance(unsigned n, int lane) {
+    // Adds n bytes; true when the image is complete (produced == limit).  One compare against
+    // `next` in the common case.
+    __device__ __forceinline__ bool advance(unsigned n, int lane) {
         produced += n;
+        if (produced < next) return false;
         if (produced - flushed >= unsigned(kFlush)) flush(produced & ~unsigned(kFlush - 1), lane);
+        return produced == limit;
     }
-    __device__ __forceinline__ void literal(uint32_t v, int lane) {   // the caller keeps produced < limit
+    __device__ __forceinline__ bool literal(uint32_t v, int lane) {   // the caller keeps produced < limit
         if (lane == 0) win[produced & kWinMask] = uint8_t(v);
-        advance(1, lane);
+        return advance(1, lane);
     }
     // n bytes from d back (1 <= d <= produced, d <= 32 KiB); the caller keeps produced + n <= limit.
     // Byte k of the copy equals byte k % d of the source.  d >= n: every source byte exists
@@ -301,7 +307,6 @@ struct Window {
             }
         }
         __syncwarp();
-        advance(unsigned(n), lane);
     }
 };
 
@@ -311,7 +316,7 @@ constexpr int kInflateSmem = kWin + 2 * int(sizeof(Huff)) + 320 + 2 * kMaxLitLen
 // inflated; a stream that would inflate more stops there (the rest is not read, its Adler-32 not
 // checked); a stream whose last block ends exactly at the image is checked against its Adler-32
 // trailer when the trailer is present, and taken without a check when the stream ends before it
-// (or before its last block, once the image is complete).
+// (or before its last block, or inside a block header, once the image is complete).
 // The whole warp runs one file's decode in lockstep: every lane decodes the same symbols (the
 // table lookups broadcast), and the lanes share the byte work (match copies, stored blocks,
 // flushes, table fills).
@@ -329,7 +334,7 @@ __device__ void inflate_file(const uint8_t* __restrict__ in, const DecFile& fd, 
     const uint8_t* src = in + fd.in_off;
     const uint32_t* words = reinterpret_cast<const uint32_t*>(src);
     BitReader br{words, words, words + (fd.in_len + 3) / 4, 0ull, 0};
-    Window wo{win, scratch + fd.out_off, mod, ho, 0u, 0u, expect};
+    Window wo{win, scratch + fd.out_off, mod, ho, 0u, 0u, expect, min(unsigned(kFlush), expect)};
     int err = kDecOk;
     bool last = false, more = false;   // more: the stream holds data past the image
     long long full_bits = -1;          // bits consumed when the image became complete
@@ -412,17 +417,16 @@ __device__ void inflate_file(const uint8_t* __restrict__ in, const DecFile& fd, 
                 break;
             }
         }
-        for (;;) {   // the block's symbols
+        bool complete = wo.produced == wo.limit, ended = false;
+        while (!complete) {   // the block's symbols, until its end or the image's
             if (br.cnt < 32) br.refill();   // a literal/length code and its extra bits: <= 20 bits
             const uint32_t e = huff_decode(br, lit, kLitLen);
             const uint32_t kind = e & kKindMask;
             if (kind == kLiteral) {
-                if (wo.produced == wo.limit) { more = true; break; }
-                wo.literal(e >> 16, lane);
-                if (wo.produced == wo.limit) full_bits = br.consumed();
+                complete = wo.literal(e >> 16, lane);
                 continue;
             }
-            if (kind == kEnd) break;
+            if (kind == kEnd) { ended = true; break; }
             if (kind == 0) { err = kDecBadCode; break; }
             const int lx = int((e >> 5) & 15);
             const int len = int(e >> 16) + int(br.peek() & ((1u << lx) - 1));
@@ -434,16 +438,37 @@ __device__ void inflate_file(const uint8_t* __restrict__ in, const DecFile& fd, 
             const int d = int(de >> 16) + int(br.peek() & ((1u << dx) - 1));
             br.skip(dx);
             if (unsigned(d) > wo.produced) { err = kDecBadDistance; break; }   // d <= 32768 always
-            if (wo.produced == wo.limit) { more = true; break; }
             const unsigned room = wo.limit - wo.produced;
             const int copy = room < unsigned(len) ? int(room) : len;
             wo.match(copy, d, lane);
-            if (wo.produced == wo.limit) full_bits = br.consumed();
-            if (copy < len) { more = true; break; }
+            complete = wo.advance(unsigned(copy), lane);
+            if (copy < len) more = true;
+        }
+        if (complete && err == kDecOk) {
+            if (full_bits < 0) full_bits = br.consumed();   // the bits that completed the image
+            // past the image, as zlib reads on: the block's end, or data the image has no room for
+            while (!ended && !more) {
+                if (br.cnt < 32) br.refill();
+                const uint32_t e = huff_decode(br, lit, kLitLen);
+                const uint32_t kind = e & kKindMask;
+                if (kind == kEnd) ended = true;
+                else if (kind == kLiteral) more = true;
+                else if (kind == 0) { err = kDecBadCode; break; }
+                else {   // a match: zlib decodes its distance code, then stops for want of room
+                    br.skip(int((e >> 5) & 15));   // (before its distance-too-far check)
+                    if (br.cnt < 28) br.refill();
+                    if (!(huff_decode(br, dist, kDistance) & kKindMask)) { err = kDecBadCode; break; }
+                    more = true;
+                }
+            }
         }
         if (!more && err == kDecOk && wo.produced < wo.limit && br.consumed() > avail) err = kDecTruncated;
     }
     wo.flush(wo.produced, lane);
+    // zlib waits for more input where a field runs past the stream's end: once the image is
+    // complete, an error found only in the zero bits past the end is no error
+    if (err != kDecOk && wo.produced == expect && full_bits >= 0 && full_bits <= avail && br.consumed() > avail)
+        err = kDecOk;
     unsigned int stored = 0;
     int check = 0;
     if (err == kDecOk) {

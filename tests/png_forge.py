@@ -114,23 +114,47 @@ def zlib_wrap(deflate: bytes, adler_of: bytes | None = None) -> bytes:
     return out if adler_of is None else out + struct.pack(">I", zlib.adler32(adler_of) & 0xFFFFFFFF)
 
 
-def fixed_block(symbols, final=True) -> BitWriter:
-    """A fixed-Huffman block of literal bytes and (length, distance) pairs, lengths 3..10 and
-    distances 1..4 only (no extra bits), ended by the end-of-block code."""
+LEN_BASE = [3, 4, 5, 6, 7, 8, 9, 10, 11, 13, 15, 17, 19, 23, 27, 31, 35, 43, 51, 59, 67, 83, 99, 115, 131,
+            163, 195, 227, 258]
+LEN_EXTRA = [0] * 8 + [1] * 4 + [2] * 4 + [3] * 4 + [4] * 4 + [5] * 4 + [0]
+DIST_BASE = [1, 2, 3, 4, 5, 7, 9, 13, 17, 25, 33, 49, 65, 97, 129, 193, 257, 385, 513, 769, 1025, 1537, 2049,
+             3073, 4097, 6145, 8193, 12289, 16385, 24577]
+DIST_EXTRA = [0, 0, 0, 0] + [k // 2 for k in range(2, 28)]
+
+
+def _fixed_litlen(bw, sym):
+    if sym < 144:
+        bw.code(0x30 + sym, 8)
+    elif sym < 256:
+        bw.code(0x190 + sym - 144, 9)
+    elif sym < 280:
+        bw.code(sym - 256, 7)
+    else:
+        bw.code(0xC0 + sym - 280, 8)
+
+
+def fixed_block(symbols, final=True, end=True) -> BitWriter:
+    """A fixed-Huffman block (RFC 1951 3.2.6) of literal bytes, (length, distance) pairs with
+    their extra bits, and raw symbol numbers given as ("sym", n) (e.g. the never-valid 286);
+    ended by the end-of-block code unless end is False."""
     bw = BitWriter()
     bw.field(1 if final else 0, 1)
     bw.field(1, 2)
     for s in symbols:
-        if isinstance(s, tuple):
+        if isinstance(s, tuple) and s[0] == "sym":
+            _fixed_litlen(bw, s[1])
+        elif isinstance(s, tuple):
             length, dist = s
-            assert 3 <= length <= 10 and 1 <= dist <= 4
-            bw.code(length - 3 + 1, 7)          # symbols 257..264: 7-bit codes 1..8
-            bw.code(dist - 1, 5)
-        elif s < 144:
-            bw.code(0x30 + s, 8)
+            i = max(k for k in range(29) if LEN_BASE[k] <= length)
+            _fixed_litlen(bw, 257 + i)
+            bw.field(length - LEN_BASE[i], LEN_EXTRA[i])
+            j = max(k for k in range(30) if DIST_BASE[k] <= dist)
+            bw.code(j, 5)
+            bw.field(dist - DIST_BASE[j], DIST_EXTRA[j])
         else:
-            bw.code(0x190 + s - 144, 9)
-    bw.code(0, 7)                               # 256, end of block
+            _fixed_litlen(bw, s)
+    if end:
+        _fixed_litlen(bw, 256)
     return bw
 
 

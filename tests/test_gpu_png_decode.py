@@ -209,3 +209,41 @@ def test_reused_outputs_and_growing_batches():
         np.testing.assert_array_equal(got, want_big)
     for got in results[1]:
         np.testing.assert_array_equal(got, np.stack(small))
+
+
+def tiny_streams():
+    """(name, stream) for a 1x2 RGB image (7 inflated bytes) built symbol by symbol: what comes
+    after the image's last byte, and errors inside it."""
+    samples = np.array([[[1, 2, 3], [4, 5, 6]]], np.uint8)
+    raw = pf.raw_stream(samples)
+    yield "past: literal", pf.zlib_wrap(pf.fixed_block(list(raw) + [9]).data(), raw)
+    yield "past: match too far back", pf.zlib_wrap(pf.fixed_block(list(raw) + [(3, 100)]).data(), raw)
+    yield "past: invalid symbol 286", pf.zlib_wrap(pf.fixed_block(list(raw) + [("sym", 286)]).data(), raw)
+    yield "past: no end of block", pf.zlib_wrap(pf.fixed_block(list(raw), end=False).data())
+    yield "past: non-final block, then nothing", pf.zlib_wrap(pf.fixed_block(list(raw), final=False).data())
+    bw = pf.fixed_block(list(raw), end=False)
+    pf._fixed_litlen(bw, 257)
+    bw.code(30, 5)   # distance code 30 never occurs
+    yield "past: distance code 30", pf.zlib_wrap(bw.data(), raw)
+    # after a non-final block: a stored block whose LEN and NLEN disagree, all inside the stream
+    yield "past: bad stored lengths", pf.zlib_wrap(pf.fixed_block(list(raw), final=False).data() +
+                                                   b"\x01\x00\x00\x00" + bytes(8))
+    bw = pf.fixed_block(list(raw[:-1]), end=False)
+    pf._fixed_litlen(bw, 257)
+    bw.code(30, 5)
+    yield "inside: distance code 30", pf.zlib_wrap(bw.data(), raw)
+    yield "inside: match too far back", pf.zlib_wrap(pf.fixed_block(list(raw[:3]) + [(4, 100)]).data(), raw)
+    # a non-final stored block of 3 bytes (header byte, LEN 3, NLEN), then a fixed final block
+    yield "inside: two blocks", pf.zlib_wrap(b"\x00\x03\x00\xfc\xff" + raw[:3] + pf.fixed_block(list(raw[3:])).data(), raw)
+
+
+@pytest.mark.parametrize("name", [n for n, _ in tiny_streams()])
+def test_symbols_around_the_image_end_like_zlib(name):
+    samples = np.array([[[1, 2, 3], [4, 5, 6]]], np.uint8)
+    stream = next(s for n, s in tiny_streams() if n == name)
+    data = pf.make_png(samples, 2, filters=[0], stream=stream)
+    if pil_refuses(data):
+        with pytest.raises(ValueError):
+            codec.decode_png(data)
+    else:
+        check(data)
