@@ -788,13 +788,13 @@ uint32_t be32(const uint8_t* p) { return uint32_t(p[0]) << 24 | uint32_t(p[1]) <
 // the image data is the run of consecutive IDAT chunks from there, taken without their CRCs
 // (PIL does not check them; the zlib stream's Adler-32 covers the data), the last one possibly
 // cut short by the end of the file; nothing after the run is read.
-PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<uint8_t>* stream) {
+PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<std::pair<size_t, size_t>>* idat) {
     static const uint8_t sig[8] = {0x89, 'P', 'N', 'G', '\r', '\n', 0x1A, '\n'};
     require(data != nullptr && size >= 8 && std::memcmp(data, sig, 8) == 0, "not a PNG file (signature)");
     PngFileInfo info{};
     size_t at = 8;
     bool ihdr = false;
-    if (stream) stream->clear();
+    if (idat) idat->clear();
     for (;;) {
         require(size - at >= 12, "truncated PNG file (no image data)");
         const uint32_t len = be32(data + at);
@@ -828,7 +828,7 @@ PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<uint8_t>* st
     while (size - at >= 8 && std::memcmp(data + at + 4, "IDAT", 4) == 0) {
         const size_t len = be32(data + at);
         const size_t take = std::min(len, size - at - 8);
-        if (stream) stream->insert(stream->end(), data + at + 8, data + at + 8 + take);
+        if (idat && take) idat->emplace_back(at + 8, take);
         info.idat_bytes += take;
         if (len + 12 > size - at) break;
         at += len + 12;
@@ -860,6 +860,19 @@ struct DecodeCache {
     std::mutex m;
     void* p[kCount] = {};
     size_t cap[kCount] = {};
+    void* host = nullptr;   // page-locked staging of the zlib streams
+    size_t host_cap = 0;
+    uint8_t* get_host(size_t bytes) {
+        if (host_cap < bytes) {
+            if (host) cudaFreeHost(host);
+            host = nullptr;
+            host_cap = 0;
+            const size_t want = bytes + bytes / 4;
+            AEISU_CUDA(cudaHostAlloc(&host, want, cudaHostAllocDefault));
+            host_cap = want;
+        }
+        return static_cast<uint8_t*>(host);
+    }
     void* get(int k, size_t bytes) {
         if (cap[k] < bytes) {
             if (p[k]) cudaFree(p[k]);
@@ -890,21 +903,28 @@ void png_decode(const uint8_t* data, const uint64_t* offsets, const uint64_t* si
     AEISU_CUDA(cudaGetDevice(&prev));
     AEISU_CUDA(cudaSetDevice(device));
     struct Restore { int d; ~Restore() { if (d >= 0) cudaSetDevice(d); } } restore{prev};
-    // host: parse and check every file, concatenate the zlib streams
+    // host: parse and check every file; the zlib streams (without their 2-byte headers) are
+    // gathered straight from the files into page-locked staging, each 16-byte aligned
     std::vector<DecFile> files(n);
-    std::vector<uint8_t> in, pal;
-    std::vector<uint8_t> stream_bytes;
-    unsigned long long out_off = 0;
+    std::vector<std::vector<std::pair<size_t, size_t>>> idat(n);
+    std::vector<uint8_t> pal;
+    unsigned long long out_off = 0, in_off = 0;
     for (int i = 0; i < n; ++i) {
-        const PngFileInfo info = png_parse(data + offsets[i], size_t(sizes[i]), &stream_bytes);
+        const uint8_t* file = data + offsets[i];
+        const PngFileInfo info = png_parse(file, size_t(sizes[i]), &idat[i]);
         png_check_supported(info);
         if (info.h != h || info.w != w)
             fail(AEISU_ERR_INVALID_ARG, "PNG file " + std::to_string(i) + " is " + std::to_string(info.w) + "x" +
                                             std::to_string(info.h) + ", the batch is " + std::to_string(w) + "x" +
                                             std::to_string(h));
         // zlib header (RFC 1950): deflate, window <= 32 KiB, no preset dictionary, check bits
-        require(stream_bytes.size() >= 6, "PNG image data too short");
-        const uint8_t cmf = stream_bytes[0], flg = stream_bytes[1];
+        require(info.idat_bytes >= 6, "PNG image data too short");
+        uint8_t head[2];
+        for (int k = 0, r = 0, at = 0; k < 2; ++k) {   // the stream's first two bytes, across chunks
+            while (size_t(at) >= idat[i][r].second) at -= int(idat[i][r++].second);
+            head[k] = file[idat[i][r].first + at++];
+        }
+        const uint8_t cmf = head[0], flg = head[1];
         require((cmf & 15) == 8 && (cmf >> 4) <= 7 && ((cmf << 8) | flg) % 31 == 0 && !(flg & 0x20),
                 "bad zlib header in PNG image data");
         DecFile& fd = files[i];
@@ -913,26 +933,41 @@ void png_decode(const uint8_t* data, const uint64_t* offsets, const uint64_t* si
         fd.npal = info.color == 3 ? info.npal : 0;
         fd.pal_off = int(pal.size());
         if (fd.npal) pal.insert(pal.end(), info.palette, info.palette + 3 * fd.npal);
-        while (in.size() % 16) in.push_back(0);
-        fd.in_off = in.size();
-        fd.in_len = stream_bytes.size() - 2;
-        in.insert(in.end(), stream_bytes.begin() + 2, stream_bytes.end());
+        fd.in_off = in_off;
+        fd.in_len = info.idat_bytes - 2;
+        in_off += (fd.in_len + 15) / 16 * 16;
         require((unsigned long long)h * (1ull + (unsigned long long)w * fd.bpp) < (1ull << 32), "PNG image too large");
         fd.out_off = out_off;
         out_off += ((unsigned long long)h * (1ull + (unsigned long long)w * fd.bpp) + 15) / 16 * 16;
     }
-    in.resize(in.size() + 16, 0);
+    const size_t in_bytes = size_t(in_off) + 16;   // + zero words the bit reader may load past an end
     if (pal.empty()) pal.push_back(0);
     DecGeom g{n, h, w, (unsigned long long)h * w * 3};
     DecodeCache& cache = decode_cache(device);
     std::lock_guard<std::mutex> lock(cache.m);
+    uint8_t* staged = cache.get_host(in_bytes);
+    for (int i = 0; i < n; ++i) {
+        uint8_t* dst = staged + files[i].in_off;
+        size_t skip = 2;   // the zlib header, checked above
+        for (const auto& r : idat[i]) {
+            if (skip >= r.second) {
+                skip -= r.second;
+                continue;
+            }
+            std::memcpy(dst, data + offsets[i] + r.first + skip, r.second - skip);
+            dst += r.second - skip;
+            skip = 0;
+        }
+        const uint8_t* end = staged + (i + 1 < n ? files[i + 1].in_off : in_bytes);
+        std::memset(dst, 0, size_t(end - dst));
+    }
     // once work is queued, the buffers stay locked until it is done, errors included
     struct Drain {
         cudaStream_t s;
         bool armed = false;
         ~Drain() { if (armed) cudaStreamSynchronize(s); }
     } drain{stream};
-    void* d_in = cache.get(DecodeCache::kIn, in.size());
+    void* d_in = cache.get(DecodeCache::kIn, in_bytes);
     void* d_files = cache.get(DecodeCache::kFiles, sizeof(DecFile) * n);
     void* d_pal = cache.get(DecodeCache::kPal, pal.size());
     // + slack: the unfilter stages whole aligned words and chunks past a row's end
@@ -940,7 +975,7 @@ void png_decode(const uint8_t* data, const uint64_t* offsets, const uint64_t* si
     void* d_status = cache.get(DecodeCache::kStatus, sizeof(DecStatus) * n);
     uint8_t* dev_out = host_out ? static_cast<uint8_t*>(cache.get(DecodeCache::kOut, g.out_stride * n)) : out;
     drain.armed = true;
-    AEISU_CUDA(cudaMemcpyAsync(d_in, in.data(), in.size(), cudaMemcpyHostToDevice, stream));
+    AEISU_CUDA(cudaMemcpyAsync(d_in, staged, in_bytes, cudaMemcpyHostToDevice, stream));
     AEISU_CUDA(cudaMemcpyAsync(d_files, files.data(), sizeof(DecFile) * n, cudaMemcpyHostToDevice, stream));
     AEISU_CUDA(cudaMemcpyAsync(d_pal, pal.data(), pal.size(), cudaMemcpyHostToDevice, stream));
     AEISU_CUDA(cudaMemsetAsync(d_status, 0, sizeof(DecStatus) * n, stream));

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
 #include <vector>
 
 #include "../../include/aeisu.h"
@@ -124,14 +125,15 @@ void png_encode(const void* src, int kind, int n, int h, int w, bool host_io, in
                 uint64_t capacity, uint64_t* sizes, cudaStream_t stream);
 int png_launches_per_call();
 
-// PNG ingress (k_pngdec.cu): the header facts of one file and, when `stream` is given, its zlib
-// stream (the IDAT payloads concatenated); every chunk's CRC is checked.
+// PNG ingress (k_pngdec.cu): the header facts of one file, checked as PIL checks them, and, when
+// `idat` is given, where its zlib stream lies in `data` (the IDAT payloads, in order, as
+// (offset, length) pairs).
 struct PngFileInfo {
     int w, h, depth, color, interlace, npal;
     uint8_t palette[768];
     unsigned long long idat_bytes;
 };
-PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<uint8_t>* stream);
+PngFileInfo png_parse(const uint8_t* data, size_t size, std::vector<std::pair<size_t, size_t>>* idat);
 // AEISU_ERR_UNSUPPORTED unless 8-bit samples, colour type 0/2/3/4/6, no interlacing.
 void png_check_supported(const PngFileInfo& info);
 // n PNG files (host memory) of one size h x w -> n uint8 RGB frames h x w x 3 in `out` (host or
