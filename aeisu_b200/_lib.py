@@ -88,6 +88,7 @@ _SIGNATURES = {
     "aeisu_tensor_peak": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "aeisu_timings_get": (C.c_int, [C.c_void_p, C.POINTER(Timings)]),
     "aeisu_set_detailed_timing": (C.c_int, [C.c_void_p, C.c_int]),
+    "aeisu_set_fused_head": (C.c_int, [C.c_void_p, C.c_int]),
     "aeisu_set_timeout": (C.c_int, [C.c_void_p, C.c_double]),
     "aeisu_set_workspace_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
     "aeisu_report": (C.c_char_p, [C.c_void_p]),

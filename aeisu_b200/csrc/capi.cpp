@@ -291,6 +291,10 @@ int aeisu_set_detailed_timing(aeisu_t* handle, int enabled) {
     return guarded([&] { engine_of(handle).set_detailed(enabled != 0); });
 }
 
+int aeisu_set_fused_head(aeisu_t* handle, int enabled) {
+    return guarded([&] { engine_of(handle).set_fused_head(enabled != 0); });
+}
+
 int aeisu_set_workspace_limit(aeisu_t* handle, uint64_t bytes) {
     return guarded([&] { engine_of(handle).set_workspace_cap(size_t(bytes)); });
 }

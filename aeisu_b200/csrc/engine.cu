@@ -383,7 +383,8 @@ struct RegionBytes {
 };
 
 // Workspace bytes per region: f32 NHWC for the FP32 route; chunk-planar f16/e4m3 otherwise.
-RegionBytes region_bytes(int precision, int rh, int rw, bool predict) {
+// A fused tensor-core reconstruction keeps the coefficients on chip: no meta buffer.
+RegionBytes region_bytes(int precision, int rh, int rw, bool predict, bool fused) {
     const size_t packed = size_t(rh / 2) * (rw / 2), low = size_t(rh / 4) * (rw / 4);
     const bool tcr = precision != AEISU_PRECISION_FP32, fp8 = precision == AEISU_PRECISION_MIXED;
     RegionBytes b;
@@ -392,7 +393,7 @@ RegionBytes region_bytes(int precision, int rh, int rw, bool predict) {
     b.low = tcr ? low * (fp8 ? 64 : 128) : low * 64 * 4;
     b.dec = tcr ? packed * 64 : packed * 32 * 4;
     b.ref = tcr ? 0 : packed * 64 * 4;
-    b.meta = tcr ? size_t(rh) * rw * 32 : packed * 64 * 4;
+    b.meta = tcr ? (fused ? 0 : size_t(rh) * rw * 32) : packed * 64 * 4;
     b.raw = (tcr && predict) ? packed * 64 * 4 : 0;
     return b;
 }
@@ -405,7 +406,7 @@ constexpr int kSplitRegions = 8;
 
 void Engine::run_group(const Call& c, const Geometry& g, const Geometry::Group& grp, const SrcDesc& src,
                        const DstDesc& dst, cudaStream_t s) {
-    const RegionBytes rb = region_bytes(precision_, grp.rh, grp.rw, c.mode == Mode::Predict);
+    const RegionBytes rb = region_bytes(precision_, grp.rh, grp.rw, c.mode == Mode::Predict, fused(c));
     const size_t chunk = std::max<size_t>(1, std::min<size_t>(grp.regions.size(), workspace_cap_ / rb.per_region()));
     for (size_t first = 0; first < grp.regions.size(); first += chunk) {
         const int R = int(std::min(chunk, grp.regions.size() - first));
@@ -433,7 +434,8 @@ void Engine::run_regions(const Call& c, const Geometry::Group& grp, size_t first
     const int rh = grp.rh, rw = grp.rw;
     const size_t packed = size_t(rh / 2) * (rw / 2);
     const bool tcr = precision_ != AEISU_PRECISION_FP32;
-    const RegionBytes rb = region_bytes(precision_, rh, rw, c.mode == Mode::Predict);
+    const bool fuse = fused(c);
+    const RegionBytes rb = region_bytes(precision_, rh, rw, c.mode == Mode::Predict, fuse);
     std::vector<int4> table(2 * size_t(R));
     int core_h = 0, core_w = 0;
     for (int i = 0; i < R; ++i) {
@@ -466,7 +468,7 @@ void Engine::run_regions(const Call& c, const Geometry::Group& grp, size_t first
     if (rb.ref) ws.refined.ensure(rb.ref * R, s);
     if (rb.encu) ws.encu.ensure(rb.encu * R, s);
     if (rb.raw) ws.raw.ensure(rb.raw * R, s);
-    ws.meta.ensure(rb.meta * R, s);
+    if (rb.meta) ws.meta.ensure(rb.meta * R, s);
     ws.low_a.ensure(rb.low * R, s);
     ws.low_b.ensure(rb.low * R, s);
     int launches = 0;
@@ -476,9 +478,10 @@ void Engine::run_regions(const Call& c, const Geometry::Group& grp, size_t first
     mark.fn = [](void* p, int stage) { auto* c = static_cast<Ctx*>(p); c->e->record(stage, c->s); };
     const bool predict = c.mode == Mode::Predict;
     if (tcr) {
+        const FusedHead head{&dst, head_img_, flag_.as<int>()};
         launch_tc_controller(tc_route_of(precision_), src, rs, tcw_, ws.enc540.get(), ws.encu.get(), ws.low_a.get(),
                              ws.low_b.get(), ws.dec540.get(), ws.meta.get(), predict ? ws.raw.as<float>() : nullptr,
-                             flag_.as<int>() + 1, s, &launches, mark);
+                             flag_.as<int>() + 1, s, &launches, mark, fuse ? &head : nullptr);
     } else {
         launch_f32_controller(src, rs, stencil_, f32_layers_, ws.enc540.as<float>(), ws.low_a.as<float>(),
                               ws.low_b.as<float>(), ws.dec540.as<float>(), ws.refined.as<float>(), ws.meta.as<float>(), s,
@@ -498,7 +501,8 @@ void Engine::run_regions(const Call& c, const Geometry::Group& grp, size_t first
             AEISU_CUDA(cudaMemcpyAsync(out, meta + size_t(i) * bytes, bytes, cudaMemcpyDeviceToDevice, s));
         }
     } else if (tcr) {
-        launch_tc_head(src, rs, dst, ws.meta.get(), head_img_, flag_.as<int>(), flag_.as<int>() + 1, s, &launches);
+        if (!fuse)
+            launch_tc_head(src, rs, dst, ws.meta.get(), head_img_, flag_.as<int>(), flag_.as<int>() + 1, s, &launches);
     } else {
         launch_f32_head(src, rs, dst, ws.meta.as<float>(), base_, basis_, flag_.as<int>(), s, &launches);
     }

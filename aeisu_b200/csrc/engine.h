@@ -121,6 +121,9 @@ public:
     // Stage times of the last call (waits for it to finish when stage marks are pending).
     const aeisu_timings& timings();
     void set_detailed(bool on) { detailed_ = on; }
+    // Tensor-core upscales reconstruct in a separate head kernel over coefficients kept in HBM
+    // (default, the faster) or inside the controller's last kernel (same output bit for bit).
+    void set_fused_head(bool on) { fused_head_ = on; }
     void set_timeout(double ms) { timeout_ms_ = ms; }
     void set_workspace_cap(size_t bytes) { workspace_cap_ = bytes; }
     int precision() const { return precision_; }
@@ -162,6 +165,9 @@ private:
     void finish_host_call(const Call& c, cudaStream_t s, bool staged, size_t dst_bytes);
     void wait(cudaStream_t s, double timeout_ms);
     void record(int stage, cudaStream_t s);
+    bool fused(const Call& c) const {
+        return fused_head_ && precision_ != AEISU_PRECISION_FP32 && (c.mode == Mode::Upscale || c.mode == Mode::Forward);
+    }
 
     HostModel model_;
     int precision_, device_;
@@ -170,6 +176,7 @@ private:
     std::string report_;
     double timeout_ms_ = 60000.0;
     bool detailed_ = false;
+    bool fused_head_ = false;
     uint64_t launches_ = 0;
     aeisu_timings timings_{};
 

@@ -1265,6 +1265,519 @@ __global__ void __launch_bounds__(kThreads, PX == 1 ? 4 : 2) k_tc_head(const __g
     cta_teardown(tmem, kCols);
 }
 
+// ---- fused refine_540 + metadata_head + reconstruction head ---------------------------------
+// One kernel from dec540 to the output frames: the clamped coefficients of a packed row go from
+// the tail epilogue into shared memory as the head's A operands and never reach HBM.
+// Eight warps, two warpgroups, one CTA per SM (all 512 TMEM columns); with no producer warp each
+// thread may hold 255 registers.  Warpgroup wg takes packed row y + wg of every row pair: the
+// refine epilogue, tail MMA and tail epilogue of k_tc_refine_tail, then the reconstruction of
+// the row.  Lane tq holds packed pixel x = x0 + tq, whose four LR pixels (2y + i, 2x + j) make
+// four tiles of 128 pixels: the A row of tile (i, j) is the lane's tail channels
+// (2i + j)*16 .. +16, i.e. the 16 coefficients of LR pixel (2y + i, 2x + j).  The filter-mix
+// MMAs of k_tc_head build each tile's 100 weights in two halves (columns 0-63 and 64-111 of the
+// tile's layout: tap pairs of rows 0-3, then tap pairs of row 4 and the fifth column), eight
+// halves per row.  Each warpgroup owns three 64-column TMEM buffers (128 + 192 wg); once every
+// thread of the warpgroup has loaded half s, half s + 3 of the row is issued into its buffer, so
+// each MMA runs under the FMAs of the halves before it.  Weights, accumulation order and output
+// rounding are k_tc_head's, so the frames equal the unfused pair's bit for bit.
+// Thread 0 also does the producer's work: dec540 rows (TMA) through a ring of six row slots, two
+// pairs ahead, and the refine MMAs of the next pair (one pair buffer, TMEM columns 0-127) in four
+// groups of six, the first once both warpgroups have read their tails (pair_empty), each issued
+// after the head MMAs of a tile so that they queue behind them.
+// LR source rows (region- then frame-clamped, converted to float once per strip) slide through
+// a ring of 12 rows shared by both warpgroups: a pair reads 8 (2y - 2 .. 2y + 5) while the
+// next pair's 4 new rows are fetched into registers and stored at the end of the pair; one
+// barrier of both warpgroups per pair publishes them.  Each (row, channel) is stored twice, E =
+// s[0..] and O = s[1..] (ring column c = LR column 2 x0 - 2 + c), so the horizontal tap pairs
+// of an even pixel are the float2 E[tq + jj] and those of an odd pixel O[tq + jj]: a warp reads
+// consecutive 8-byte pairs, free of bank conflicts.
+// Work items: (region, strip of kConvStrip packed columns, band of packed rows) over the packed
+// rectangle that covers the region's core, its rows rounded out to whole pairs.
+constexpr int kFusedThreads = 256;
+constexpr int kFusedRing = 6;             // dec540 row slots
+constexpr int kSrcRing = 12;              // LR source rows in the ring
+constexpr int kSrcCols = 2 * kM + 5;      // ring columns a strip reads (2 x0 - 2 .. 2 x0 + 258)
+constexpr int kSrcArr = 264;              // floats per (row, channel) array E or O
+constexpr int kFusedBytes = 1024 + kFusedRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 +
+                            3 * kHeadBCH + 2 * kM * 16 + 2 * 64 * 4 + 256 * 4 + kSrcRing * 3 * 2 * kSrcArr * 4;
+static_assert(kFusedBytes <= 220 * 1024, "fused kernel's shared memory");
+
+struct FusedItem {
+    int r, x0, y0, y1, px1;
+    int4 core;
+    bool skip;
+};
+__device__ __forceinline__ FusedItem fused_item(long long item, const RegionSet& rs, int nstrip, int nband,
+                                                int band) {
+    FusedItem f;
+    f.r = int(item / ((long long)nstrip * nband));
+    const int bi = int((item / nstrip) % nband), si = int(item % nstrip);
+    f.core = rs.cores[f.r];
+    const int py0 = (f.core.x >> 1) & ~1, py1 = min(rs.rh / 2, (((f.core.z + 1) >> 1) + 1) & ~1);
+    f.px1 = (f.core.w + 1) >> 1;
+    f.x0 = (f.core.y >> 1) + si * kConvStrip;
+    f.y0 = py0 + bi * band;
+    f.y1 = min(f.y0 + band, py1);
+    f.skip = f.x0 >= f.px1 || f.y0 >= py1;
+    return f;
+}
+
+// Barrier of both warpgroups (id 3, 256 threads); returns whether any thread passed `v`.
+__device__ __forceinline__ bool epilogues_sync_or(bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 3, 256, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r) : "r"(uint32_t(v)) : "memory");
+    return r != 0;
+}
+
+template <bool SRC_U8, bool DST_U8>
+__global__ void __launch_bounds__(kFusedThreads, 1) k_tc_refine_head(const __grid_constant__ CUtensorMap tin, RegionSet rs,
+                                                              const uint8_t* __restrict__ wref,
+                                                              const uint8_t* __restrict__ wtail,
+                                                              const float* __restrict__ rbias,
+                                                              const float* __restrict__ tbias, float slope,
+                                                              const uint8_t* __restrict__ bimg, SrcDesc src,
+                                                              DstDesc dst, int band, int nstrip, int nband,
+                                                              int* nonfinite, int* err) {
+    constexpr int ICH = 4, LBO = kM * 16, SLOT = ICH * LBO;
+    constexpr int BREF = 36 * 64 * 16, BTAIL = 8 * 64 * 16, A2 = 8 * kM * 16;
+    constexpr int WBLK = 64 * 16, WLBO = 3 * WBLK;
+    constexpr int ROWF = 3 * 2 * kSrcArr;     // floats per source ring row: per channel E then O
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = align_smem(smem_raw);     // TMA destinations: 1024-byte aligned ring
+    uint8_t* sB = smem + kFusedRing * SLOT;   // refine weights
+    uint8_t* sT = sB + BREF;                  // tail weights
+    uint8_t* sA2 = sT + BTAIL;                // per warpgroup: the tail's A operand, then the head's 4 tiles
+    uint8_t* sHB = sA2 + 2 * A2;              // head B operands: basis hi, basis lo, base
+    uint8_t* sOnes = sHB + 3 * kHeadBCH;      // [2 chunks][128][16 B]
+    float* s_rb = reinterpret_cast<float*>(sOnes + 2 * kM * 16);
+    float* s_tb = s_rb + 64;
+    float* s_lut = s_tb + 64;
+    float* s_src = s_lut + 256;               // [kSrcRing][3][E | O][kSrcArr]
+    __shared__ uint32_t s_tmem;
+    // dec540 slots, ref_full; per warpgroup tail_full, drain; per warpgroup and head buffer
+    // head_full (all count 1); pair_empty (count 8: every warp, once it has read its tail)
+    __shared__ alignas(8) uint64_t s_bar[kFusedRing + 12];
+    uint64_t* ring_full = s_bar;
+    uint64_t* ref_full = s_bar + kFusedRing;
+    uint64_t* tail_full = s_bar + kFusedRing + 1;
+    uint64_t* drain = s_bar + kFusedRing + 3;
+    uint64_t* head_full = s_bar + kFusedRing + 5;
+    uint64_t* pair_empty = s_bar + kFusedRing + 11;
+    copy_image(sB, wref, BREF);
+    copy_image(sT, wtail, BTAIL);
+    copy_image(sHB, bimg, 3 * kHeadBCH);
+    for (int i = threadIdx.x; i < 2 * kM; i += blockDim.x) {
+        const uint32_t one2 = 0x3C003C00u;   // f16 1.0, 1.0
+        *reinterpret_cast<uint4*>(sOnes + i * 16) = (i < kM) ? make_uint4(one2, 0, 0, 0) : make_uint4(0, 0, 0, 0);
+    }
+    if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
+    if (SRC_U8) fill_lut(s_lut);
+    if (threadIdx.x == 0) mbar_init(pair_empty, 8);
+    fence_async_smem();
+    cta_setup(&s_tmem, s_bar, kFusedRing + 11, 512);
+    const uint32_t tmem = s_tmem;
+    const long long items = (long long)rs.R * nstrip * nband;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int wg = warp >> 2, tq = t & 127;
+    const bool issuer = t == 0;                  // producer work, and warpgroup 0's tail and head MMAs
+    const uint32_t lrow = uint32_t(32 * (warp & 3)) << 16;
+    const uint32_t half = wg == 0 ? 64 : 0;   // TMEM columns of this warpgroup's row in the pair buffer
+    uint8_t* a2 = sA2 + wg * A2;
+    const uint32_t a2addr = smem_addr(a2), t0 = smem_addr(sT), hb0 = smem_addr(sHB), o0 = smem_addr(sOnes);
+    const uint32_t b0 = smem_addr(sB), ring0 = smem_addr(smem);
+    constexpr uint32_t idesc64 = idesc_m128(64), idesc128 = idesc_m128(128);
+    // this warpgroup's three filter-weight buffers; half s of a row (tile s >> 1, half s & 1)
+    // goes to buffer (hs + s) % 3, hs counting the halves of the warpgroup's earlier rows
+    const uint32_t hcol = tmem + 128 + uint32_t(wg) * 192;
+    const size_t plane = size_t(src.H) * src.W;
+    uint32_t p = 0, tail_phase = 0, hs = 0, head_phase = 0;   // head_phase: bit per buffer
+    uint32_t ring_phase = 0, ring_pend = 0;          // issuer: per dec540 slot
+    // bad: a wait of this warp expired; pbad: one of the issuer's producer waits expired; dead:
+    // the warpgroup voted to stop.  All three enter every vote.
+    bool live = true, bad = false, dead = false, pbad = false;
+
+    // ---- producer work (issuer only) ----
+    auto slot_of = [](int row) { return (row + kFusedRing) % kFusedRing; };   // rows >= -1
+    auto load_row = [&](int row, const FusedItem& fi) {
+        const int sl = slot_of(row);
+        mbar_arrive_expect_tx(&ring_full[sl], uint32_t(SLOT));
+        tma_load_4d(smem + sl * SLOT, &tin, 2 * (fi.x0 - 1), 0, row, fi.r, &ring_full[sl]);
+        ring_pend |= 1u << sl;
+    };
+    auto wait_row = [&](int row) {
+        const int sl = slot_of(row);
+        if (!(ring_pend & (1u << sl))) return true;   // already observed
+        const bool ok = mbar_wait_bounded(&ring_full[sl], (ring_phase >> sl) & 1u, err, kErrTimeout);
+        if (ok) {
+            ring_phase ^= 1u << sl;
+            ring_pend &= ~(1u << sl);
+        }
+        return ok;
+    };
+    // group g (0-3) of the refine MMAs of the pair whose first output row is y, into buffer d:
+    // [W0; W1] x row y (initialises both rows), W0 x row y-1, [W1; W2] x row y+1, W2 x row y+2
+    auto refine_group = [&](uint32_t d, int y, int g) {
+        const int row = g == 0 ? y : g == 1 ? y - 1 : g == 2 ? y + 1 : y + 2;
+        const int ky = g < 2 ? 0 : g - 1;
+        const bool n128 = g != 1 && g != 3;
+        const uint32_t dd = g == 1 ? d + 64 : d;
+        const uint32_t a = ring0 + slot_of(row) * SLOT;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+                mma_f16(dd, sdesc(a + 2 * kk * LBO + kx * 16, LBO, 128),
+                        sdesc(b0 + ((kx * 4 + 2 * kk) * 3 + ky) * WBLK, WLBO, 128), n128 ? idesc128 : idesc64,
+                        !(g == 0 && kx == 0 && kk == 0));
+    };
+    // half s of the current row (hs: the row's first half) into its buffer
+    auto head_mma = [&](int s) {
+        const int tile = s >> 1, h = s & 1, buf = (hs + s) % 3;
+        const uint64_t a = sdesc(a2addr + tile * kHeadTile, kM * 16, 128);
+        const uint32_t d = hcol + 64 * buf, bo = hb0 + 64 * 16 * h, id = h ? idesc_m128(48) : idesc64;
+        mma_f16(d, a, sdesc(bo, 128 * 16, 128), id, 0);
+        mma_f16(d, a, sdesc(bo + kHeadBCH, 128 * 16, 128), id, 1);
+        mma_f16(d, sdesc(o0, kM * 16, 128), sdesc(bo + 2 * kHeadBCH, 128 * 16, 128), id, 1);
+        commit(&head_full[3 * wg + buf]);
+    };
+    // this warp's wait for half s of the current row; false if it expired
+    auto head_wait = [&](int s) {
+        const int buf = (hs + s) % 3;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_idle(&head_full[3 * wg + buf], (head_phase >> buf) & 1u, err,
+                                                                kErrTimeout));
+        if (ok) {
+            head_phase ^= 1u << buf;
+            fence_after_sync();
+        }
+        return ok;
+    };
+    auto head_cols = [&](int s) { return hcol + lrow + 64 * uint32_t((hs + s) % 3); };
+
+    for (long long item = blockIdx.x; item < items && live; item += gridDim.x) {
+        last_item(item, items);
+        const FusedItem fi = fused_item(item, rs, nstrip, nband, band);
+        if (fi.skip) continue;   // uniform across the CTA
+        const int4 reg = rs.regions[fi.r];
+        const int x = fi.x0 + tq;
+        const bool xin = tq < kConvStrip && x < fi.px1;
+        const int row0 = 2 * fi.y0 - 2;   // LR row of source ring slot 0
+        const uint8_t* sfu8 = static_cast<const uint8_t*>(src.ptr) + size_t(reg.x) * plane * 3;
+        const float* sff = static_cast<const float*>(src.ptr) + size_t(reg.x) * plane * 3;
+        auto fetch = [&](int row, int c) -> uint3 {
+            const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
+            const int sx = clampi(reg.z + clampi(2 * fi.x0 - 2 + c, 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
+            if (SRC_U8) {
+                const uint8_t* q = sfu8 + (size_t(sy) * src.W + sx) * 3;
+                return make_uint3(q[0], q[1], q[2]);
+            }
+            const float* q = sff + size_t(sy) * src.W + sx;
+            return make_uint3(__float_as_uint(q[0]), __float_as_uint(q[plane]), __float_as_uint(q[2 * plane]));
+        };
+        auto put = [&](int row, int c, uint3 raw) {
+            float* ps = s_src + ((row - row0) % kSrcRing) * ROWF;
+            float v[3];
+            if (SRC_U8) {
+                v[0] = s_lut[raw.x]; v[1] = s_lut[raw.y]; v[2] = s_lut[raw.z];
+            } else {
+                v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y); v[2] = __uint_as_float(raw.z);
+            }
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                ps[ch * 2 * kSrcArr + c] = v[ch];
+                if (c > 0) ps[ch * 2 * kSrcArr + kSrcArr + c - 1] = v[ch];
+            }
+        };
+        // both warpgroups are done with the previous item (its source rows, its MMAs observed)
+        if (epilogues_sync_or(bad || dead || pbad)) {
+            live = false;
+            break;
+        }
+        // item prologue: dec540 rows y0-1 .. y0+4 and the refine MMAs of the first pair
+        if (issuer) {
+            bool ok = true;
+            for (int row = fi.y0 - 1; row <= min(fi.y0 + 4, fi.y1); ++row) load_row(row, fi);
+            for (int row = fi.y0 - 1; row <= fi.y0 + 2 && ok; ++row) ok = wait_row(row);
+            if (ok) {
+                fence_after_sync();
+                for (int g = 0; g < 4; ++g) refine_group(tmem, fi.y0, g);
+            }
+            commit(ref_full);   // also on a failed wait, so that every parity stays in step
+            pbad = !ok;
+        }
+        __syncwarp();
+        for (int e = t; e < 8 * kSrcCols; e += kFusedThreads)
+            put(row0 + e / kSrcCols, e % kSrcCols, fetch(row0 + e / kSrcCols, e % kSrcCols));
+        for (int y0 = fi.y0; y0 < fi.y1; y0 += 2, ++p) {
+            const int y = y0 + wg;
+            const bool more = y0 + 2 < fi.y1;      // the item has a next pair
+            const int nrow = 2 * y0 + 6;           // the next pair's first new LR source row
+            // uint8 samples are held packed, one register per pixel, until the end of the pair
+            uint3 pre[5];
+            if (more) {
+#pragma unroll
+                for (int m = 0; m < 5; ++m) {
+                    const int e = t + kFusedThreads * m;
+                    if (e < 4 * kSrcCols) {
+                        pre[m] = fetch(nrow + e / kSrcCols, e % kSrcCols);
+                        if (SRC_U8) pre[m].x = pre[m].x | (pre[m].y << 8) | (pre[m].z << 16);
+                    }
+                }
+            }
+            // the source rows stored so far are visible; both warpgroups are done with the
+            // previous pair
+            if (epilogues_sync_or(bad || dead || pbad)) {
+                live = false;
+                break;
+            }
+            const uint32_t col = tmem + lrow + half;
+            // refine epilogue -> tail operand of this row
+            bad = !__all_sync(0xffffffffu, mbar_wait_idle(ref_full, p & 1, err, kErrTimeout));
+            if (!bad) {
+                fence_after_sync();
+                // this pair's MMAs have completed: its first two dec540 slots take the rows of the
+                // pair after next
+                if (issuer && y0 + 4 < fi.y1) {
+                    load_row(y0 + 5, fi);
+                    if (y0 + 6 <= fi.y1) load_row(y0 + 6, fi);
+                }
+                __syncwarp();
+                float vr[2][32];
+                tmem_ld32x2(col, col + 32, vr[0], vr[1]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    epi_add_leaky(vr[h], s_rb + h * 32, slope);
+                    uint4 q[4];
+                    pack_f16x32(vr[h], q);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(a2 + ((h * 4 + c) * kM + tq) * 16) = q[c];
+                }
+                fence_async_smem();
+            }
+            fence_before_sync();
+            dead = warpgroup_sync_or(wg, bad || pbad);
+            if (!dead && tq == 0) {
+                fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16(tmem + half, sdesc(a2addr + kk * 2 * kM * 16, kM * 16, 128),
+                            sdesc(t0 + kk * 2 * 64 * 16, 64 * 16, 128), idesc64, kk > 0);
+                commit(&tail_full[wg]);
+            }
+            __syncwarp();
+            // tail epilogue: coefficients (tail bias, coefficient_clamp, f16) into the head's four
+            // A tiles, which take the place of the tail operand (its MMAs have completed)
+            if (!dead) {
+                bad = !__all_sync(0xffffffffu, mbar_wait_idle(&tail_full[wg], tail_phase, err, kErrTimeout));
+                if (!bad) {
+                    tail_phase ^= 1u;
+                    fence_after_sync();
+                    float vt[2][32];
+                    tmem_ld32x2(col, col + 32, vt[0], vt[1]);
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pair_empty);   // this warp's part of the pair buffer is read
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float (&v)[32] = vt[h];
+                        epi_add(v, s_tb + h * 32);
+#pragma unroll
+                        for (int n = 0; n < 32; n += 2) {   // coefficient_clamp, as k_tc_refine_tail
+                            const float2 soft = __ffma2_rn(make_float2(0.05f, 0.05f),
+                                                           __fadd2_rn(make_float2(fminf(fabsf(v[n]), 12.f),
+                                                                                  fminf(fabsf(v[n + 1]), 12.f)),
+                                                                      make_float2(-2.f, -2.f)),
+                                                           make_float2(2.f, 2.f));
+                            v[n] = min_xorsign_abs(v[n], soft.x);
+                            v[n + 1] = min_xorsign_abs(v[n + 1], soft.y);
+                        }
+                        uint4 q[4];
+                        pack_f16x32(v, q);
+                        // tile (h, j): channels h*32 + j*16 .. +16 = chunks q[2j], q[2j+1]
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+#pragma unroll
+                            for (int c = 0; c < 2; ++c)
+                                *reinterpret_cast<uint4*>(a2 + (2 * h + j) * kHeadTile + (c * kM + tq) * 16) = q[2 * j + c];
+                    }
+                    fence_async_smem();
+                }
+            }
+            fence_before_sync();
+            dead = warpgroup_sync_or(wg, dead || bad || pbad);
+            if (!dead && tq == 0) {
+                fence_after_sync();
+                head_mma(0);
+                head_mma(1);
+                head_mma(2);
+            }
+            __syncwarp();
+            // the source ring rows of LR rows 2y - 2 .. 2y + 3: tile (i, j) reads rows i .. i + 4
+            const float* srow[6];
+#pragma unroll
+            for (int r6 = 0; r6 < 6; ++r6) srow[r6] = s_src + ((2 * y - 2 + r6 - row0) % kSrcRing) * ROWF;
+            // reconstruction of the row's four tiles.  Per tile and half: wait for its MMAs, load
+            // its weights, and once every thread of the warpgroup has them, issue the same half
+            // of the next tile into the freed columns, then run its FMAs.
+#pragma unroll
+            for (int tile = 0; tile < 4; ++tile) {
+                const int i = tile >> 1, j = tile & 1;
+                const int Y = 2 * y + i, X = 2 * x + j;   // region-local LR pixel
+                const float2* rows[5];
+#pragma unroll
+                for (int ky = 0; ky < 5; ++ky) rows[ky] = reinterpret_cast<const float2*>(srow[i + ky] + j * kSrcArr) + tq;
+                // k_tc_head's accumulation: acc[phase][ch] = (taps with even kx and the fifth
+                // column | taps with odd kx), tap pairs in column order, then the fifth column
+                float2 acc[4][3];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int ch = 0; ch < 3; ++ch) acc[q][ch] = make_float2(0.f, 0.f);
+                {   // half 0: tap pairs of rows 0-3 (columns 0-63)
+                    float w[2][32];
+                    if (!dead) {
+                        bad = !head_wait(2 * tile);
+                        if (!bad) tmem_ld32x2(head_cols(2 * tile), head_cols(2 * tile) + 32, w[0], w[1]);
+                    }
+                    fence_before_sync();
+                    dead = warpgroup_sync_or(wg, dead || bad || pbad);
+                    if (!dead) {
+                        if (2 * tile + 3 < 8 && tq == 0) {
+                            fence_after_sync();
+                            head_mma(2 * tile + 3);
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int pr = 0; pr < 8; ++pr) {
+                            const int ky = pr >> 1, jj = pr & 1, n = pr * 8;
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch) {
+                                const float2 sv = rows[ky][ch * kSrcArr + jj];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    acc[q][ch] = __ffma2_rn(sv, make_float2(w[n >> 5][(n & 31) + 2 * q], w[n >> 5][(n & 31) + 2 * q + 1]),
+                                                            acc[q][ch]);
+                            }
+                        }
+                    }
+                }
+                {   // half 1: tap pairs of row 4 (columns 64-79), fifth column (80-99)
+                    uint32_t w[2][32];
+                    if (!dead) {
+                        bad = !head_wait(2 * tile + 1);
+                        if (!bad) {
+                            tmem_ld_x32(head_cols(2 * tile + 1), w[0]);
+                            tmem_ld_x4(head_cols(2 * tile + 1) + 32, w[1]);
+                            tmem_wait_ld();
+                            tmem_regs_ready(w[0]);
+                            tmem_regs_ready(w[1]);
+                        }
+                    }
+                    fence_before_sync();
+                    dead = warpgroup_sync_or(wg, dead || bad || pbad);
+                    if (!dead) {
+                        if (tq == 0) {
+                            fence_after_sync();
+                            if (2 * tile + 4 < 8) head_mma(2 * tile + 4);
+                        }
+                        // producer: group `tile` of the next pair's refine MMAs, behind the head
+                        // MMAs; the first once both warpgroups have read this pair's tails
+                        if (issuer && more) {
+                            bool ok = true;
+                            if (tile == 0) ok = mbar_wait_bounded(pair_empty, p & 1, err, kErrTimeout);
+                            if (tile == 2) ok = wait_row(y0 + 3);
+                            if (tile == 3) ok = wait_row(y0 + 4);
+                            if (ok) {
+                                fence_after_sync();
+                                refine_group(tmem, y0 + 2, tile);
+                            }
+                            if (tile == 3) commit(ref_full);
+                            pbad = pbad || !ok;
+                        }
+                        __syncwarp();
+                        auto wv = [&](int n) { return __uint_as_float(n < 96 ? w[0][n - 64] : w[1][n - 96]); };
+#pragma unroll
+                        for (int pr = 8; pr < 10; ++pr) {
+                            const int jj = pr & 1, n = pr * 8;
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch) {
+                                const float2 sv = rows[4][ch * kSrcArr + jj];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    acc[q][ch] = __ffma2_rn(sv, make_float2(wv(n + 2 * q), wv(n + 2 * q + 1)), acc[q][ch]);
+                            }
+                        }
+#pragma unroll
+                        for (int ky = 0; ky < 5; ++ky)
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch) {
+                                const float sv = rows[ky][ch * kSrcArr + 2].x;
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) acc[q][ch].x = fmaf(sv, wv(80 + ky * 4 + q), acc[q][ch].x);
+                            }
+                    }
+                }
+                if (!dead && xin && Y >= fi.core.x && Y < fi.core.z && X >= fi.core.y && X < fi.core.w) {
+                    float out[4][3];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch) out[q][ch] = acc[q][ch].x + acc[q][ch].y;
+                    if (!SRC_U8) {   // only float sources can make a non-finite value (k_tc_head)
+                        float2 all = __fadd2_rn(make_float2(out[0][0], out[0][1]), make_float2(out[0][2], out[1][0]));
+                        all = __fadd2_rn(all, __fadd2_rn(make_float2(out[1][1], out[1][2]), make_float2(out[2][0], out[2][1])));
+                        all = __fadd2_rn(all, __fadd2_rn(make_float2(out[2][2], out[3][0]), make_float2(out[3][1], out[3][2])));
+                        if (!isfinite(all.x + all.y)) atomicOr(nonfinite, 1);
+                    }
+                    const int oy = 2 * (reg.y + Y - dst.pad_y), ox = 2 * (reg.z + X - dst.pad_x);
+#pragma unroll
+                    for (int ii = 0; ii < 2; ++ii) {
+                        if (!DST_U8) {
+                            float* o = static_cast<float*>(dst.ptr) + (size_t(reg.x) * 3 * dst.OH + oy + ii) * dst.OW + ox;
+                            const size_t chs = size_t(dst.OH) * dst.OW;
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch)
+                                *reinterpret_cast<float2*>(o + ch * chs) = make_float2(out[2 * ii][ch], out[2 * ii + 1][ch]);
+                        } else {
+                            const uint2 q01 = u8_code_bits2(out[2 * ii][0], out[2 * ii][1]);
+                            const uint2 q23 = u8_code_bits2(out[2 * ii][2], out[2 * ii + 1][0]);
+                            const uint2 q45 = u8_code_bits2(out[2 * ii + 1][1], out[2 * ii + 1][2]);
+                            unsigned short* o = reinterpret_cast<unsigned short*>(
+                                static_cast<uint8_t*>(dst.ptr) + ((size_t(reg.x) * dst.OH + oy + ii) * dst.OW + ox) * 3);
+                            __stcs(o, (unsigned short)__byte_perm(q01.x, q01.y, 0x0040));
+                            __stcs(o + 1, (unsigned short)__byte_perm(q23.x, q23.y, 0x0040));
+                            __stcs(o + 2, (unsigned short)__byte_perm(q45.x, q45.y, 0x0040));
+                        }
+                    }
+                }
+            }
+            hs = (hs + 8) % 3;
+            // the next pair's new source rows into the slots the previous pair used
+            if (more && !dead) {
+#pragma unroll
+                for (int m = 0; m < 5; ++m) {
+                    const int e = t + kFusedThreads * m;
+                    if (e < 4 * kSrcCols) {
+                        if (SRC_U8) pre[m] = make_uint3(pre[m].x & 255u, (pre[m].x >> 8) & 255u, pre[m].x >> 16);
+                        put(nrow + e / kSrcCols, e % kSrcCols, pre[m]);
+                    }
+                }
+            }
+        }
+    }
+    // every MMA this warpgroup's issuing thread committed, and every dec540 load, lands before
+    // TMEM and shared memory are released (a commit covers all of the thread's earlier MMAs)
+    if (tq == 0) {
+        commit(&drain[wg]);
+        mbar_wait_bounded(&drain[wg], 0, err, kErrTimeout, 200000000LL);
+        if (issuer)
+            for (int sl = 0; sl < kFusedRing; ++sl)
+                if (ring_pend & (1u << sl)) mbar_wait_bounded(&ring_full[sl], (ring_phase >> sl) & 1u, err, kErrTimeout, 200000000LL);
+    }
+    cta_teardown(tmem, 512);
+}
+
 // Per-call host work is part of a frame's latency: device properties and kernel attributes are
 // looked up or set once per device.
 int sm_count() {
@@ -1341,11 +1854,42 @@ int pick_band_balanced(long long strips_x_regions, int rows, int slots) {
     return best;
 }
 
+// Fused refine + tail + reconstruction (k_tc_refine_head): one CTA per SM, its shared memory
+// request raised near the SM's limit so that no CTA of the other stream's tensor-core kernels
+// shares the SM and waits there for the TMEM this kernel holds until its last item.
+void launch_refine_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const TcWeights& w,
+                        void* dec540, const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, bool pdl,
+                        int sms) {
+    if ((long long)rs.R * rs.core_h * rs.core_w == 0) return;
+    const int ph = rs.rh / 2, pw = rs.rw / 2;
+    // packed columns and rows a core can cover (its rows rounded out to whole pairs)
+    const int nstrip = (rs.core_w / 2 + 1 + kConvStrip - 1) / kConvStrip;
+    const int span = std::min(ph, rs.core_h / 2 + 3);
+    // even band minimising the rows of the busiest CTA, counting about six rows of set-up per item
+    int band = 2;
+    long long best = -1;
+    for (int b = 2; b <= span + 1; b += 2) {
+        const long long items = (long long)rs.R * nstrip * ((span + b - 1) / b);
+        const long long cost = (items + sms - 1) / sms * (b + 6);
+        if (best < 0 || cost < best) { best = cost; band = b; }
+    }
+    const int nband = (span + band - 1) / band;
+    const long long items = (long long)rs.R * nstrip * nband;
+    const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM);
+    auto k = src.kind == 0 ? (dst.kind == 0 ? k_tc_refine_head<true, true> : k_tc_refine_head<true, false>)
+                           : (dst.kind == 0 ? k_tc_refine_head<false, true> : k_tc_refine_head<false, false>);
+    constexpr int bytes = 220 * 1024;
+    static_assert(bytes >= kFusedBytes, "fused kernel's shared memory");
+    smem_attr(k, bytes);
+    launch(pdl, k, grid_for(items, 1, sms), kFusedThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias,
+           w.tail_bias, w.slope, head_img, src, dst, band, nstrip, nband, nonfinite, err);
+}
+
 }  // namespace
 
 void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
-                          int* err, cudaStream_t s, int* launches, const StageMark& mark) {
+                          int* err, cudaStream_t s, int* launches, const StageMark& mark, const FusedHead* head) {
     const int sms = sm_count();
     const bool pdl = use_pdl(rs);
     const bool fp8 = route == kRouteE4M3, i8 = route == kRouteI8;
@@ -1395,7 +1939,9 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
         launch(pdl, ke, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err);
     }
     mark(3);
-    {
+    if (head) {
+        launch_refine_head(src, rs, *head->dst, w, dec540, head->head_img, head->nonfinite, err, s, pdl, sms);
+    } else {
         const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
         const long long strips = (long long)rs.R * ((pw + kConvStrip - 1) / kConvStrip);
         const int band = (pick_band(strips, ph, sms * 2) + 1) & ~1;   // whole row pairs (ph is even)

@@ -96,12 +96,22 @@ inline int tc_route_of(int precision) {
     return precision == AEISU_PRECISION_MIXED ? kRouteE4M3 : precision == AEISU_PRECISION_INT8 ? kRouteI8 : kRouteF16;
 }
 
+// Reconstruction fused into the controller's last stage: refine_540 + metadata_head + head in
+// one kernel that writes the output frames, so the coefficients never reach HBM.
+struct FusedHead {
+    const DstDesc* dst;
+    const uint8_t* head_img;
+    int* nonfinite;
+};
+
 // Tensor-core route (k_tc.cu).
 // Buffers are chunk-planar: enc540 [R][ph][4][pw][16], encu [R][lh][K/epc][lw][16],
 // low [R][lh][64/epc][lw][16], dec540 [R][ph][4][pw][16], meta [R][rh][2][rw][16].
+// With `head`, the last stage writes the output frames instead of meta (unused, may be null).
 void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, const TcWeights& w, void* enc540,
                           void* encu, void* low_a, void* low_b, void* dec540, void* meta, float* raw_meta,
-                          int* err, cudaStream_t s, int* launches, const StageMark& mark);
+                          int* err, cudaStream_t s, int* launches, const StageMark& mark,
+                          const FusedHead* head = nullptr);
 void launch_tc_head(const SrcDesc& src, const RegionSet& rs, const DstDesc& dst, const void* meta,
                     const uint8_t* head_img, int* nonfinite, int* err, cudaStream_t s, int* launches);
 

@@ -250,6 +250,12 @@ class Model:
     def set_timeout(self, ms: float):
         _lib.check(_lib.lib().aeisu_set_timeout(self._handle(), float(ms)))
 
+    def set_fused_head(self, on: bool):
+        """Tensor-core routes: reconstruct in a separate head kernel over coefficients kept in
+        device memory (default) or inside the controller's last kernel, so that they never reach
+        device memory; the output is the same bit for bit."""
+        _lib.check(_lib.lib().aeisu_set_fused_head(self._handle(), int(bool(on))))
+
     def set_workspace_limit(self, nbytes: int):
         """Bound the intermediate-tensor bytes of one call; larger batches run in passes."""
         _lib.check(_lib.lib().aeisu_set_workspace_limit(self._handle(), int(nbytes)))

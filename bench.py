@@ -740,6 +740,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20, help="steps of the end-to-end measurement")
     ap.add_argument("--no-config5", dest="config5", action="store_false",
                     help="skip the 4K-stream and 8K-band measurements of the default workload")
+    ap.add_argument("--fused-head", action="store_true",
+                    help="run the reconstruction inside the controller's last kernel (aeisu_set_fused_head)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -765,6 +767,8 @@ def main():
 
     from aeisu_b200 import load_model
     model = load_model(WEIGHTS / ckpt, f"cuda:{local_rank}", precision)
+    if args.fused_head:
+        model.set_fused_head(True)
     stream = torch.cuda.Stream(dev)
     src = torch.from_numpy(frames).to(dev)
     out = torch.empty((n, 2 * h, 2 * w, 3), dtype=torch.uint8, device=dev)

@@ -342,6 +342,18 @@ typedef struct aeisu_timings {
 int aeisu_timings_get(aeisu_t* handle, aeisu_timings* out);
 int aeisu_set_detailed_timing(aeisu_t* handle, int enabled);
 
+/* Implementation switch with no counterpart in the reference.  Tensor-core routes (FP16,
+ * mixed, INT8): where the reconstruction head runs.  enabled = 0 (default): a separate head
+ * kernel reads the clamped coefficients back from a workspace tensor (32 bytes per LR pixel), as
+ * the reference's fused refine+tail kernel and ReconstructConstant pass them
+ * (SrcPyrCudaRuntime.cu:4662-4666, 4831-4834).  enabled = 1: inside the controller's last kernel
+ * (refine_540 + metadata_head + head), so the coefficients stay in shared memory and never reach
+ * device memory and the workspace tensor is not allocated; refine_tail_ms then holds both stages
+ * and reconstruction_ms is 0.  The output is the same bit for bit; on a B200 the fused kernel
+ * measures slower (eight warps per SM against the two kernels' 16 and 18).  The FP32 route
+ * always runs its separate head. */
+int aeisu_set_fused_head(aeisu_t* handle, int enabled);
+
 /* Bound, in milliseconds, on every host wait for GPU completion (default 60000). */
 int aeisu_set_timeout(aeisu_t* handle, double timeout_ms);
 
