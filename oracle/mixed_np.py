@@ -108,6 +108,28 @@ def _conv(x, w, b, groups=1):
     return O.conv2d_nhwc(x, w, np.zeros(w.shape[0], F32) if b is None else b, groups)
 
 
+def own_weights_state(t, state16):
+    """FP32 folded state that holds the mixed route's own weights: the FP8 layers (compress_270,
+    the four bottleneck layers, expand_270) as their E4M3 codes times the per-output-channel
+    weight_scale, with bias_fp8, the layers the mixed route runs in FP16 (project_540,
+    refine_540, metadata_head) as stored.  ``state16`` is spyr8.folded_state_from_spyr8(t)[0];
+    the mixed route's _fp8_layer applies exactly these weights to its quantised activations."""
+    st = dict(state16)
+
+    def deq(name):
+        w = e4m3_decode(t[f"{name}.weight_fp8"]).astype(F32)
+        ws = np.asarray(t[f"{name}.weight_scale"], F32).reshape(-1, *([1] * (w.ndim - 1)))
+        return (w * ws).astype(F32), np.asarray(t[f"{name}.bias_fp8"], F32)
+
+    for name, key in (("compress", "compress_270"), ("expand", "expand_270")):
+        st[f"{key}.weight"], st[f"{key}.bias"] = deq(name)
+    for i in range(4):
+        w, b = deq(f"bottleneck{i}")
+        st[f"bottleneck_270_a{i + 1}.weight"], st[f"bottleneck_270_b{i + 1}.weight"] = w[:32], w[32:]
+        st[f"bottleneck_270_a{i + 1}.bias"], st[f"bottleneck_270_b{i + 1}.bias"] = b[:32], b[32:]
+    return st
+
+
 class QuantizedModel:
     """Reduced-precision restatement.  ``t`` holds SPYR8 tensors (names as in the artifact) for
     ``mode`` "mixed" (FP8 compress/core/expand) or "fp16", or the tensors of

@@ -128,6 +128,39 @@ def test_mixed_route_every_frame_reaches_50db(headroom, request):
         model.close()
 
 
+# The gate read literally, "against the reference FP32 output on the same weights": the reference
+# FP32 forward on the mixed route's own weights (the artifact's E4M3 codes times their channel
+# scales with bias_fp8, its FP16 layers as stored; oracle/mixed_np.py own_weights_state), so the
+# difference is the route's arithmetic alone: activation quantisation to E4M3 at the artifact's
+# scales, FP16 activations and coefficients.  Measured on the CPU restatement over 40 scenes
+# (seeds 2000-2007 at 128x128, 4000-4031 at 256x256): headroom 2 reaches min 50.27 / mean 55.88
+# dB; headroom 1 (the artifact's own scales) min 45.47 / mean 54.98 dB, with four scenes below
+# 50 dB where activations saturate.  The scenes here are the eight 128x128 ones plus the three
+# 256x256 ones that come closest to the bar at headroom 2 (4004, 4007, 4028).
+OWN_WEIGHTS_H1_MISS = ("artifact's own activation scales saturate on high-contrast scenes: seeds 2005, 4004, 4007, "
+                       "4028 at 50.00, 45.47, 49.69, 49.23 dB against FP32 on the same weights (restatement)")
+
+
+@pytest.mark.parametrize("headroom", [2.0, 1.0])
+def test_mixed_route_every_frame_reaches_50db_on_its_own_weights(headroom, request):
+    if headroom == 1.0:
+        request.node.add_marker(pytest.mark.xfail(reason=OWN_WEIGHTS_H1_MISS, strict=False))
+    t = spyr8.read_spyr8(staged("adaptive_fp8.bin").read_bytes())
+    state16, basis = spyr8.folded_state_from_spyr8(t)
+    ref_model = O.FoldedModel(M.own_weights_state(t, state16), basis=basis)
+    model = load_model(staged("adaptive_fp8.bin"), "cuda:0", "mixed", activation_headroom=headroom)
+    try:
+        scenes = [(s, 128, 128) for s in range(2000, 2008)] + [(s, 256, 256) for s in (4004, 4007, 4028)]
+        ps = []
+        for seed, h, w in scenes:
+            src = O.u8_to_chw(make_frame(seed, h, w))
+            ps.append(psnr_vs(O.upscale(ref_model, src, 0), model.upscale_f32(src, 0)))
+        print(f"mixed route, headroom x{headroom:g}, vs FP32 on its own weights: {[round(float(p), 2) for p in ps]}")
+        assert min(ps) >= MIN_PSNR, [round(float(p), 2) for p in ps]
+    finally:
+        model.close()
+
+
 def test_fp16_route_from_folded_checkpoint_1080p():
     path = staged("aeisu_area.pt")
     frame = make_frame(1000, 1080, 1920)

@@ -42,3 +42,21 @@ def test_fp16_restatement_is_close_to_fp32():
     ref = O.load_folded(staged("aeisu_area.pt"))
     src = O.u8_to_chw(make_frame(801, 96, 96))
     assert O.psnr(O.upscale(M.QuantizedModel(t, "fp16"), src, 0), O.upscale(ref, src, 0)) >= 60
+
+
+def test_own_weights_state_is_the_mixed_routes_weights():
+    # FP32 on the mixed route's own weights: the FP8 layers dequantised (E4M3 code x channel scale,
+    # bias_fp8).  With the activations left unquantised the mixed restatement's FP8 layers reduce
+    # to it, so a frame through the restatement at 2x headroom stays close (activation rounding
+    # only), and nearer to it than to FP32 on the FP16 weights
+    t = spyr8.read_spyr8(staged("adaptive_fp8.bin").read_bytes())
+    state16, basis = spyr8.folded_state_from_spyr8(t)
+    own = O.FoldedModel(M.own_weights_state(t, state16), basis=basis)
+    w = M.e4m3_decode(t["compress.weight_fp8"]) * t["compress.weight_scale"].reshape(-1, 1, 1, 1)
+    np.testing.assert_array_equal(own.state["compress_270.weight"], w.astype(np.float32))
+    np.testing.assert_array_equal(own.state["bottleneck_270_b3.bias"], t["bottleneck2.bias_fp8"][32:])
+    src = O.u8_to_chw(make_frame(2005, 64, 64))
+    mixed = O.upscale(M.QuantizedModel(t, "mixed", headroom=2.0), src, 0)
+    p_own = O.psnr(np.clip(mixed, 0, 1), np.clip(O.upscale(own, src, 0), 0, 1))
+    p_f16 = O.psnr(np.clip(mixed, 0, 1), np.clip(O.upscale(O.FoldedModel(state16, basis=basis), src, 0), 0, 1))
+    assert p_own >= 50 and p_own > p_f16, (p_own, p_f16)
