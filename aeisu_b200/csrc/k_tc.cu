@@ -704,6 +704,27 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
 // (2i + j)*16 .. +16; optionally also the raw float32 head output (NHWC, 64 channels).
 constexpr int kRefineThreads = 288;
 
+// Packed rows of the region a refine work item covers: all of them when the raw head output is
+// wanted (predict_coefficients returns the whole padded grid), otherwise only the row pairs
+// that cover the region's core, the rows whose coefficients the head reads.  `span` is the
+// number of rows the bands divide (the same on the host).
+__host__ __device__ inline int refine_span(const RegionSet& rs, bool trim) {
+    return trim ? min(rs.rh / 2, rs.core_h / 2 + 3) : rs.rh / 2;
+}
+__device__ __forceinline__ StripBand refine_item(long long item, const RegionSet& rs, int nstrip, int nband, int band,
+                                                 bool trim, bool& skip) {
+    StripBand s = strip_band(item, nstrip, nband, band, rs.rh / 2, kConvStrip);
+    skip = false;
+    if (trim) {
+        const int4 core = rs.cores[s.r];
+        const int py0 = (core.x >> 1) & ~1, py1 = min(rs.rh / 2, (((core.z + 1) >> 1) + 1) & ~1);
+        s.y0 += py0;
+        s.y1 = min(s.y0 + band, py1);
+        skip = s.y0 >= py1;
+    }
+    return s;
+}
+
 // sign(a) xor sign(b) times min(|a|, |b|); with one NaN operand, the other's magnitude
 __device__ __forceinline__ float min_xorsign_abs(float a, float b) {
     float r;
@@ -755,7 +776,8 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     cta_setup(&s_tmem, s_bar, kRing + 5, 256);
     const uint32_t tmem = s_tmem;
     const int ph = rs.rh / 2, pw = rs.rw / 2;
-    const int nstrip = (pw + kConvStrip - 1) / kConvStrip, nband = (ph + band - 1) / band;
+    const bool trim = raw == nullptr;
+    const int nstrip = (pw + kConvStrip - 1) / kConvStrip, nband = (refine_span(rs, trim) + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     constexpr uint32_t idesc64 = idesc_m128(64), idesc128 = idesc_m128(128);
@@ -793,7 +815,9 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
         };
         for (long long item = blockIdx.x; item < items && ok; item += gridDim.x) {
             last_item(item, items);
-            const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
+            bool skip;
+            const StripBand sb = refine_item(item, rs, nstrip, nband, band, trim, skip);
+            if (skip) continue;   // uniform across the CTA
             // the previous item's last MMAs still read the ring: let them finish before refilling it
             if (seen < pairs && !(ok = done(pairs - 1))) break;
             for (int row = sb.y0 - 1; row <= min(sb.y0 + 2, sb.y1); ++row) load(row, sb);
@@ -853,7 +877,9 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
         bool tail_pend = false;          // thread tq == 0 committed a tail not yet observed
         for (long long item = blockIdx.x; item < items && live; item += gridDim.x) {
             last_item(item, items);
-            const StripBand sb = strip_band(item, nstrip, nband, band, ph, kConvStrip);
+            bool skip;
+            const StripBand sb = refine_item(item, rs, nstrip, nband, band, trim, skip);
+            if (skip) continue;
             const int x = sb.x0 + tq;
             for (int y0 = sb.y0; y0 < sb.y1 && live; y0 += 2, ++p) {
                 const int b = p & 1, y = y0 + wg;
@@ -1944,8 +1970,9 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     } else {
         const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
         const long long strips = (long long)rs.R * ((pw + kConvStrip - 1) / kConvStrip);
-        const int band = (pick_band(strips, ph, sms * 2) + 1) & ~1;   // whole row pairs (ph is even)
-        const long long items = strips * ((ph + band - 1) / band);
+        const int span = refine_span(rs, raw_meta == nullptr);
+        const int band = (pick_band(strips, span, sms * 2) + 1) & ~1;   // whole row pairs (ph is even)
+        const long long items = strips * ((span + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM);
         smem_attr(k_tc_refine_tail, bytes);
         launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kRefineThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
