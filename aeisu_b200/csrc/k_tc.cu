@@ -1038,7 +1038,10 @@ __global__ void __launch_bounds__(kThreads, PX == 1 ? 4 : 2) k_tc_head(const __g
     const int nstrip = (rs.core_w + kHeadStrip - 1) / kHeadStrip, nband = (rs.core_h + band - 1) / band;
     const long long items = (long long)rs.R * nstrip * nband;
     const uint32_t o0 = smem_addr(sOnes), b0 = smem_addr(sB), a0 = smem_addr(sA);
-    constexpr uint32_t idesc = idesc_m128(128);
+    // N = 112: the 100 weight columns of a tile; columns 112-119 take the tile's coefficients
+    // (the MMAs' A operand, copied there from shared memory), 120-127 a constant ones operand
+    // (its first two K entries 1) for the base term
+    constexpr uint32_t idesc = idesc_m128(112);
     // Work beside the apply is spread over the warps: warp 1 issues the loads and MMAs, the last
     // four threads stage the four window columns beyond PX per thread.
     constexpr int kExtra = kHeadTW - PX * kThreads;
@@ -1046,6 +1049,9 @@ __global__ void __launch_bounds__(kThreads, PX == 1 ? 4 : 2) k_tc_head(const __g
     // strip column of source column j of this thread: t + 128 j, and for j = PX the extra column
     auto col_of = [&](int j) { return j < PX ? t + j * kThreads : PX * kThreads + t - (kThreads - kExtra); };
     const bool issuer = t == 32;
+    if (issuer)
+#pragma unroll
+        for (int tile = 0; tile < PX; ++tile) tmem_cp_128x256b(tmem + tile * 128 + 120, sdesc(o0, kM * 16, 128));
     uint32_t mma_phase = 0, tma_phase = 0, tma_pend = 0;   // tma bits: per A buffer
     bool ok = true, mma_pend = false;
     // coefficient rows of row y into A buffer b: PX boxes of 128 pixels x 2 chunks
@@ -1067,11 +1073,11 @@ __global__ void __launch_bounds__(kThreads, PX == 1 ? 4 : 2) k_tc_head(const __g
             fence_after_sync();
 #pragma unroll
             for (int tile = 0; tile < PX; ++tile) {
-                const uint64_t a = sdesc(a0 + b * kHeadABytes + tile * kHeadTile, kM * 16, 128);
                 const uint32_t d = tmem + tile * 128;
-                mma_f16(d, a, sdesc(b0, 128 * 16, 128), idesc, 0);
-                mma_f16(d, a, sdesc(b0 + kHeadBCH, 128 * 16, 128), idesc, 1);
-                mma_f16(d, sdesc(o0, kM * 16, 128), sdesc(b0 + 2 * kHeadBCH, 128 * 16, 128), idesc, 1);
+                tmem_cp_128x256b(d + 112, sdesc(a0 + b * kHeadABytes + tile * kHeadTile, kM * 16, 128));
+                mma_f16_ta(d, d + 112, sdesc(b0, 128 * 16, 128), idesc, 0);
+                mma_f16_ta(d, d + 112, sdesc(b0 + kHeadBCH, 128 * 16, 128), idesc, 1);
+                mma_f16_ta(d, d + 120, sdesc(b0 + 2 * kHeadBCH, 128 * 16, 128), idesc, 1);
             }
         }
         commit(&s_bar[0]);

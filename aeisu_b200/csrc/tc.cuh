@@ -46,6 +46,21 @@ __device__ __forceinline__ void mma_e4m3(uint32_t tmem_d, uint64_t a, uint64_t b
         :: "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
+// The same MMA with the A operand in TMEM (M = 128 rows in the 128 lanes, K packed along the
+// columns, as tcgen05.cp writes it from a K-major shared-memory operand).
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
+        :: "r"(tmem_d), "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Copy a 128-row x 32-byte operand (shared-memory descriptor) into 8 TMEM columns of all 128
+// lanes.  Asynchronous; tcgen05.mma issued later by the same thread sees the copied data.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" :: "r"(taddr), "l"(sdesc));
+}
+
 // Arrive once on `bar` when every MMA this thread issued so far has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
