@@ -292,6 +292,8 @@ void Engine::upload_weights() {
         return EpiParams{F + L.scale, F + L.bias, P.slope, L.out_inv, L.out_deq};
     };
     tcw_.stencil = F + P.stencil;
+    std::copy(P.floats.begin() + P.stencil, P.floats.begin() + P.stencil + 24, tcw_.proj.st);
+    std::copy(P.floats.begin() + P.project_bias, P.floats.begin() + P.project_bias + 32, tcw_.proj.bias);
     tcw_.project = B + P.project;
     tcw_.project_bias = F + P.project_bias;
     tcw_.slope = P.slope;

@@ -57,24 +57,21 @@ using namespace tcd;
 constexpr int kProjRing = 8;
 constexpr int kProjTW = 2 * kM + 2;   // 258 LR columns per strip
 
-template <bool FP8, bool I8 = false>
-__global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet rs, const float* __restrict__ stencil,
-                                                         const uint8_t* __restrict__ wimg, const float* __restrict__ bias,
+template <bool FP8, bool I8, bool SRC_U8>
+__global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet rs, const ProjParams pp,
+                                                         const uint8_t* __restrict__ wimg,
                                                          float slope, float inv_s1, void* __restrict__ enc540,
                                                          void* __restrict__ encu, int band, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* sA = smem;                                        // [2][4 chunks][128][16 B]
     uint8_t* sB = smem + 2 * 4 * kM * 16;                      // [4][32][16 B]
     float4 (*s_src)[kProjTW] = reinterpret_cast<float4 (*)[kProjTW]>(sB + 4 * 32 * 16);
-    __shared__ float s_st[24];
-    __shared__ alignas(16) float s_bias[32];
     __shared__ float s_lut[256];
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar[2];
     copy_image(sB, wimg, 4 * 32 * 16);
-    if (threadIdx.x < 24) s_st[threadIdx.x] = stencil[threadIdx.x];
-    if (threadIdx.x < 32) s_bias[threadIdx.x] = bias[threadIdx.x];
-    fill_lut(s_lut);
+    if (SRC_U8) fill_lut(s_lut);
+    const float* s_st = pp.st;   // kernel parameters: the constant bank
     fence_async_smem();
     cta_setup(&s_tmem, s_bar, 2, 64);
     const uint32_t tmem = s_tmem;
@@ -106,7 +103,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             sx[j] = clampi(reg.z + clampi(2 * sb.x0 - 1 + col_of(j), 0, rs.rw - 1) - src.pad_x, 0, src.W - 1);
         auto raw_at = [&](int row, int j) -> uint3 {
             const int sy = clampi(reg.y + clampi(row, 0, rs.rh - 1) - src.pad_y, 0, src.H - 1);
-            if (src.kind == 0) {
+            if (SRC_U8) {
                 const uint8_t* p = static_cast<const uint8_t*>(src.ptr) + ((size_t(reg.x) * src.H + sy) * src.W + sx[j]) * 3;
                 return make_uint3(p[0], p[1], p[2]);
             }
@@ -115,7 +112,8 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             return make_uint3(__float_as_uint(p[0]), __float_as_uint(p[plane]), __float_as_uint(p[2 * plane]));
         };
         auto put = [&](int row, int j, uint3 raw) {
-            const float3 v = finish_src(src, raw, s_lut);
+            const float3 v = SRC_U8 ? make_float3(s_lut[raw.x], s_lut[raw.y], s_lut[raw.z])
+                                    : make_float3(__uint_as_float(raw.x), __uint_as_float(raw.y), __uint_as_float(raw.z));
             s_src[slot(row)][col_of(j)] = make_float4(v.x, v.y, v.z, mix3(v.x, v.y, v.z, s_st[9], s_st[10], s_st[11]));
         };
         auto fetch2 = [&](int row, uint3 (&pre)[2][PER]) {   // raw loads of rows row, row+1
@@ -144,7 +142,13 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + b * 32, v);
 #pragma unroll
-            epi_add_leaky(v, s_bias, slope);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {   // v = leaky(v + bias), as epi_add_leaky
+                const float2 a = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(pp.bias[2 * i], pp.bias[2 * i + 1]));
+                const float2 n = __fmul2_rn(a, make_float2(slope, slope));
+                v[2 * i] = fmaxf(a.x, n.x);
+                v[2 * i + 1] = fmaxf(a.y, n.y);
+            }
             uint4 o[4];
             pack_f16x32(v, o);
             if (qx < pw && good) {
@@ -1932,9 +1936,10 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
         const int band = pick_band(strips, ph, sms * 4);
         const long long items = strips * ((ph + band - 1) / band);
         const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;
-        auto kp = fp8 ? k_tc_project<true> : i8 ? k_tc_project<false, true> : k_tc_project<false>;
+        auto kp = src.kind == 0 ? (fp8 ? k_tc_project<true, false, true> : i8 ? k_tc_project<false, true, true> : k_tc_project<false, false, true>)
+                                : (fp8 ? k_tc_project<true, false, false> : i8 ? k_tc_project<false, true, false> : k_tc_project<false, false, false>);
         smem_attr(kp, bytes);
-        launch(pdl, kp, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.stencil, w.project, w.project_bias, w.slope, w.inv_s1, enc540, encu, band, err);
+        launch(pdl, kp, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.proj, w.project, w.slope, w.inv_s1, enc540, encu, band, err);
     }
     mark(1);
     {

@@ -67,9 +67,17 @@ struct EpiParams {
     float out_deq;        // expand: dequantisation s_out
 };
 
+// The feature-analysis stencil (24 values, SPYR8 analysis_stencil order) and project_540's bias,
+// passed by value to the project kernel so that they sit in the constant bank.
+struct ProjParams {
+    float st[24];
+    float bias[32];
+};
+
 // Device images of the tensor-core routes' weights, already in the K-major operand layout
 // of tc.cuh (chunk-major, 16 bytes per row per chunk), plus per-channel epilogue vectors.
 struct TcWeights {
+    ProjParams proj;               // host copy of stencil and project bias
     const float* stencil;
     const uint8_t* project;        // [4 chunks][32][16 B] f16
     const float* project_bias;
