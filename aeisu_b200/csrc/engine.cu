@@ -310,6 +310,8 @@ void Engine::upload_weights() {
     tcw_.tail = B + P.tail;
     tcw_.refine_bias = F + P.refine_bias;
     tcw_.tail_bias = F + P.tail_bias;
+    std::copy(P.floats.begin() + P.refine_bias, P.floats.begin() + P.refine_bias + 64, tcw_.rbias.refine);
+    std::copy(P.floats.begin() + P.tail_bias, P.floats.begin() + P.tail_bias + 64, tcw_.rbias.tail);
     tcw_.head = B + P.head;
     head_img_ = B + P.head;
 }

@@ -749,8 +749,7 @@ __device__ __forceinline__ bool warpgroup_sync_or(int wg, bool v) {
 __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                                const uint8_t* __restrict__ wref,
                                                                const uint8_t* __restrict__ wtail,
-                                                               const float* __restrict__ rbias,
-                                                               const float* __restrict__ tbias, float slope,
+                                                               const RefineBiases bias, float slope,
                                                                void* __restrict__ meta, float* __restrict__ raw,
                                                                int band, int* err) {
     constexpr int ICH = 4, LBO = kM * 16, SLOT = ICH * LBO;   // a 128-pixel window per chunk
@@ -761,8 +760,6 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     uint8_t* sB = smem + kRing * SLOT;   // refine weights
     uint8_t* sT = sB + BREF;             // tail weights
     uint8_t* sA2 = sT + BTAIL;           // tail operands, one per warpgroup
-    float* s_rb = reinterpret_cast<float*>(sA2 + 2 * A2);
-    float* s_tb = s_rb + 64;
     __shared__ uint32_t s_tmem;
     // ring slots, then per buffer b: ref_full, tail_full (count 1); slot_free (count 1); then
     // per buffer pair_empty (count 8: every epilogue warp)
@@ -773,7 +770,6 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
     uint64_t* pair_empty = s_bar + kRing + 5;
     copy_image(sB, wref, BREF);
     copy_image(sT, wtail, BTAIL);
-    if (threadIdx.x < 64) { s_rb[threadIdx.x] = rbias[threadIdx.x]; s_tb[threadIdx.x] = tbias[threadIdx.x]; }
     if (threadIdx.x == 0)
         for (int i = kRing + 5; i < kRing + 7; ++i) mbar_init(&s_bar[i], 8);
     fence_async_smem();
@@ -896,7 +892,14 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                     tmem_ld32x2(col, col + 32, vr[0], vr[1]);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        epi_add_leaky(vr[h], s_rb + h * 32, slope);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {   // leaky(v + bias), as epi_add_leaky
+                            const float2 a = __fadd2_rn(make_float2(vr[h][2 * i], vr[h][2 * i + 1]),
+                                                        make_float2(bias.refine[h * 32 + 2 * i], bias.refine[h * 32 + 2 * i + 1]));
+                            const float2 n = __fmul2_rn(a, make_float2(slope, slope));
+                            vr[h][2 * i] = fmaxf(a.x, n.x);
+                            vr[h][2 * i + 1] = fmaxf(a.y, n.y);
+                        }
                         uint4 q[4];
                         pack_f16x32(vr[h], q);
 #pragma unroll
@@ -935,7 +938,13 @@ __global__ void __launch_bounds__(kRefineThreads, 2) k_tc_refine_tail(const __gr
                 for (int h = 0; h < 2; ++h) {
                     float (&v)[32] = vt[h];
                     if (tq < kConvStrip && x < pw) {
-                        epi_add(v, s_tb + h * 32);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {   // v + bias, as epi_add
+                            const float2 a = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]),
+                                                        make_float2(bias.tail[h * 32 + 2 * i], bias.tail[h * 32 + 2 * i + 1]));
+                            v[2 * i] = a.x;
+                            v[2 * i + 1] = a.y;
+                        }
                         if (raw) {
                             float* rp = raw + (((size_t)sb.r * ph + y) * pw + x) * 64 + h * 32;
 #pragma unroll
@@ -1979,14 +1988,14 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     if (head) {
         launch_refine_head(src, rs, *head->dst, w, dec540, head->head_img, head->nonfinite, err, s, pdl, sms);
     } else {
-        const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16 + 2 * 64 * 4;
+        const int bytes = 1024 + kRing * 4 * kM * 16 + 36 * 64 * 16 + 8 * 64 * 16 + 2 * 8 * kM * 16;
         const long long strips = (long long)rs.R * ((pw + kConvStrip - 1) / kConvStrip);
         const int span = refine_span(rs, raw_meta == nullptr);
         const int band = (pick_band(strips, span, sms * 2) + 1) & ~1;   // whole row pairs (ph is even)
         const long long items = strips * ((span + band - 1) / band);
         const CUtensorMap map = make_row_window_map(dec540, rs.R, ph, 4, pw, kM);
         smem_attr(k_tc_refine_tail, bytes);
-        launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kRefineThreads, bytes, s, map, rs, w.refine, w.tail, w.refine_bias, w.tail_bias, w.slope, meta, raw_meta, band, err);
+        launch(pdl, k_tc_refine_tail, grid_for(items, 2, sms), kRefineThreads, bytes, s, map, rs, w.refine, w.tail, w.rbias, w.slope, meta, raw_meta, band, err);
     }
     AEISU_CUDA(cudaGetLastError());
     *launches += 8;

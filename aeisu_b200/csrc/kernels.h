@@ -74,10 +74,18 @@ struct ProjParams {
     float bias[32];
 };
 
+// refine_540's and metadata_head's biases (the tail's as the route adds it), passed by value to
+// the refine kernel so that they sit in the constant bank.
+struct RefineBiases {
+    float refine[64];
+    float tail[64];
+};
+
 // Device images of the tensor-core routes' weights, already in the K-major operand layout
 // of tc.cuh (chunk-major, 16 bytes per row per chunk), plus per-channel epilogue vectors.
 struct TcWeights {
     ProjParams proj;               // host copy of stencil and project bias
+    RefineBiases rbias;            // host copy of the refine and tail biases
     const float* stencil;
     const uint8_t* project;        // [4 chunks][32][16 B] f16
     const float* project_bias;
