@@ -300,12 +300,16 @@ void Engine::upload_weights() {
     tcw_.inv_s1 = P.inv_s1;
     tcw_.compress = B + P.compress.image;
     tcw_.compress_ep = ep(P.compress);
+    std::copy(P.floats.begin() + P.compress.scale, P.floats.begin() + P.compress.scale + 64, tcw_.compress_cp.scale);
+    std::copy(P.floats.begin() + P.compress.bias, P.floats.begin() + P.compress.bias + 64, tcw_.compress_cp.bias);
     for (int i = 0; i < 4; ++i) {
         tcw_.core[i] = B + P.core[i].image;
         tcw_.core_ep[i] = ep(P.core[i]);
     }
     tcw_.expand = B + P.expand.image;
     tcw_.expand_ep = ep(P.expand);
+    std::copy(P.floats.begin() + P.expand.scale, P.floats.begin() + P.expand.scale + 128, tcw_.expand_cp.scale);
+    std::copy(P.floats.begin() + P.expand.bias, P.floats.begin() + P.expand.bias + 128, tcw_.expand_cp.bias);
     tcw_.refine = B + P.refine;
     tcw_.tail = B + P.tail;
     tcw_.refine_bias = F + P.refine_bias;

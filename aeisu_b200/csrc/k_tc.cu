@@ -288,18 +288,16 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
 // FP8: A/B e4m3 (16 per chunk); else f16 (8 per chunk).
 template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
-                                                          const void* __restrict__ encu, void* __restrict__ out, int* err) {
+                                                          const ChannelParams<64> cp, const void* __restrict__ encu,
+                                                          void* __restrict__ out, int* err) {
     constexpr int KCH = FP8 ? 8 : 16;   // chunks of K = 128
     constexpr int OCH = FP8 ? 4 : 8;    // chunks of the 64 outputs
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* sA = smem;                        // KCH x 128 x 16
     uint8_t* sB = smem + KCH * kM * 16;        // KCH x 64 x 16
-    float* s_scale = reinterpret_cast<float*>(sB + KCH * 64 * 16);
-    float* s_bias = s_scale + 64;
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
     copy_image(sB, wimg, KCH * 64 * 16);
-    if (threadIdx.x < 64) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     fence_async_smem();
     cta_setup(&s_tmem, &s_bar, 1, 64);
     const uint32_t tmem = s_tmem;
@@ -344,7 +342,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
             float v[32];
             tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + h * 32, v);
 #pragma unroll
-            epi_fma_leaky(v, s_scale + h * 32, s_bias + h * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+            epi_fma_leaky_cp(v, cp, h * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
             if (I8) s8_codes32(v);
             if (x < lw) {
                 if (FP8) {
@@ -369,18 +367,15 @@ __global__ void __launch_bounds__(kThreads) k_tc_compress(RegionSet rs, const ui
 // [32p, 32p+32) are the 32 channels of output pixel (2y + p/2, 2x + p%2).
 template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const uint8_t* __restrict__ wimg, EpiParams ep,
-                                                        const void* __restrict__ low, const void* __restrict__ enc540,
-                                                        void* __restrict__ dec, int* err) {
+                                                        const ChannelParams<128> cp, const void* __restrict__ low,
+                                                        const void* __restrict__ enc540, void* __restrict__ dec, int* err) {
     constexpr int KCH = FP8 ? 4 : 8;   // chunks of K = 64
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* sA = smem;                        // KCH x 128 x 16
     uint8_t* sB = smem + KCH * kM * 16;        // KCH x 128 x 16
-    float* s_scale = reinterpret_cast<float*>(sB + KCH * 128 * 16);
-    float* s_bias = s_scale + 128;
     __shared__ uint32_t s_tmem;
     __shared__ alignas(8) uint64_t s_bar;
     copy_image(sB, wimg, KCH * 128 * 16);
-    if (threadIdx.x < 128) { s_scale[threadIdx.x] = ep.scale[threadIdx.x]; s_bias[threadIdx.x] = ep.bias[threadIdx.x]; }
     fence_async_smem();
     cta_setup(&s_tmem, &s_bar, 1, 128);
     const uint32_t tmem = s_tmem;
@@ -433,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_tc_expand(RegionSet rs, const u
             if (x < lw) {
                 const int oy = 2 * y + (p >> 1), ox = 2 * x + (p & 1);
                 const __half2* skh = reinterpret_cast<const __half2*>(sk[p]);
-                epi_fma_leaky(v, s_scale + p * 32, s_bias + p * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+                epi_fma_leaky_cp(v, cp, p * 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
                 if (FP8) {   // K8: requantise to e4m3 at 1/s7, dequantise
 #pragma unroll
                     for (int n = 0; n < 32; n += 4) {
@@ -1953,10 +1948,10 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     mark(1);
     {
         const int kch = fp8 ? 8 : 16;
-        const int bytes = kch * kM * 16 + kch * 64 * 16 + 2 * 64 * 4;
+        const int bytes = kch * kM * 16 + kch * 64 * 16;
         auto kc = fp8 ? k_tc_compress<true> : i8 ? k_tc_compress<false, true> : k_tc_compress<false>;
         smem_attr(kc, bytes);
-        launch(pdl, kc, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, encu, low_a, err);
+        launch(pdl, kc, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.compress, w.compress_ep, w.compress_cp, encu, low_a, err);
     }
     {
         // one group per CTA (two CTAs per work item), four CTAs per SM; bands hold whole row pairs
@@ -1979,10 +1974,10 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     mark(2);
     {
         const int kch = fp8 ? 4 : 8;
-        const int bytes = kch * kM * 16 + kch * 128 * 16 + 2 * 128 * 4;
+        const int bytes = kch * kM * 16 + kch * 128 * 16;
         auto ke = fp8 ? k_tc_expand<true> : i8 ? k_tc_expand<false, true> : k_tc_expand<false>;
         smem_attr(ke, bytes);
-        launch(pdl, ke, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, low_a, enc540, dec540, err);
+        launch(pdl, ke, grid_for(low_tiles, 4, sms), kThreads, bytes, s, rs, w.expand, w.expand_ep, w.expand_cp, low_a, enc540, dec540, err);
     }
     mark(3);
     if (head) {

@@ -81,11 +81,21 @@ struct RefineBiases {
     float tail[64];
 };
 
+// Per-channel epilogue multipliers and biases of a 1x1 layer (compress_270: 64 channels,
+// expand_270: 128), passed by value so that they sit in the constant bank.
+template <int C>
+struct ChannelParams {
+    float scale[C];
+    float bias[C];
+};
+
 // Device images of the tensor-core routes' weights, already in the K-major operand layout
 // of tc.cuh (chunk-major, 16 bytes per row per chunk), plus per-channel epilogue vectors.
 struct TcWeights {
     ProjParams proj;               // host copy of stencil and project bias
     RefineBiases rbias;            // host copy of the refine and tail biases
+    ChannelParams<64> compress_cp;   // host copies of the 1x1 layers' epilogue vectors
+    ChannelParams<128> expand_cp;
     const float* stencil;
     const uint8_t* project;        // [4 chunks][32][16 B] f16
     const float* project_bias;

@@ -38,6 +38,22 @@ __device__ __forceinline__ void epi_fma_leaky(float (&v)[32], const float* scale
         v[2 * i + 1] = a.y;
     }
 }
+// The same with the channel vectors in a kernel-parameter struct (scale[], bias[]) at channel
+// offset `off` (a constant after unrolling): the values come from the constant bank.
+template <typename CP>
+__device__ __forceinline__ void epi_fma_leaky_cp(float (&v)[32], const CP& cp, int off, float slope, float post) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float2 a = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]),
+                              make_float2(cp.scale[off + 2 * i], cp.scale[off + 2 * i + 1]),
+                              make_float2(cp.bias[off + 2 * i], cp.bias[off + 2 * i + 1]));
+        const float2 n = __fmul2_rn(a, make_float2(slope, slope));
+        a = make_float2(fmaxf(a.x, n.x), fmaxf(a.y, n.y));
+        a = __fmul2_rn(a, make_float2(post, post));
+        v[2 * i] = a.x;
+        v[2 * i + 1] = a.y;
+    }
+}
 // INT8 route: the int8 code of an already scaled value, as the shader route's quantize_s8
 // (optimized/shader/src/int8_kernels.cuh:2-4): round to nearest even, clamp to [-127, 127]
 // (NaN gives 0).  Kept as a float: f16 holds every code exactly, so f16 MMAs over the codes
