@@ -305,6 +305,8 @@ void Engine::upload_weights() {
     for (int i = 0; i < 4; ++i) {
         tcw_.core[i] = B + P.core[i].image;
         tcw_.core_ep[i] = ep(P.core[i]);
+        std::copy(P.floats.begin() + P.core[i].scale, P.floats.begin() + P.core[i].scale + 64, tcw_.core_cp[i].scale);
+        std::copy(P.floats.begin() + P.core[i].bias, P.floats.begin() + P.core[i].bias + 64, tcw_.core_cp[i].bias);
     }
     tcw_.expand = B + P.expand.image;
     tcw_.expand_ep = ep(P.expand);

@@ -529,7 +529,8 @@ constexpr int kWsThreads = 160;
 template <bool FP8, bool I8 = false>
 __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant__ CUtensorMap tin, RegionSet rs,
                                                         const uint8_t* __restrict__ wimg, EpiParams ep,
-                                                        void* __restrict__ out, int band, int* err) {
+                                                        const ChannelParams<64> cp, void* __restrict__ out, int band,
+                                                        int* err) {
     constexpr int ICH = FP8 ? 4 : 8;          // 16-byte chunks of the 64 input channels
     constexpr int CPG = ICH / 2;              // chunks per group (staged per row)
     constexpr int LBO = kM * 16, SLOT = CPG * LBO;   // a 128-pixel window per chunk
@@ -540,8 +541,6 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = align_smem(smem_raw);   // TMA destinations: 1024-byte aligned ring
     uint8_t* sB = smem + kRing * SLOT;
-    float* s_scale = reinterpret_cast<float*>(sB + BG);
-    float* s_bias = s_scale + 32;
     __shared__ uint32_t s_tmem;
     // ring slots, acc_full x2, slot_free (count 1), acc_empty x2 (count 4)
     __shared__ alignas(8) uint64_t s_bar[kRing + 5];
@@ -549,7 +548,6 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
     uint64_t* slot_free = s_bar + kRing + 2;
     uint64_t* acc_empty = s_bar + kRing + 3;
     copy_image(sB, wimg + gb * BG, BG);
-    if (threadIdx.x < 32) { s_scale[threadIdx.x] = ep.scale[gb * 32 + threadIdx.x]; s_bias[threadIdx.x] = ep.bias[gb * 32 + threadIdx.x]; }
     if (threadIdx.x == 0)
         for (int b = 0; b < 2; ++b) mbar_init(&acc_empty[b], 4);
     fence_async_smem();
@@ -665,7 +663,10 @@ __global__ void __launch_bounds__(kWsThreads, 4) k_tc_core(const __grid_constant
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[b]);
                     }
-                    epi_fma_leaky(v, s_scale, s_bias, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+                    // this CTA's group's channel vectors, from the constant bank (a uniform branch,
+                    // so that each copy reads at constant offsets)
+                    if (gb == 0) epi_fma_leaky_cp(v, cp, 0, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
+                    else epi_fma_leaky_cp(v, cp, 32, ep.slope, (FP8 || I8) ? ep.out_inv : 1.f);
                     if (I8) s8_codes32(v);
                     if (t < kConvStrip && x < lw) {
                         if (FP8) {
@@ -1956,7 +1957,7 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     {
         // one group per CTA (two CTAs per work item), four CTAs per SM; bands hold whole row pairs
         const int ich = fp8 ? 4 : 8, cpg = ich / 2;
-        const int bytes = 1024 + kRing * cpg * kM * 16 + 9 * cpg * 32 * 16 + 2 * 32 * 4;
+        const int bytes = 1024 + kRing * cpg * kM * 16 + 9 * cpg * 32 * 16;
         const int slots = sms * 2;   // work items in flight: two CTAs each
         const long long strips = (long long)rs.R * ((lw + kConvStrip - 1) / kConvStrip);
         const int band = (pick_band(strips, lh, slots) + 1) & ~1;   // lh is a multiple of 8
@@ -1969,7 +1970,7 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
         auto kk = fp8 ? k_tc_core<true> : i8 ? k_tc_core<false, true> : k_tc_core<false>;
         smem_attr(kk, bytes);
         for (int i = 0; i < 4; ++i)
-            launch(pdl, kk, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], bufs[(i + 1) & 1], band, err);
+            launch(pdl, kk, grid, kWsThreads, bytes, s, *maps[i & 1], rs, w.core[i], w.core_ep[i], w.core_cp[i], bufs[(i + 1) & 1], band, err);
     }
     mark(2);
     {

@@ -95,6 +95,7 @@ struct TcWeights {
     ProjParams proj;               // host copy of stencil and project bias
     RefineBiases rbias;            // host copy of the refine and tail biases
     ChannelParams<64> compress_cp;   // host copies of the 1x1 layers' epilogue vectors
+    ChannelParams<64> core_cp[4];    // and of the bottleneck layers' (both groups)
     ChannelParams<128> expand_cp;
     const float* stencil;
     const uint8_t* project;        // [4 chunks][32][16 B] f16
