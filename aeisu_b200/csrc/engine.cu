@@ -288,14 +288,10 @@ void Engine::upload_weights() {
     AEISU_CUDA(cudaMemcpy(tc_floats.get(), P.floats.data(), P.floats.size() * 4, cudaMemcpyHostToDevice));
     const uint8_t* B = tc_bytes.as<uint8_t>();
     const float* F = tc_floats.as<float>();
-    auto ep = [&](const TcHostLayer& L) {
-        return EpiParams{F + L.scale, F + L.bias, P.slope, L.out_inv, L.out_deq};
-    };
-    tcw_.stencil = F + P.stencil;
+    auto ep = [&](const TcHostLayer& L) { return EpiParams{P.slope, L.out_inv, L.out_deq}; };
     std::copy(P.floats.begin() + P.stencil, P.floats.begin() + P.stencil + 24, tcw_.proj.st);
     std::copy(P.floats.begin() + P.project_bias, P.floats.begin() + P.project_bias + 32, tcw_.proj.bias);
     tcw_.project = B + P.project;
-    tcw_.project_bias = F + P.project_bias;
     tcw_.slope = P.slope;
     tcw_.inv_s1 = P.inv_s1;
     tcw_.compress = B + P.compress.image;

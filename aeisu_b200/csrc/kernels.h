@@ -58,10 +58,9 @@ void launch_f32_controller(const SrcDesc& src, const RegionSet& rs, const float*
                            const F32Layer* layers, float* enc540, float* low_a, float* low_b,
                            float* dec540, float* refined, float* meta, cudaStream_t s, int* launches,
                            const StageMark& mark, float* peaks = nullptr, double* sums = nullptr);
-// Epilogue parameters of a tensor-core convolution layer.
+// Scalar epilogue parameters of a tensor-core convolution layer; its per-channel accumulator
+// multipliers (FP8: s_in * w_scale; INT8: factor) and biases travel beside it as ChannelParams.
 struct EpiParams {
-    const float* scale;   // per output channel: accumulator multiplier (FP8: s_in * w_scale; INT8: factor)
-    const float* bias;    // per output channel
     float slope;          // LeakyReLU negative slope
     float out_inv;        // FP8 / INT8 output quantisation: 1/s_out
     float out_deq;        // expand: dequantisation s_out
@@ -97,9 +96,7 @@ struct TcWeights {
     ChannelParams<64> compress_cp;   // host copies of the 1x1 layers' epilogue vectors
     ChannelParams<64> core_cp[4];    // and of the bottleneck layers' (both groups)
     ChannelParams<128> expand_cp;
-    const float* stencil;
     const uint8_t* project;        // [4 chunks][32][16 B] f16
-    const float* project_bias;
     float slope;
     float inv_s1;                  // 1/activation_scales[1] (e4m3 and int8 routes; else 1)
     const uint8_t* compress;       // [K/epc][64][16 B], K order phase*32 + c
