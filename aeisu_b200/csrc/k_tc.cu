@@ -46,15 +46,17 @@ using namespace tcd;
 
 // ---- stage 1: feature analysis + unshuffle + project_540 ------------------------------------
 // Work item: a strip of 128 packed pixels and a band of packed rows.  The LR source rows the
-// strip needs (2qy-1 .. 2qy+2, 258 columns) slide through an 8-row ring in shared memory as
-// (r, g, b, luma) float4, so each source pixel is read and mixed once per strip.  Per packed
+// strip needs (2qy-1 .. 2qy+2, 258 columns) slide through a 6-row ring in shared memory as
+// (r, g, b, luma) float4, so each source pixel is read and mixed once per strip (a row qy reads
+// four rows while the two the previous step loaded are stored: six in all, so five CTAs fit
+// an SM's shared memory).  Per packed
 // row qy: the raw loads of rows 2qy+5, 2qy+6 are issued, the features of row qy are computed
 // into the A operand, the rows loaded during the previous step enter the ring, one barrier,
 // then the MMA of row qy runs while the epilogue of row qy-1 drains the other TMEM buffer.
 // A = 32 features (f16) of the strip's packed pixels; B = project weights [32][32].
 // Writes enc540 (f16, 4 chunks, packed grid: the skip input of expand) and the compress
 // input at low resolution, unshuffled with K order phase*32 + c (f16: 16 chunks, e4m3: 8).
-constexpr int kProjRing = 8;
+constexpr int kProjRing = 6;
 constexpr int kProjTW = 2 * kM + 2;   // 258 LR columns per strip
 
 template <bool FP8, bool I8, bool SRC_U8>
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_project(SrcDesc src, RegionSet 
         const StripBand sb = strip_band(item, nstrip, nband, band, ph);
         const int4 reg = rs.regions[sb.r];
         const int base_row = 2 * sb.y0 - 1;
-        auto slot = [&](int row) { return (row - base_row) & (kProjRing - 1); };
+        auto slot = [&](int row) { return (row - base_row) % kProjRing; };   // row >= base_row
         // source columns this thread stages, clamped once per item
         int sx[PER];
 #pragma unroll
@@ -1938,13 +1940,13 @@ void launch_tc_controller(int route, const SrcDesc& src, const RegionSet& rs, co
     const long long low_tiles = (long long)rs.R * lh * ((lw + kM - 1) / kM);
     {
         const long long strips = (long long)rs.R * ((pw + kM - 1) / kM);
-        const int band = pick_band(strips, ph, sms * 4);
+        const int band = pick_band(strips, ph, sms * 5);
         const long long items = strips * ((ph + band - 1) / band);
-        const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;
+        const int bytes = 2 * 4 * kM * 16 + 4 * 32 * 16 + kProjRing * kProjTW * 16;   // five CTAs per SM
         auto kp = src.kind == 0 ? (fp8 ? k_tc_project<true, false, true> : i8 ? k_tc_project<false, true, true> : k_tc_project<false, false, true>)
                                 : (fp8 ? k_tc_project<true, false, false> : i8 ? k_tc_project<false, true, false> : k_tc_project<false, false, false>);
         smem_attr(kp, bytes);
-        launch(pdl, kp, grid_for(items, 4, sms), kThreads, bytes, s, src, rs, w.proj, w.project, w.slope, w.inv_s1, enc540, encu, band, err);
+        launch(pdl, kp, grid_for(items, 5, sms), kThreads, bytes, s, src, rs, w.proj, w.project, w.slope, w.inv_s1, enc540, encu, band, err);
     }
     mark(1);
     {
